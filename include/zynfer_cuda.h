@@ -1,0 +1,184 @@
+/* zynfer_cuda.h: C ABI of the Zynfer `cuda` backend (libzynfer_cuda.so, sm_100a).
+ *
+ * Pure C99 so that Zig's @cImport, ctypes, cgo and JNI can bind it. It plays
+ * the role the Apple bridge plays for the `apple` backend
+ * (src/backends/apple/bridge.h:11-99 in the reference): opaque handles, an int
+ * status with 0 = OK, a per-handle last-error string, and one single-owner
+ * context per device per thread.
+ *
+ * Citations name the reference function each entry point replaces
+ * (file:line within the Zynfer reference project).
+ *
+ * Ownership: the context owns all device memory (weights, paged KV pool,
+ * scratch, graphs). Host pointers passed in are borrowed for the duration of
+ * the call; output arrays are caller-allocated. zynfer_cu_decode_step and
+ * zynfer_cu_generate allocate no memory (device or host) after
+ * zynfer_cu_model_init.
+ *
+ * Threading: a context is not internally synchronised; use one per owner
+ * thread (bridge.h:37-43). Several contexts may run on different devices
+ * (one per GPU, one process or thread each) without any collective.
+ *
+ * Errors: every function returns a status; no exception, abort, assert or
+ * device trap crosses the ABI. Device-side failures (a bounded wait that ran
+ * out, an out-of-range index) raise a device error word that the next
+ * synchronising call turns into a status.
+ *
+ * Fault injection (host side, for tests of the error paths): the environment
+ * variable ZYNFER_CUDA_FAIL_AT, or zynfer_cu_set_fail_at, takes
+ * "alloc:N" (the N-th device allocation after the call fails with OOM),
+ * "upload" (the next weight upload fails with INTERNAL) or "launch" (the next
+ * call that would launch kernels fails with LAUNCH before launching any).
+ */
+#ifndef ZYNFER_CUDA_H
+#define ZYNFER_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ZYNFER_CU_API __attribute__((visibility("default")))
+#else
+#define ZYNFER_CU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct ZynferCuCtx ZynferCuCtx;
+
+/* Status codes (bridge.h:14-23 pattern). */
+enum {
+    ZYNFER_CU_OK = 0,
+    ZYNFER_CU_NO_DEVICE = 1,
+    ZYNFER_CU_OOM = 2,
+    ZYNFER_CU_INVALID = 3,
+    ZYNFER_CU_UNSUPPORTED = 4,
+    ZYNFER_CU_LAUNCH = 5,
+    ZYNFER_CU_TIMEOUT = 6,
+    ZYNFER_CU_INTERNAL = 7
+};
+
+/* Weight storage of a model. */
+enum {
+    ZYNFER_CU_W_Q8 = 0,   /* int8 per-output-row + f32 scale (packRowQ8, src/backends/cpu/ops.zig:145-162) */
+    ZYNFER_CU_W_BF16 = 1  /* bf16 as stored in a checkpoint (src/runtime/bf16.zig:6-19) */
+};
+
+/* Stable capability record (bridge.h:25-35, hip_probe.h:10-35 pattern). */
+typedef struct ZynferCuCaps {
+    char device_name[256];
+    int sm_major, sm_minor;
+    int sm_count;
+    uint64_t hbm_bytes;
+    uint64_t l2_bytes;
+    uint32_t max_smem_per_block;
+    int bulk_copy;       /* cp.async.bulk + mbarrier path usable (sm_90+) */
+    int tcgen05;         /* sm_100a tensor-core (tcgen05/TMEM) path usable */
+} ZynferCuCaps;
+
+/* Architecture and runtime sizing. Architecture fields follow Arch
+ * (src/model/qwen3.zig:36-59). */
+typedef struct ZynferCuModelDesc {
+    uint32_t vocab, hidden, inter, layers, n_q, n_kv, head_dim, max_pos;
+    float eps, theta;
+    uint32_t weights;         /* ZYNFER_CU_W_Q8 or ZYNFER_CU_W_BF16 */
+    uint32_t max_batch;       /* sequences per decode step */
+    uint32_t max_seqs;        /* sequence slots (ids 0 .. max_seqs-1) */
+    uint32_t max_seq_len;     /* positions per sequence (KvCache max_seq, kv_cache.zig:14-33) */
+    uint32_t kv_blocks;       /* paged pool size in 16-token blocks; 0 = enough for every slot */
+    uint32_t max_prefill;     /* tokens per zynfer_cu_prefill call */
+    uint32_t prefill_kv_f32;  /* 1: prefill attention reads unrounded f32 K/V (the f32
+                                 reference path); 0: the bf16 values the cache stores */
+} ZynferCuModelDesc;
+
+/* ---- context (bridge.h:44-48) ---- */
+ZYNFER_CU_API int zynfer_cu_create(int device, ZynferCuCtx **out);
+ZYNFER_CU_API void zynfer_cu_destroy(ZynferCuCtx *ctx);
+ZYNFER_CU_API int zynfer_cu_caps(const ZynferCuCtx *ctx, ZynferCuCaps *out);
+ZYNFER_CU_API const char *zynfer_cu_last_error(const ZynferCuCtx *ctx);
+ZYNFER_CU_API int zynfer_cu_sync(ZynferCuCtx *ctx);
+ZYNFER_CU_API int zynfer_cu_set_fail_at(ZynferCuCtx *ctx, const char *spec);
+/* Label of the last executed path, e.g. "decode:gemv:graph" (block.zig:20-25 counters). */
+ZYNFER_CU_API const char *zynfer_cu_last_path(const ZynferCuCtx *ctx);
+/* Library build identity (sm target, version). */
+ZYNFER_CU_API const char *zynfer_cu_build_info(void);
+
+/* ---- model and weights (qwen_forward.Session.init, qwen_forward.zig:32-71;
+ *      Weights.load, qwen_weights.zig:61-175) ---- */
+ZYNFER_CU_API int zynfer_cu_model_init(ZynferCuCtx *ctx, const ZynferCuModelDesc *desc);
+/* Upload one tensor by its HF name (qwen3.zig:86-132) in HF layout [out, in].
+ * f32 data is packed on the device (int8 models, bit-exact packRowQ8) or
+ * rounded to bf16 (bf16 models). */
+ZYNFER_CU_API int zynfer_cu_upload_f32(ZynferCuCtx *ctx, const char *name, const float *data, uint64_t rows,
+                         uint64_t cols);
+ZYNFER_CU_API int zynfer_cu_upload_bf16(ZynferCuCtx *ctx, const char *name, const uint16_t *data, uint64_t rows,
+                          uint64_t cols);
+ZYNFER_CU_API int zynfer_cu_upload_q8(ZynferCuCtx *ctx, const char *name, const int8_t *q, const float *scale,
+                        uint64_t rows, uint64_t cols);
+/* Generate every tensor on the device from the seeded synthetic generator:
+ * linears and embedding ~ normal(0, w_std), norm weights 1 + normal(0, norm_std). */
+ZYNFER_CU_API int zynfer_cu_fill_synthetic(ZynferCuCtx *ctx, uint64_t seed, float w_std, float norm_std);
+/* Read back a packed int8 tensor (int8 models) in HF layout. */
+ZYNFER_CU_API int zynfer_cu_download_q8(ZynferCuCtx *ctx, const char *name, int8_t *q, float *scale, uint64_t rows,
+                          uint64_t cols);
+
+/* ---- sequences (KvCache.reset/used, kv_cache.zig:41-47) ---- */
+ZYNFER_CU_API int zynfer_cu_seq_reset(ZynferCuCtx *ctx, uint32_t seq);
+ZYNFER_CU_API int zynfer_cu_seq_len(const ZynferCuCtx *ctx, uint32_t seq, uint32_t *len);
+/* K or V of one layer for positions [0, len): out [n_kv][len][head_dim] f32. */
+ZYNFER_CU_API int zynfer_cu_kv_read(ZynferCuCtx *ctx, uint32_t seq, uint32_t layer, int which_v, float *out);
+
+/* ---- forward ---- */
+/* Session.prefillLastLogits (qwen_forward.zig:89-160): resets `seq`, runs the
+ * n prompt tokens through all layers, then the final norm and tied LM head on
+ * the last row. last_logits [vocab] and argmax may be NULL. */
+ZYNFER_CU_API int zynfer_cu_prefill(ZynferCuCtx *ctx, uint32_t seq, const uint32_t *tokens, uint32_t n,
+                      float *last_logits, uint32_t *argmax);
+/* One greedy decode step for `batch` sequences (block-level decode,
+ * qwen_block.zig:161-235 with t = 1 at pos0 = used, for every layer): feeds
+ * tokens[i] to seqs[i], appends its K/V, and returns the argmax of the new
+ * logits (lowest index on ties, topK qwen_forward.zig:177-193). logits
+ * [batch][vocab] may be NULL. Host buffers; copies are part of the call. */
+ZYNFER_CU_API int zynfer_cu_decode_step(ZynferCuCtx *ctx, const uint32_t *seqs, const uint32_t *tokens,
+                          uint32_t batch, uint32_t *argmax, float *logits);
+/* `steps` greedy steps kept on the device (each step's argmax is the next
+ * step's input). out_ids [steps][batch]; device_ms (nullable) receives the
+ * CUDA-event time of the steps on the context stream. */
+ZYNFER_CU_API int zynfer_cu_generate(ZynferCuCtx *ctx, const uint32_t *seqs, const uint32_t *first,
+                       uint32_t batch, uint32_t steps, uint32_t *out_ids, float *device_ms);
+/* One transformer block (qwen_block.forward, qwen_block.zig:161-235) of layer
+ * `layer` on host hidden states x [t][hidden] at pos0 = the sequence's length;
+ * out [t][hidden]. Appends to the sequence's cache for that layer. */
+ZYNFER_CU_API int zynfer_cu_block_forward(ZynferCuCtx *ctx, uint32_t layer, uint32_t seq, const float *x,
+                            uint32_t t, float *out);
+
+/* ---- op level (device pointers; run on the context stream) ---- */
+/* matvecQ8 / matmul over `batch` rows (ops.zig:181-197): y[b][m] = (W[m,:] . x[b,:]) * scale[m]. */
+ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, const float *scale,
+                     const float *x, uint32_t batch, uint32_t m, uint32_t k, float *y);
+/* packRowQ8 (ops.zig:145-162) on the device, bit-exact. */
+ZYNFER_CU_API int zynfer_cu_pack_q8(ZynferCuCtx *ctx, const float *w, uint32_t rows, uint32_t cols, int8_t *q,
+                      float *scale);
+/* rmsNorm (ops.zig:49-67) over rows. */
+ZYNFER_CU_API int zynfer_cu_rmsnorm(ZynferCuCtx *ctx, const float *x, const float *w, uint32_t rows, uint32_t cols,
+                      float eps, float *y);
+
+/* ---- timing (signpost intervals, bridge.h:94-99) ---- */
+/* Per-kernel-class CUDA-event timing of decode steps (eager launches while on). */
+ZYNFER_CU_API int zynfer_cu_set_timing(ZynferCuCtx *ctx, int enable);
+enum { ZYNFER_CU_K_ATTN = 0, ZYNFER_CU_K_LINEAR = 1, ZYNFER_CU_K_LMHEAD = 2, ZYNFER_CU_K_OTHER = 3 };
+ZYNFER_CU_API int zynfer_cu_kernel_time(const ZynferCuCtx *ctx, int kernel_class, uint64_t *launches, double *total_ms);
+ZYNFER_CU_API uint64_t zynfer_cu_last_step_ns(const ZynferCuCtx *ctx);
+/* Kernels one decode step enqueues (the last one built). */
+ZYNFER_CU_API int zynfer_cu_step_launches(const ZynferCuCtx *ctx);
+/* Host->device and device->host bytes copied by decode/generate/prefill calls
+ * since the last reset (reset != 0 clears after reading). */
+ZYNFER_CU_API int zynfer_cu_io_bytes(ZynferCuCtx *ctx, uint64_t *h2d, uint64_t *d2h, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

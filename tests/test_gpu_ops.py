@@ -1,0 +1,139 @@
+"""Op-level parity of the CUDA kernels against the oracle (B200 only).
+
+Tolerances: int8 packing is bit-exact; f32-accumulate linears and norms use
+the reference's GPU-vs-CPU tolerance for reductions (docs/numerics.md:24-28,
+q8 GEMV 2e-4) with the compare.zig rule max_abs <= atol + rtol * |expected|.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from zynfer_b200 import cuda as zc
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    g = zc.Gpu(0)
+    yield g
+    g.close()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    return t.cpu().numpy()
+
+
+def test_caps(gpu):
+    c = gpu.caps()
+    assert c.sm_major == 10 and c.sm_count >= 132
+    assert c.tcgen05 == 1 and c.bulk_copy == 1
+
+
+def test_pack_q8_device_is_bit_exact(gpu):  # ops.zig:145-162
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((257, 1024)) * 0.02).astype(np.float32)
+    w[0] = 0.0                                        # zero row: scale 1
+    w[1, :4] = [127.0, -63.5, 0.5, -0.5]              # ties round away from zero
+    w[1, 4:] = 0.0
+    w[2] = np.float32(1e-30)                          # tiny values
+    q_ref, s_ref = O.pack_row_q8(w)
+    wd = dev(w)
+    qd = torch.empty((257, 1024), dtype=torch.int8, device="cuda")
+    sd = torch.empty(257, dtype=torch.float32, device="cuda")
+    gpu.pack_q8(wd, 257, 1024, qd, sd)
+    gpu.sync()
+    assert np.array_equal(host(qd), q_ref)
+    assert np.array_equal(host(sd), s_ref)
+
+
+SHAPES = [(3072, 1024), (4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072), (151936, 1024)]
+
+
+@pytest.mark.parametrize("m,k", SHAPES)
+@pytest.mark.parametrize("batch", [1, 8])
+def test_linear_q8_matches_matvec_q8(gpu, m, k, batch):  # ops.zig:181-197
+    w = O.synth_normal(m * k, 77, 1000 + m + k, 0.02).reshape(m, k)
+    q, s = O.pack_row_q8(w)
+    x = O.synth_normal(batch * k, 78, 5, 1.0).reshape(batch, k)
+    y = torch.empty((batch, m), dtype=torch.float32, device="cuda")
+    gpu.linear(zc.W_Q8, dev(q), dev(s), dev(x), batch, m, k, y)
+    gpu.sync()
+    got = host(y)
+    for b in range(batch):
+        ref = O.matvec_q8(q, s, x[b], threads=8)
+        d = O.diff(ref, got[b])
+        assert O.expect_close(ref, got[b], 2e-4, 2e-4), (b, d.max_abs, d.failing_index)
+
+
+@pytest.mark.parametrize("batch", [2, 3, 5, 9, 16, 64, 100])
+def test_linear_q8_batches(gpu, batch):  # gemv (<= 8 rows) and the tiled GEMM (> 8 rows)
+    m, k = 1024, 3072
+    w = O.synth_normal(m * k, 9, 9, 0.02).reshape(m, k)
+    q, s = O.pack_row_q8(w)
+    x = O.synth_normal(batch * k, 10, 5, 1.0).reshape(batch, k)
+    y = torch.empty((batch, m), dtype=torch.float32, device="cuda")
+    gpu.linear(zc.W_Q8, dev(q), dev(s), dev(x), batch, m, k, y)
+    gpu.sync()
+    got = host(y)
+    for b in range(batch):
+        assert O.expect_close(O.matvec_q8(q, s, x[b]), got[b], 2e-4, 2e-4), b
+
+
+@pytest.mark.parametrize("batch", [1, 4, 24])
+def test_linear_bf16_matches_matvec(gpu, batch):  # ops.zig:133-141 on bf16-widened weights
+    from oracle import synth_np
+    m, k = 2048, 1024
+    w = synth_np.bf16_round(O.synth_normal(m * k, 4, 4, 0.02)).reshape(m, k)
+    bits = synth_np.bf16_bits(w)
+    x = O.synth_normal(batch * k, 5, 5, 1.0).reshape(batch, k)
+    y = torch.empty((batch, m), dtype=torch.float32, device="cuda")
+    gpu.linear(zc.W_BF16, dev(bits.view(np.int16)), None, dev(x), batch, m, k, y)
+    gpu.sync()
+    got = host(y)
+    for b in range(batch):
+        assert O.expect_close(O.matvec(w, x[b]), got[b], 1e-4, 1e-4), b
+
+
+def test_rmsnorm_matches_oracle(gpu):  # ops.zig:49-67
+    x = O.synth_normal(37 * 1024, 1, 2, 1.0).reshape(37, 1024)
+    w = 1.0 + O.synth_normal(1024, 1, 3, 0.1)
+    y = torch.empty((37, 1024), dtype=torch.float32, device="cuda")
+    gpu.rmsnorm(dev(x), dev(w), 37, 1024, 1e-6, y)
+    gpu.sync()
+    assert O.expect_close(O.rms_norm(x, w), host(y), 1e-5, 1e-5)
+
+
+def test_rmsnorm_plus_minus_one(gpu):  # tests/numerical/ops.zig:16-32
+    x = np.tile(np.array([1, -1], np.float32), 64).reshape(1, 128)
+    y = torch.empty((1, 128), dtype=torch.float32, device="cuda")
+    gpu.rmsnorm(dev(x), dev(np.ones(128, np.float32)), 1, 128, 1e-6, y)
+    gpu.sync()
+    out = host(y)
+    assert abs(out[0, 0] - 1) <= 1e-5 and abs(out[0, 1] + 1) <= 1e-5
+
+
+def test_injected_launch_fault_then_recovers(gpu):
+    m, k = 512, 512
+    q = dev(np.ones((m, k), np.int8))
+    s = dev(np.ones(m, np.float32))
+    x = dev(np.ones((1, k), np.float32))
+    y = torch.empty((1, m), dtype=torch.float32, device="cuda")
+    gpu.set_fail_at("launch")
+    with pytest.raises(zc.LaunchFailed):
+        gpu.linear(zc.W_Q8, q, s, x, 1, m, k, y)
+    gpu.linear(zc.W_Q8, q, s, x, 1, m, k, y)
+    gpu.sync()
+    assert np.all(host(y) == 512.0)
+
+
+def test_linear_rejects_bad_k(gpu):
+    y = torch.empty((1, 8), dtype=torch.float32, device="cuda")
+    with pytest.raises(zc.Unsupported):
+        gpu.linear(zc.W_Q8, y, y, y, 1, 8, 100, y)

@@ -1,0 +1,148 @@
+// Shared device helpers for the sm_100a Qwen3 kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace zc {
+
+constexpr int kWarp = 32;
+constexpr int kKvBlock = 16;  // tokens per paged KV block
+
+// Device error word, set instead of trapping. Codes (bitwise OR):
+enum : uint32_t {
+    kErrTimeout = 1u,       // a bounded mbarrier wait ran out
+    kErrBadIndex = 2u,      // an index check failed (token id, block id)
+};
+
+// ---------------------------------------------------------------- numerics
+
+// bf16 bits -> f32 (exact).
+__device__ __forceinline__ float bf16lo(uint32_t two) { return __uint_as_float(two << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t two) { return __uint_as_float(two & 0xFFFF0000u); }
+
+// f32 -> bf16 bits, round to nearest even (NaN kept quiet), written out so the
+// rounding is explicit and identical to the host restatement.
+__device__ __forceinline__ uint16_t f32_to_bf16_rne(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+__device__ __forceinline__ float bf16_round(float x) {
+    return __uint_as_float((uint32_t)f32_to_bf16_rne(x) << 16);
+}
+
+// Four packed int8 -> four exact f32, without the int->float converter:
+// bias each byte to unsigned (xor 0x80), place it in the low mantissa byte of
+// 2^23 (0x4B000000), and subtract 2^23 + 128 (Kim et al., "Who Says Elephants
+// Can't Run", 2022, applied to f32). Exact for every int8 value.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& f0, float& f1, float& f2, float& f3) {
+    const uint32_t u = w ^ 0x80808080u;
+    const float magic = 8388736.0f;  // 2^23 + 128
+    f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - magic;
+    f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - magic;
+    f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - magic;
+    f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - magic;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    return v;
+}
+
+// Orderable key for a (logit, index) pair: a larger key is a larger logit,
+// and among equal logits the lower index (the reference's topK keeps the
+// first maximum, qwen_forward.zig:177-193). topK starts from (id 0, -inf) and
+// takes a logit only when it is strictly greater, so NaN and -inf never win:
+// they map to key 0, and an all-zero key decodes to id 0.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+    const uint32_t u = __float_as_uint(v);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u || u == 0xFF800000u) return 0ull;  // NaN, -inf
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+__device__ __forceinline__ uint32_t argmax_key_index(unsigned long long key) {
+    return 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
+}
+
+// 16-byte read-only global load that does not allocate in L1 (streamed once).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// ------------------------------------------------------ mbarrier + bulk copy
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after `limit` polls (each try_wait itself blocks for
+// a hardware-defined interval), sets kErrTimeout in *err and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                                  uint32_t limit = (1u << 22)) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicOr(err, kErrTimeout);
+    return false;
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completing on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait for the previous kernel's results before reading them.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+}  // namespace zc

@@ -1,0 +1,213 @@
+// Weight-only GEMV for 1..8 activation rows: y[b, r] = (sum_k W[r, k] x[b, k]) * scale[r]
+// (matvecQ8, src/backends/cpu/ops.zig:181-197), W int8 (per-row scale) or bf16.
+//
+// Design (HBM-bound): each warp streams whole weight rows with 16-byte
+// read-only loads (one row = K bytes for int8, 2K for bf16; a warp covers 512
+// contiguous bytes per instruction), converts int8 with the byte-permute
+// magic-number trick, and multiplies against activations staged once per CTA
+// in shared memory (optionally RMS-normalised on the way in). The shared
+// layout is swizzled so the 16-byte activation reads of a warp hit 32
+// distinct banks. A persistent grid (a few CTAs per SM) walks row groups so
+// the activation staging cost is paid ~600 times, not once per row group.
+// Epilogues: scale, residual add, SwiGLU over interleaved (gate, up) rows,
+// and a fused argmax for the LM head (orderable 64-bit key, atomicMax).
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace zc {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / kWarp;
+
+// Position of activation k in the swizzled shared row. int8 lanes read 16
+// consecutive k (four float4 groups); bf16 lanes read 8 (two groups).
+template <int WK>
+__device__ __forceinline__ int swz(int k) {
+    if constexpr (WK == kWQ8) {
+        return (k & ~15) | (((((k >> 2) & 3) + ((k >> 5) & 3)) & 3) << 2) | (k & 3);
+    } else {
+        return (k & ~7) | (((((k >> 2) & 1) + ((k >> 5) & 1)) & 1) << 2) | (k & 3);
+    }
+}
+
+__device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
+
+template <int WK, int NB, int R, int EPI>
+__global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
+    extern __shared__ float xs[];  // [NB][K] swizzled
+    __shared__ float red[kWarps];
+    __shared__ unsigned long long best_s[kWarps][NB];
+    const int K = a.K;
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+
+    // ---- stage activations (RMSNorm prologue when norm_w is set)
+    for (int b = 0; b < a.N; ++b) {
+        const float* xr = a.x + (size_t)b * a.ldx;
+        float inv = 1.0f;
+        if (a.norm_w) {
+            float acc = 0.0f;
+            for (int k = threadIdx.x; k < K; k += kThreads) acc += xr[k] * xr[k];
+            acc = warp_sum(acc);
+            if (lane == 0) red[warp] = acc;
+            __syncthreads();
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) tot += red[w];
+            inv = 1.0f / sqrtf(tot / (float)K + a.eps);
+            __syncthreads();
+        }
+        for (int k = threadIdx.x; k < K; k += kThreads) {
+            const float v = xr[k];
+            xs[b * K + swz<WK>(k)] = a.norm_w ? __fmul_rn(__fmul_rn(a.norm_w[k], v), inv) : v;
+        }
+    }
+    for (int b = a.N; b < NB; ++b)
+        for (int k = threadIdx.x; k < K; k += kThreads) xs[b * K + k] = 0.0f;
+    __syncthreads();
+
+    unsigned long long best[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) best[b] = 0ull;
+
+    constexpr int kElems = WK == kWQ8 ? 16 : 8;     // k values per 16-byte load
+    const int row_bytes = WK == kWQ8 ? K : 2 * K;
+    const int iters = K / (kElems * kWarp);          // K is a multiple of 512 (int8) / 256 (bf16)
+    const int groups = (a.M + R - 1) / R;
+    const char* wbase = reinterpret_cast<const char*>(a.w);
+
+    for (int g = blockIdx.x * kWarps + warp; g < groups; g += gridDim.x * kWarps) {
+        const int r0 = g * R;
+        float acc[R][NB];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) acc[r][b] = 0.0f;
+
+        for (int it = 0; it < iters; ++it) {
+            const int k0 = it * kElems * kWarp + lane * kElems;
+            uint4 wv[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int row = min(r0 + r, a.M - 1);
+                wv[r] = ldg_stream(wbase + (size_t)row * row_bytes + (size_t)k0 * (WK == kWQ8 ? 1 : 2));
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float w[kElems];
+                if constexpr (WK == kWQ8) {
+                    i8x4_to_f32(wv[r].x, w[0], w[1], w[2], w[3]);
+                    i8x4_to_f32(wv[r].y, w[4], w[5], w[6], w[7]);
+                    i8x4_to_f32(wv[r].z, w[8], w[9], w[10], w[11]);
+                    i8x4_to_f32(wv[r].w, w[12], w[13], w[14], w[15]);
+                } else {
+                    w[0] = bf16lo(wv[r].x); w[1] = bf16hi(wv[r].x);
+                    w[2] = bf16lo(wv[r].y); w[3] = bf16hi(wv[r].y);
+                    w[4] = bf16lo(wv[r].z); w[5] = bf16hi(wv[r].z);
+                    w[6] = bf16lo(wv[r].w); w[7] = bf16hi(wv[r].w);
+                }
+#pragma unroll
+                for (int b = 0; b < NB; ++b) {
+                    const float* xb = xs + b * K;
+#pragma unroll
+                    for (int q = 0; q < kElems / 4; ++q) {
+                        const float4 xv = *reinterpret_cast<const float4*>(xb + swz<WK>(k0 + 4 * q));
+                        acc[r][b] = fmaf(w[4 * q + 0], xv.x, acc[r][b]);
+                        acc[r][b] = fmaf(w[4 * q + 1], xv.y, acc[r][b]);
+                        acc[r][b] = fmaf(w[4 * q + 2], xv.z, acc[r][b]);
+                        acc[r][b] = fmaf(w[4 * q + 3], xv.w, acc[r][b]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) acc[r][b] = warp_sum(acc[r][b]);
+
+        // every lane holds the sums; lane b (< NB) writes batch row b
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            if (b >= a.N) break;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int row = r0 + r;
+                if (row >= a.M) break;
+                const float s = a.scale ? a.scale[row] : 1.0f;
+                const float val = __fmul_rn(acc[r][b], s);
+                if constexpr (EPI == kEpiSwiGLU) {
+                    if ((r & 1) == 1 && lane == b) {
+                        const float gate = __fmul_rn(acc[r - 1][b], a.scale ? a.scale[row - 1] : 1.0f);
+                        a.y[(size_t)b * a.ldy + (row >> 1)] = __fmul_rn(silu(gate), val);
+                    }
+                } else if constexpr (EPI == kEpiResid) {
+                    if (lane == b) a.y[(size_t)b * a.ldy + row] = __fadd_rn(a.resid[(size_t)b * a.ldy + row], val);
+                } else if constexpr (EPI == kEpiArgmax) {
+                    if (lane == b && a.y) a.y[(size_t)b * a.ldy + row] = val;
+                    const unsigned long long key = argmax_key(val, (uint32_t)row);
+                    best[b] = key > best[b] ? key : best[b];
+                } else {
+                    if (lane == b) a.y[(size_t)b * a.ldy + row] = val;
+                }
+            }
+        }
+    }
+
+    if constexpr (EPI == kEpiArgmax) {
+        if (lane == 0)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) best_s[warp][b] = best[b];
+        __syncthreads();
+        if (threadIdx.x < a.N) {
+            unsigned long long m = 0ull;
+            for (int w = 0; w < kWarps; ++w) m = best_s[w][threadIdx.x] > m ? best_s[w][threadIdx.x] : m;
+            if (m) atomicMax(a.argmax_keys + threadIdx.x, m);
+        }
+    }
+}
+
+template <int WK, int NB, int R>
+void launch_nb(const LinearArgs& a, cudaStream_t st) {
+    const size_t smem = (size_t)NB * a.K * sizeof(float);
+    const int groups = (a.M + R - 1) / R;
+    auto pick = [&](auto kern) {
+        // The opt-in shared-memory ceiling is a per-device function attribute.
+        static bool attr_set[64] = {false};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 3072 * 4);
+            attr_set[dev] = true;
+        }
+        // resident CTAs per SM: bounded by threads (2048 / 256) and shared memory
+        const int per_sm = std::max(1, std::min(8, (int)((220 * 1024) / (smem + 2048))));
+        const int want = (groups + kWarps - 1) / kWarps;
+        kern<<<std::min(want, per_sm * device_sm_count()), kThreads, smem, st>>>(a);
+    };
+    switch (a.epi) {
+        case kEpiResid: pick(gemv_kernel<WK, NB, R, kEpiResid>); break;
+        case kEpiSwiGLU: pick(gemv_kernel<WK, NB, R, kEpiSwiGLU>); break;
+        case kEpiArgmax: pick(gemv_kernel<WK, NB, R, kEpiArgmax>); break;
+        default: pick(gemv_kernel<WK, NB, R, kEpiNone>); break;
+    }
+}
+
+template <int WK>
+void launch_wk(const LinearArgs& a, cudaStream_t st) {
+    if (a.N <= 1) launch_nb<WK, 1, 4>(a, st);
+    else if (a.N <= 2) launch_nb<WK, 2, 4>(a, st);
+    else if (a.N <= 4) launch_nb<WK, 4, 2>(a, st);
+    else launch_nb<WK, 8, 2>(a, st);
+}
+
+}  // namespace
+
+void launch_gemv(const LinearArgs& a, cudaStream_t st) {
+    if (a.wkind == kWQ8) launch_wk<kWQ8>(a, st);
+    else launch_wk<kWBF16>(a, st);
+}
+
+}  // namespace zc

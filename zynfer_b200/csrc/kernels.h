@@ -1,0 +1,129 @@
+// Host-side launchers for the sm_100a kernels (internal to libzynfer_cuda).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace zc {
+
+enum WKind : int { kWQ8 = 0, kWBF16 = 1 };
+
+// Linear-layer epilogues.
+enum Epi : int {
+    kEpiNone = 0,     // y = acc * scale
+    kEpiResid = 1,    // y = resid + acc * scale
+    kEpiSwiGLU = 2,   // rows (2j, 2j+1) = (gate_j, up_j): y[j] = silu(g) * u
+    kEpiArgmax = 3,   // optional logits write + argmax key per batch row
+};
+
+struct LinearArgs {
+    const void* w = nullptr;       // [M][K] int8 or bf16, row-major (HF [out, in])
+    const float* scale = nullptr;  // [M] (int8) or nullptr (bf16)
+    int wkind = kWQ8;
+    int M = 0, K = 0;
+    const float* x = nullptr;      // [N][ldx] f32 activations
+    int ldx = 0;
+    int N = 0;                     // batch rows (tokens / sequences)
+    float* y = nullptr;            // [N][ldy] f32 output
+    int ldy = 0;
+    int epi = kEpiNone;
+    const float* resid = nullptr;  // [N][ldy] for kEpiResid (may alias y)
+    const float* norm_w = nullptr; // optional RMSNorm applied to x rows first (GEMV only)
+    float eps = 1e-6f;
+    unsigned long long* argmax_keys = nullptr;  // [N] for kEpiArgmax
+};
+
+// synth.cu
+int device_sm_count();  // SMs of the current device (cached)
+void launch_synth_normal(float* out, size_t n, uint64_t seed, uint64_t stream, float k,
+                         float add, cudaStream_t st);
+void launch_fill(float* out, size_t n, float v, cudaStream_t st);
+void launch_pack_q8_rows(const float* w, int rows, int cols, int8_t* q, float* scale,
+                         int dst_stride, int dst_offset, cudaStream_t st);
+void launch_to_bf16_rows(const float* w, int rows, int cols, uint16_t* out, int dst_stride,
+                         int dst_offset, cudaStream_t st);
+void launch_copy_rows_i8(const int8_t* src, const float* ssrc, int rows, int cols, int8_t* dst,
+                         float* sdst, int dst_stride, int dst_offset, cudaStream_t st);
+void launch_copy_rows_u16(const uint16_t* src, int rows, int cols, uint16_t* dst, int dst_stride,
+                          int dst_offset, cudaStream_t st);
+void launch_unpack_rows_i8(const int8_t* src, const float* ssrc, int rows, int cols, int8_t* dst,
+                           float* sdst, int src_stride, int src_offset, cudaStream_t st);
+
+// norm.cu
+void launch_rmsnorm(const float* x, const float* w, float* y, int rows, int cols, float eps,
+                    cudaStream_t st);
+void launch_embed(const void* table, const float* scale, int wkind, const uint32_t* ids, int n,
+                  int H, int V, float* x, uint32_t* err, cudaStream_t st);
+struct QkvArgs {
+    const float* qkv;  // [T][ (n_q + 2 n_kv) * d ]
+    int T, n_q, n_kv, d;
+    const float* q_norm;
+    const float* k_norm;
+    float eps;
+    const float2* rope;  // [max_pos][d/2] (cos, sin)
+    int rope_max_pos;
+    // positions: row_pos[t] (nullable -> pos0 + t); sequences: row_seq[t] (nullable -> seq0)
+    const int* row_pos;
+    int pos0;
+    const int* row_seq;
+    int seq0;
+    // paged bf16 cache
+    uint16_t* kv_layer;         // this layer's pool base: [blocks][2][n_kv][16][d]
+    const int* block_table;     // [seqs][max_blocks]
+    int max_blocks;
+    int n_pool_blocks;
+    // outputs
+    float* q_out;          // decode: [T][n_q][d]; prefill: heads-major [n_q][T][d]
+    int q_heads_major;
+    float* k_stage;        // prefill only (nullable): [n_kv][T][d]
+    float* v_stage;
+    int stage_round_bf16;  // staged K/V rounded to bf16 (the values the cache holds)
+    uint32_t* err;
+};
+void launch_qkv_post(const QkvArgs& a, cudaStream_t st);
+struct FinalizeArgs {
+    unsigned long long* keys;  // [B], reset to 0 after reading
+    uint32_t* ids_out;         // [B] argmax ids
+    uint32_t* next_tokens;     // [B] (nullable) next step's input ids
+    int* positions;            // [B] (nullable) incremented by one
+    uint32_t* history;         // (nullable) [steps][B]; row = *step, then *step += 1
+    int* step;
+    int B;                     // <= 1024 (one CTA)
+};
+void launch_bf16_to_f32(const uint16_t* src, size_t n, float* dst, cudaStream_t st);
+void launch_finalize(const FinalizeArgs& a, cudaStream_t st);
+
+// gemv.cu (N <= 8)
+void launch_gemv(const LinearArgs& a, cudaStream_t st);
+// gemm_simt.cu (any N)
+void launch_gemm_simt(const LinearArgs& a, cudaStream_t st);
+
+// attn.cu
+struct AttnDecodeArgs {
+    const float* q;             // [B][n_q][d]
+    const uint16_t* kv_layer;   // [blocks][2][n_kv][16][d]
+    const int* block_table;     // [seqs][max_blocks]
+    int max_blocks;
+    int n_pool_blocks;
+    const int* seq_of;          // [B] sequence slot per batch row
+    const int* positions;       // [B] position of the current token (kv_len = pos + 1)
+    int B, n_q, n_kv, d;
+    int chunk;                  // tokens per split (multiple of 32)
+    int max_splits;
+    float* partial;             // [B][n_kv][max_splits][group][d + 2]
+    unsigned int* counters;     // [B][n_kv], zero between launches
+    float* out;                 // [B][n_q][d]
+    uint32_t* err;
+};
+void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st);
+struct AttnPrefillArgs {
+    const float* q;   // [n_q][T][d]
+    const float* k;   // [n_kv][T][d]
+    const float* v;
+    int T, n_q, n_kv, d;
+    float* out;       // [T][n_q][d]
+};
+void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st);
+
+}  // namespace zc

@@ -1,0 +1,1190 @@
+// C ABI of the Zynfer `cuda` backend: context, weights, paged KV cache,
+// prefill / decode schedules and CUDA graphs. See include/zynfer_cuda.h.
+//
+// The host schedule mirrors the reference's Qwen3 forward
+// (src/model/qwen_forward.zig:94-175 around src/model/qwen_block.zig:161-235)
+// with the B200 layout: fused QKV and interleaved gate/up weights, a paged
+// bf16 KV pool of 16-token blocks, token-major activations, and one captured
+// CUDA graph per decode batch size.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/zynfer_cuda.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "synth_rng.h"
+
+using namespace zc;
+
+namespace {
+
+struct LayerDev {
+    void* wqkv = nullptr;
+    float* sqkv = nullptr;
+    void* wo = nullptr;
+    float* so = nullptr;
+    void* wgu = nullptr;
+    float* sgu = nullptr;
+    void* wd = nullptr;
+    float* sd = nullptr;
+    float* input_ln = nullptr;
+    float* post_ln = nullptr;
+    float* q_norm = nullptr;
+    float* k_norm = nullptr;
+};
+
+struct TimedEvent {
+    cudaEvent_t a, b;
+    int cls;
+};
+
+}  // namespace
+
+struct ZynferCuCtx {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    std::string path = "none";
+    ZynferCuCaps caps{};
+
+    // fault injection
+    long fail_alloc_at = -1;
+    long alloc_count = 0;
+    bool fail_upload = false;
+    bool fail_launch = false;
+    std::vector<void*> allocs;
+    std::vector<void*> pinned;
+
+    // model
+    bool ready = false;
+    ZynferCuModelDesc d{};
+    int wkind = kWQ8;
+    size_t esz = 1;
+    int qd = 0, kvd = 0, qkv_rows = 0;
+    std::vector<LayerDev> L;
+    void* embed = nullptr;
+    float* sembed = nullptr;
+    float* final_norm = nullptr;
+    float2* rope = nullptr;
+    uint16_t* kv = nullptr;
+    size_t kv_layer_elems = 0;
+    int max_blocks = 0, n_blocks = 0;
+    std::vector<int> free_blocks;
+    std::vector<std::vector<int>> seq_blocks;
+    std::vector<uint32_t> seq_len;
+    std::vector<char> table_dirty;  // host row changed since its last upload
+    int* table_host = nullptr;  // pinned [max_seqs][max_blocks]
+    int* table_dev = nullptr;
+
+    // decode scratch (max_batch rows)
+    float *dx = nullptr, *dx1 = nullptr, *dxn = nullptr, *dqkv = nullptr, *dq = nullptr,
+          *dattn = nullptr, *dh = nullptr, *dlogits = nullptr, *dpart = nullptr;
+    uint32_t* dio = nullptr;  // [tokens B][seq B][pos B] contiguous
+    uint32_t* dtok = nullptr;
+    int* dseq = nullptr;
+    int* dpos = nullptr;
+    unsigned long long* dkeys = nullptr;
+    uint32_t* dids = nullptr;
+    unsigned* dcnt = nullptr;
+    uint32_t* dhist = nullptr;
+    int* dstep = nullptr;
+    size_t hist_cap = 0;  // entries
+    // prefill scratch (max_prefill rows)
+    float *px = nullptr, *px1 = nullptr, *pxn = nullptr, *pqkv = nullptr, *pq = nullptr,
+          *pk = nullptr, *pv = nullptr, *pattn = nullptr, *ph = nullptr;
+    uint32_t* ptok = nullptr;
+    // device error word and pinned host staging
+    uint32_t* derr = nullptr;
+    uint32_t* herr = nullptr;
+    uint32_t* hio = nullptr;   // pinned [3 * max_batch]
+    uint32_t* hids = nullptr;  // pinned [max_batch]
+
+    std::map<int, cudaGraphExec_t> graphs;
+    int step_launches = 0;  // kernels enqueued by the last decode step
+    uint64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device bytes of decode/generate calls
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    uint64_t last_step_ns = 0;
+
+    // per-kernel timing
+    bool timing = false;
+    std::vector<TimedEvent> tev;
+    size_t tev_used = 0;
+    uint64_t t_launch[4] = {0, 0, 0, 0};
+    double t_ms[4] = {0, 0, 0, 0};
+};
+
+namespace {
+
+int fail(ZynferCuCtx* c, int code, const std::string& msg) {
+    if (c) c->err = msg;
+    return code;
+}
+
+int cuda_fail(ZynferCuCtx* c, cudaError_t e, const char* what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+    int code = e == cudaErrorMemoryAllocation ? ZYNFER_CU_OOM : ZYNFER_CU_LAUNCH;
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) code = ZYNFER_CU_NO_DEVICE;
+    return fail(c, code, m);
+}
+
+#define ZC_CHECK(c, expr, what)                          \
+    do {                                                 \
+        cudaError_t e_ = (expr);                         \
+        if (e_ != cudaSuccess) return cuda_fail(c, e_, what); \
+    } while (0)
+
+template <typename T>
+int dalloc(ZynferCuCtx* c, T** p, size_t count) {
+    *p = nullptr;
+    if (c->fail_alloc_at >= 0 && c->alloc_count++ == c->fail_alloc_at) {
+        c->fail_alloc_at = -1;
+        return fail(c, ZYNFER_CU_OOM, "injected allocation failure (ZYNFER_CUDA_FAIL_AT=alloc)");
+    }
+    void* v = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(c, ZYNFER_CU_OOM, std::string("cudaMalloc(") + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    }
+    c->allocs.push_back(v);
+    *p = reinterpret_cast<T*>(v);
+    return ZYNFER_CU_OK;
+}
+
+template <typename T>
+int halloc(ZynferCuCtx* c, T** p, size_t count) {
+    void* v = nullptr;
+    cudaError_t e = cudaMallocHost(&v, std::max<size_t>(count * sizeof(T), 16));
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaMallocHost");
+    c->pinned.push_back(v);
+    *p = reinterpret_cast<T*>(v);
+    return ZYNFER_CU_OK;
+}
+
+void parse_fail_spec(ZynferCuCtx* c, const char* spec) {
+    if (!spec || !*spec) return;
+    if (strncmp(spec, "alloc:", 6) == 0) {
+        c->fail_alloc_at = atol(spec + 6);
+        c->alloc_count = 0;
+    } else if (strcmp(spec, "upload") == 0) {
+        c->fail_upload = true;
+    } else if (strcmp(spec, "launch") == 0) {
+        c->fail_launch = true;
+    }
+}
+
+bool take_launch_fault(ZynferCuCtx* c) {
+    if (!c->fail_launch) return false;
+    c->fail_launch = false;
+    c->err = "injected launch failure (ZYNFER_CUDA_FAIL_AT=launch)";
+    return true;
+}
+
+// Map an HF tensor name (qwen3.zig:86-132) to its device destination.
+struct Dest {
+    enum Kind { None, Vec, Mat } kind = None;
+    float* vec = nullptr;
+    void* w = nullptr;
+    float* s = nullptr;
+    int rows = 0, cols = 0;          // HF shape
+    int stride = 1, offset = 0;      // destination row = r * stride + offset
+};
+
+Dest find_dest(ZynferCuCtx* c, const char* name) {
+    Dest d;
+    const ZynferCuModelDesc& m = c->d;
+    const int H = m.hidden, I = m.inter, hd = m.head_dim;
+    if (!strcmp(name, "model.embed_tokens.weight") || !strcmp(name, "lm_head.weight")) {
+        d.kind = Dest::Mat; d.w = c->embed; d.s = c->sembed; d.rows = m.vocab; d.cols = H;
+        return d;
+    }
+    if (!strcmp(name, "model.norm.weight")) {
+        d.kind = Dest::Vec; d.vec = c->final_norm; d.rows = H; d.cols = 1;
+        return d;
+    }
+    unsigned layer = 0;
+    char rest[128];
+    if (sscanf(name, "model.layers.%u.%127s", &layer, rest) != 2 || layer >= m.layers) return d;
+    LayerDev& Ld = c->L[layer];
+    auto vec = [&](float* p, int n) { d.kind = Dest::Vec; d.vec = p; d.rows = n; d.cols = 1; };
+    auto mat = [&](void* w, float* s, int r, int cc, int stride, int offset) {
+        d.kind = Dest::Mat; d.w = w; d.s = s; d.rows = r; d.cols = cc; d.stride = stride; d.offset = offset;
+    };
+    if (!strcmp(rest, "input_layernorm.weight")) vec(Ld.input_ln, H);
+    else if (!strcmp(rest, "post_attention_layernorm.weight")) vec(Ld.post_ln, H);
+    else if (!strcmp(rest, "self_attn.q_norm.weight")) vec(Ld.q_norm, hd);
+    else if (!strcmp(rest, "self_attn.k_norm.weight")) vec(Ld.k_norm, hd);
+    else if (!strcmp(rest, "self_attn.q_proj.weight")) mat(Ld.wqkv, Ld.sqkv, c->qd, H, 1, 0);
+    else if (!strcmp(rest, "self_attn.k_proj.weight")) mat(Ld.wqkv, Ld.sqkv, c->kvd, H, 1, c->qd);
+    else if (!strcmp(rest, "self_attn.v_proj.weight")) mat(Ld.wqkv, Ld.sqkv, c->kvd, H, 1, c->qd + c->kvd);
+    else if (!strcmp(rest, "self_attn.o_proj.weight")) mat(Ld.wo, Ld.so, H, c->qd, 1, 0);
+    else if (!strcmp(rest, "mlp.gate_proj.weight")) mat(Ld.wgu, Ld.sgu, I, H, 2, 0);
+    else if (!strcmp(rest, "mlp.up_proj.weight")) mat(Ld.wgu, Ld.sgu, I, H, 2, 1);
+    else if (!strcmp(rest, "mlp.down_proj.weight")) mat(Ld.wd, Ld.sd, H, I, 1, 0);
+    return d;
+}
+
+// Place an f32 HF-layout tensor already on the device into its destination.
+void place_f32(ZynferCuCtx* c, const Dest& d, const float* src) {
+    if (d.kind == Dest::Vec) {
+        cudaMemcpyAsync(d.vec, src, (size_t)d.rows * 4, cudaMemcpyDeviceToDevice, c->stream);
+    } else if (c->wkind == kWQ8) {
+        launch_pack_q8_rows(src, d.rows, d.cols, reinterpret_cast<int8_t*>(d.w), d.s, d.stride, d.offset,
+                            c->stream);
+    } else {
+        launch_to_bf16_rows(src, d.rows, d.cols, reinterpret_cast<uint16_t*>(d.w), d.stride, d.offset,
+                            c->stream);
+    }
+}
+
+int check_device_error(ZynferCuCtx* c) {
+    ZC_CHECK(c, cudaMemcpyAsync(c->herr, c->derr, 4, cudaMemcpyDeviceToHost, c->stream), "read error word");
+    c->d2h_bytes += 4;
+    ZC_CHECK(c, cudaStreamSynchronize(c->stream), "stream synchronize");
+    const uint32_t e = *c->herr;
+    if (!e) return ZYNFER_CU_OK;
+    cudaMemsetAsync(c->derr, 0, 4, c->stream);
+    cudaMemsetAsync(c->dcnt, 0, (size_t)c->d.max_batch * c->d.n_kv * 4, c->stream);
+    cudaStreamSynchronize(c->stream);
+    if (e & kErrTimeout) return fail(c, ZYNFER_CU_TIMEOUT, "device wait timed out (bounded mbarrier wait)");
+    return fail(c, ZYNFER_CU_INVALID, "device index check failed (token id, position or KV block)");
+}
+
+int decode_chunk(int B) { return B <= 2 ? 64 : (B <= 16 ? 128 : 256); }
+
+// --------------------------------------------------------- timing helpers
+void tbegin(ZynferCuCtx* c, int cls, TimedEvent** te) {
+    *te = nullptr;
+    if (!c->timing) return;
+    if (c->tev_used == c->tev.size()) {
+        // fold completed intervals into the totals, then reuse the pool
+        cudaStreamSynchronize(c->stream);
+        for (size_t i = 0; i < c->tev_used; ++i) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, c->tev[i].a, c->tev[i].b);
+            c->t_ms[c->tev[i].cls] += ms;
+            c->t_launch[c->tev[i].cls] += 1;
+        }
+        c->tev_used = 0;
+    }
+    TimedEvent* e = &c->tev[c->tev_used++];
+    e->cls = cls;
+    cudaEventRecord(e->a, c->stream);
+    *te = e;
+}
+void tend(ZynferCuCtx* c, TimedEvent* te) {
+    if (te) cudaEventRecord(te->b, c->stream);
+}
+
+void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, int M, int K, const float* x, int N,
+            float* y, int epi, const float* resid, const float* norm_w, unsigned long long* keys) {
+    LinearArgs a;
+    a.w = w; a.scale = s; a.wkind = c->wkind; a.M = M; a.K = K; a.x = x; a.ldx = K; a.N = N;
+    a.y = y; a.ldy = epi == kEpiSwiGLU ? M / 2 : M; a.epi = epi; a.resid = resid; a.norm_w = norm_w;
+    a.eps = c->d.eps; a.argmax_keys = keys;
+    TimedEvent* te;
+    tbegin(c, cls, &te);
+    if (N <= 8) launch_gemv(a, c->stream);
+    else launch_gemm_simt(a, c->stream);
+    tend(c, te);
+    c->step_launches += 1;
+}
+
+// One decode step for the rows already staged in dtok/dseq/dpos.
+void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
+    const ZynferCuModelDesc& m = c->d;
+    const int H = m.hidden, I = m.inter;
+    const int chunk = decode_chunk(B);
+    const int max_splits = (int)((m.max_seq_len + chunk - 1) / chunk);
+    c->step_launches = 0;
+    TimedEvent* te;
+    tbegin(c, ZYNFER_CU_K_OTHER, &te);
+    launch_embed(c->embed, c->sembed, c->wkind, c->dtok, B, H, m.vocab, c->dx, c->derr, c->stream);
+    tend(c, te);
+    c->step_launches += 1;
+    for (uint32_t l = 0; l < m.layers; ++l) {
+        const LayerDev& Ld = c->L[l];
+        if (B <= 8) {
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, c->qkv_rows, H, c->dx, B, c->dqkv, kEpiNone,
+                   nullptr, Ld.input_ln, nullptr);
+        } else {
+            launch_rmsnorm(c->dx, Ld.input_ln, c->dxn, B, H, m.eps, c->stream);
+            c->step_launches += 1;
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, c->qkv_rows, H, c->dxn, B, c->dqkv, kEpiNone,
+                   nullptr, nullptr, nullptr);
+        }
+        QkvArgs qa{};
+        qa.qkv = c->dqkv; qa.T = B; qa.n_q = m.n_q; qa.n_kv = m.n_kv; qa.d = m.head_dim;
+        qa.q_norm = Ld.q_norm; qa.k_norm = Ld.k_norm; qa.eps = m.eps;
+        qa.rope = c->rope; qa.rope_max_pos = m.max_seq_len;
+        qa.row_pos = c->dpos; qa.row_seq = c->dseq;
+        qa.kv_layer = c->kv + l * c->kv_layer_elems; qa.block_table = c->table_dev;
+        qa.max_blocks = c->max_blocks; qa.n_pool_blocks = c->n_blocks;
+        qa.q_out = c->dq; qa.q_heads_major = 0; qa.err = c->derr;
+        tbegin(c, ZYNFER_CU_K_OTHER, &te);
+        launch_qkv_post(qa, c->stream);
+        tend(c, te);
+        c->step_launches += 1;
+        AttnDecodeArgs aa{};
+        aa.q = c->dq; aa.kv_layer = qa.kv_layer; aa.block_table = c->table_dev;
+        aa.max_blocks = c->max_blocks; aa.n_pool_blocks = c->n_blocks;
+        aa.seq_of = c->dseq; aa.positions = c->dpos; aa.B = B; aa.n_q = m.n_q; aa.n_kv = m.n_kv;
+        aa.d = m.head_dim; aa.chunk = chunk; aa.max_splits = max_splits; aa.partial = c->dpart;
+        aa.counters = c->dcnt; aa.out = c->dattn; aa.err = c->derr;
+        tbegin(c, ZYNFER_CU_K_ATTN, &te);
+        launch_attn_decode(aa, c->stream);
+        tend(c, te);
+        c->step_launches += 1;
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, H, c->qd, c->dattn, B, c->dx1, kEpiResid, c->dx,
+               nullptr, nullptr);
+        if (B <= 8) {
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, 2 * I, H, c->dx1, B, c->dh, kEpiSwiGLU, nullptr,
+                   Ld.post_ln, nullptr);
+        } else {
+            launch_rmsnorm(c->dx1, Ld.post_ln, c->dxn, B, H, m.eps, c->stream);
+            c->step_launches += 1;
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, 2 * I, H, c->dxn, B, c->dh, kEpiSwiGLU, nullptr,
+                   nullptr, nullptr);
+        }
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, H, I, c->dh, B, c->dx, kEpiResid, c->dx1, nullptr,
+               nullptr);
+    }
+    if (B <= 8) {
+        linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, m.vocab, H, c->dx, B,
+               want_logits ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
+    } else {
+        launch_rmsnorm(c->dx, c->final_norm, c->dxn, B, H, m.eps, c->stream);
+        c->step_launches += 1;
+        linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, m.vocab, H, c->dxn, B,
+               want_logits ? c->dlogits : nullptr, kEpiArgmax, nullptr, nullptr, c->dkeys);
+    }
+    FinalizeArgs fa{};
+    fa.keys = c->dkeys; fa.ids_out = c->dids; fa.next_tokens = c->dtok; fa.positions = c->dpos;
+    fa.history = c->dhist; fa.step = c->dstep; fa.B = B;
+    launch_finalize(fa, c->stream);
+    c->step_launches += 1;
+}
+
+int ensure_blocks(ZynferCuCtx* c, uint32_t seq, uint32_t upto_len) {
+    std::vector<int>& bl = c->seq_blocks[seq];
+    const size_t need = (upto_len + kKvBlock - 1) / kKvBlock;
+    if (need > (size_t)c->max_blocks) return fail(c, ZYNFER_CU_INVALID, "sequence exceeds max_seq_len");
+    while (bl.size() < need) {
+        if (c->free_blocks.empty()) return fail(c, ZYNFER_CU_OOM, "KV block pool exhausted");
+        const int b = c->free_blocks.back();
+        c->free_blocks.pop_back();
+        c->table_host[(size_t)seq * c->max_blocks + bl.size()] = b;
+        bl.push_back(b);
+        c->table_dirty[seq] = 1;
+    }
+    return ZYNFER_CU_OK;
+}
+
+void release_seq(ZynferCuCtx* c, uint32_t seq) {
+    for (int b : c->seq_blocks[seq]) c->free_blocks.push_back(b);
+    c->seq_blocks[seq].clear();
+    c->seq_len[seq] = 0;
+    std::fill(c->table_host + (size_t)seq * c->max_blocks, c->table_host + (size_t)(seq + 1) * c->max_blocks, -1);
+    c->table_dirty[seq] = 1;
+}
+
+// Upload the block-table rows of `seqs` that changed since their last upload.
+int upload_table_rows(ZynferCuCtx* c, const uint32_t* seqs, uint32_t n) {
+    for (uint32_t i = 0; i < n; ++i) {
+        if (!c->table_dirty[seqs[i]]) continue;
+        c->table_dirty[seqs[i]] = 0;
+        const size_t off = (size_t)seqs[i] * c->max_blocks;
+        c->h2d_bytes += (size_t)c->max_blocks * 4;
+        ZC_CHECK(c, cudaMemcpyAsync(c->table_dev + off, c->table_host + off, (size_t)c->max_blocks * 4,
+                                    cudaMemcpyHostToDevice, c->stream),
+                 "block table upload");
+    }
+    return ZYNFER_CU_OK;
+}
+
+int validate_batch(ZynferCuCtx* c, const uint32_t* seqs, uint32_t batch, uint32_t extra) {
+    if (!c->ready) return fail(c, ZYNFER_CU_INVALID, "model not initialised");
+    if (batch == 0 || batch > c->d.max_batch) return fail(c, ZYNFER_CU_INVALID, "batch must be 1..max_batch");
+    for (uint32_t i = 0; i < batch; ++i) {
+        if (seqs[i] >= c->d.max_seqs) return fail(c, ZYNFER_CU_INVALID, "sequence id out of range");
+        for (uint32_t j = 0; j < i; ++j)
+            if (seqs[j] == seqs[i]) return fail(c, ZYNFER_CU_INVALID, "a sequence appears twice in one batch");
+        if (c->seq_len[seqs[i]] + extra > c->d.max_seq_len)
+            return fail(c, ZYNFER_CU_INVALID, "KV cache full: step would exceed max_seq_len");
+    }
+    return ZYNFER_CU_OK;
+}
+
+int stage_batch(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* tokens, uint32_t B) {
+    for (uint32_t i = 0; i < B; ++i) {
+        if (tokens[i] >= c->d.vocab) return fail(c, ZYNFER_CU_INVALID, "token id >= vocab");
+        c->hio[i] = tokens[i];
+        c->hio[B + i] = seqs[i];
+        c->hio[2 * B + i] = c->seq_len[seqs[i]];
+    }
+    ZC_CHECK(c, cudaMemcpyAsync(c->dio, c->hio, (size_t)3 * B * 4, cudaMemcpyHostToDevice, c->stream), "stage batch");
+    c->h2d_bytes += (size_t)3 * B * 4;
+    return ZYNFER_CU_OK;
+}
+
+void set_io_views(ZynferCuCtx* c, int B) {
+    c->dtok = c->dio;
+    c->dseq = reinterpret_cast<int*>(c->dio + B);
+    c->dpos = reinterpret_cast<int*>(c->dio + 2 * B);
+}
+
+int get_graph(ZynferCuCtx* c, int B, cudaGraphExec_t* out) {
+    auto it = c->graphs.find(B);
+    if (it != c->graphs.end()) {
+        *out = it->second;
+        return ZYNFER_CU_OK;
+    }
+    cudaGraph_t g = nullptr;
+    ZC_CHECK(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed), "begin capture");
+    enqueue_decode(c, B, false);
+    cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (e != cudaSuccess) return cuda_fail(c, e, "end capture");
+    cudaGraphExec_t ge = nullptr;
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(c, e, "graph instantiate");
+    c->graphs[B] = ge;
+    *out = ge;
+    return ZYNFER_CU_OK;
+}
+
+// Prefill scratch-based forward of `t` tokens of `seq` at pos0 = 0 through
+// layers [l0, l1). Input rows in px; output rows in px.
+void enqueue_prefill_layers(ZynferCuCtx* c, uint32_t seq, int T, uint32_t l0, uint32_t l1) {
+    const ZynferCuModelDesc& m = c->d;
+    const int H = m.hidden, I = m.inter;
+    for (uint32_t l = l0; l < l1; ++l) {
+        const LayerDev& Ld = c->L[l];
+        launch_rmsnorm(c->px, Ld.input_ln, c->pxn, T, H, m.eps, c->stream);
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, c->qkv_rows, H, c->pxn, T, c->pqkv, kEpiNone,
+               nullptr, nullptr, nullptr);
+        QkvArgs qa{};
+        qa.qkv = c->pqkv; qa.T = T; qa.n_q = m.n_q; qa.n_kv = m.n_kv; qa.d = m.head_dim;
+        qa.q_norm = Ld.q_norm; qa.k_norm = Ld.k_norm; qa.eps = m.eps;
+        qa.rope = c->rope; qa.rope_max_pos = m.max_seq_len;
+        qa.row_pos = nullptr; qa.pos0 = 0; qa.row_seq = nullptr; qa.seq0 = (int)seq;
+        qa.kv_layer = c->kv + l * c->kv_layer_elems; qa.block_table = c->table_dev;
+        qa.max_blocks = c->max_blocks; qa.n_pool_blocks = c->n_blocks;
+        qa.q_out = c->pq; qa.q_heads_major = 1; qa.k_stage = c->pk; qa.v_stage = c->pv;
+        qa.stage_round_bf16 = m.prefill_kv_f32 ? 0 : 1; qa.err = c->derr;
+        launch_qkv_post(qa, c->stream);
+        AttnPrefillArgs pa{};
+        pa.q = c->pq; pa.k = c->pk; pa.v = c->pv; pa.T = T; pa.n_q = m.n_q; pa.n_kv = m.n_kv;
+        pa.d = m.head_dim; pa.out = c->pattn;
+        launch_attn_prefill(pa, c->stream);
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, H, c->qd, c->pattn, T, c->px1, kEpiResid, c->px,
+               nullptr, nullptr);
+        launch_rmsnorm(c->px1, Ld.post_ln, c->pxn, T, H, m.eps, c->stream);
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, 2 * I, H, c->pxn, T, c->ph, kEpiSwiGLU, nullptr,
+               nullptr, nullptr);
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, H, I, c->ph, T, c->px, kEpiResid, c->px1, nullptr,
+               nullptr);
+    }
+}
+
+}  // namespace
+
+// =================================================================== ABI
+
+extern "C" {
+
+const char* zynfer_cu_build_info(void) {
+    return "zynfer_cuda sm_100a (int8/bf16 weight-only Qwen3 decode + prefill, paged bf16 KV)";
+}
+
+int zynfer_cu_create(int device, ZynferCuCtx** out) {
+    if (!out) return ZYNFER_CU_INVALID;
+    *out = nullptr;
+    ZynferCuCtx* c = new ZynferCuCtx();
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        c->err = std::string("no CUDA device: ") + (e != cudaSuccess ? cudaGetErrorString(e) : "count is 0");
+        *out = c;  // handle kept so the caller can read last_error; destroy it
+        return ZYNFER_CU_NO_DEVICE;
+    }
+    if (device < 0 || device >= n) {
+        c->err = "device index out of range";
+        *out = c;
+        return ZYNFER_CU_NO_DEVICE;
+    }
+    c->device = device;
+    cudaSetDevice(device);
+    cudaDeviceProp p{};
+    cudaGetDeviceProperties(&p, device);
+    snprintf(c->caps.device_name, sizeof(c->caps.device_name), "%s", p.name);
+    c->caps.sm_major = p.major;
+    c->caps.sm_minor = p.minor;
+    c->caps.sm_count = p.multiProcessorCount;
+    c->caps.hbm_bytes = p.totalGlobalMem;
+    c->caps.l2_bytes = (uint64_t)p.l2CacheSize;
+    c->caps.max_smem_per_block = (uint32_t)p.sharedMemPerBlockOptin;
+    c->caps.bulk_copy = p.major >= 9;
+    c->caps.tcgen05 = p.major == 10 && p.minor == 0;
+    if (p.major != 10) {
+        c->err = std::string("device ") + p.name + " is not sm_100 (this library is built for sm_100a only)";
+        *out = c;
+        return ZYNFER_CU_UNSUPPORTED;
+    }
+    e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        c->err = cudaGetErrorString(e);
+        *out = c;
+        return ZYNFER_CU_LAUNCH;
+    }
+    cudaEventCreate(&c->ev0);
+    cudaEventCreate(&c->ev1);
+    parse_fail_spec(c, getenv("ZYNFER_CUDA_FAIL_AT"));
+    *out = c;
+    return ZYNFER_CU_OK;
+}
+
+void zynfer_cu_destroy(ZynferCuCtx* c) {
+    if (!c) return;
+    if (c->device >= 0) {
+        cudaSetDevice(c->device);
+        if (c->stream) cudaStreamSynchronize(c->stream);
+        for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+        for (auto& t : c->tev) {
+            cudaEventDestroy(t.a);
+            cudaEventDestroy(t.b);
+        }
+        if (c->ev0) cudaEventDestroy(c->ev0);
+        if (c->ev1) cudaEventDestroy(c->ev1);
+        for (void* p : c->allocs) cudaFree(p);
+        for (void* p : c->pinned) cudaFreeHost(p);
+        if (c->stream) cudaStreamDestroy(c->stream);
+    }
+    delete c;
+}
+
+int zynfer_cu_caps(const ZynferCuCtx* c, ZynferCuCaps* out) {
+    if (!c || !out) return ZYNFER_CU_INVALID;
+    *out = c->caps;
+    return c->device >= 0 ? ZYNFER_CU_OK : ZYNFER_CU_NO_DEVICE;
+}
+
+const char* zynfer_cu_last_error(const ZynferCuCtx* c) { return c ? c->err.c_str() : "null context"; }
+
+const char* zynfer_cu_last_path(const ZynferCuCtx* c) { return c ? c->path.c_str() : "null context"; }
+
+int zynfer_cu_set_fail_at(ZynferCuCtx* c, const char* spec) {
+    if (!c) return ZYNFER_CU_INVALID;
+    parse_fail_spec(c, spec);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_sync(ZynferCuCtx* c) {
+    if (!c || c->device < 0) return ZYNFER_CU_INVALID;
+    cudaSetDevice(c->device);
+    ZC_CHECK(c, cudaStreamSynchronize(c->stream), "stream synchronize");
+    if (c->derr) return check_device_error(c);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
+    if (!c || !desc || c->device < 0) return ZYNFER_CU_INVALID;
+    if (c->ready) return fail(c, ZYNFER_CU_INVALID, "model already initialised");
+    cudaSetDevice(c->device);
+    const ZynferCuModelDesc& m = *desc;
+    if (m.head_dim != 128 || m.n_kv == 0 || m.n_q != 2 * m.n_kv)
+        return fail(c, ZYNFER_CU_UNSUPPORTED, "kernels are built for head_dim 128 and 2 query heads per kv head");
+    if (m.hidden % 512 || m.inter % 512 || (m.n_q * m.head_dim) % 512)
+        return fail(c, ZYNFER_CU_UNSUPPORTED, "hidden, intermediate and q dims must be multiples of 512");
+    if (m.weights != ZYNFER_CU_W_Q8 && m.weights != ZYNFER_CU_W_BF16)
+        return fail(c, ZYNFER_CU_INVALID, "unknown weight kind");
+    if (m.max_batch == 0 || m.max_batch > 1024 || m.max_seqs == 0 || m.max_seq_len == 0 ||
+        m.max_seq_len > m.max_pos || m.layers == 0 || m.vocab == 0)
+        return fail(c, ZYNFER_CU_INVALID, "invalid sizes in model descriptor");
+    c->d = m;
+    if (c->d.max_prefill == 0) c->d.max_prefill = std::min<uint32_t>(m.max_seq_len, 4096);
+    c->wkind = m.weights == ZYNFER_CU_W_Q8 ? kWQ8 : kWBF16;
+    c->esz = c->wkind == kWQ8 ? 1 : 2;
+    const size_t H = m.hidden, I = m.inter, V = m.vocab, hd = m.head_dim;
+    c->qd = m.n_q * hd;
+    c->kvd = m.n_kv * hd;
+    c->qkv_rows = c->qd + 2 * c->kvd;
+    const bool q8 = c->wkind == kWQ8;
+    int rc;
+#define ALLOC(p, n) do { if ((rc = dalloc(c, &(p), (n))) != ZYNFER_CU_OK) return rc; } while (0)
+    c->L.resize(m.layers);
+    for (auto& Ld : c->L) {
+        char* w;
+        ALLOC(w, (size_t)c->qkv_rows * H * c->esz); Ld.wqkv = w;
+        ALLOC(w, H * (size_t)c->qd * c->esz); Ld.wo = w;
+        ALLOC(w, 2 * I * H * c->esz); Ld.wgu = w;
+        ALLOC(w, H * I * c->esz); Ld.wd = w;
+        if (q8) {
+            ALLOC(Ld.sqkv, (size_t)c->qkv_rows);
+            ALLOC(Ld.so, H);
+            ALLOC(Ld.sgu, 2 * I);
+            ALLOC(Ld.sd, H);
+        }
+        ALLOC(Ld.input_ln, H);
+        ALLOC(Ld.post_ln, H);
+        ALLOC(Ld.q_norm, hd);
+        ALLOC(Ld.k_norm, hd);
+    }
+    {
+        char* w;
+        ALLOC(w, V * H * c->esz);
+        c->embed = w;
+    }
+    if (q8) ALLOC(c->sembed, V);
+    ALLOC(c->final_norm, H);
+    // RoPE table: the reference's f32 formula (ops.zig:250-253) evaluated once
+    // on the host: freq = 1 / theta^(i/half), angle = pos * freq.
+    {
+        const int half = (int)hd / 2;
+        std::vector<float2> tab((size_t)m.max_seq_len * half);
+        for (int i = 0; i < half; ++i) {
+            const float freq = 1.0f / powf(m.theta, (float)i / (float)half);
+            for (uint32_t pos = 0; pos < m.max_seq_len; ++pos) {
+                const float angle = (float)pos * freq;
+                tab[(size_t)pos * half + i] = make_float2(cosf(angle), sinf(angle));
+            }
+        }
+        ALLOC(c->rope, tab.size());
+        ZC_CHECK(c, cudaMemcpy(c->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice), "rope table");
+    }
+    // paged KV pool
+    c->max_blocks = (int)((m.max_seq_len + kKvBlock - 1) / kKvBlock);
+    c->n_blocks = m.kv_blocks ? (int)m.kv_blocks : (int)(m.max_seqs * c->max_blocks);
+    c->kv_layer_elems = (size_t)c->n_blocks * 2 * m.n_kv * kKvBlock * hd;
+    ALLOC(c->kv, c->kv_layer_elems * m.layers);
+    c->free_blocks.clear();
+    for (int b = c->n_blocks - 1; b >= 0; --b) c->free_blocks.push_back(b);
+    c->seq_blocks.assign(m.max_seqs, {});
+    c->seq_len.assign(m.max_seqs, 0);
+    c->table_dirty.assign(m.max_seqs, 0);
+    if ((rc = halloc(c, &c->table_host, (size_t)m.max_seqs * c->max_blocks)) != ZYNFER_CU_OK) return rc;
+    std::fill(c->table_host, c->table_host + (size_t)m.max_seqs * c->max_blocks, -1);
+    ALLOC(c->table_dev, (size_t)m.max_seqs * c->max_blocks);
+    ZC_CHECK(c, cudaMemcpy(c->table_dev, c->table_host, (size_t)m.max_seqs * c->max_blocks * 4, cudaMemcpyHostToDevice), "table");
+    // decode scratch
+    const size_t B = m.max_batch;
+    ALLOC(c->dx, B * H);
+    ALLOC(c->dx1, B * H);
+    ALLOC(c->dxn, B * H);
+    ALLOC(c->dqkv, B * c->qkv_rows);
+    ALLOC(c->dq, B * c->qd);
+    ALLOC(c->dattn, B * c->qd);
+    ALLOC(c->dh, B * I);
+    ALLOC(c->dlogits, B * V);
+    ALLOC(c->dio, 3 * B);
+    ALLOC(c->dkeys, B);
+    ALLOC(c->dids, B);
+    ALLOC(c->dcnt, B * m.n_kv);
+    const size_t max_splits = (m.max_seq_len + 63) / 64;
+    ALLOC(c->dpart, B * m.n_kv * max_splits * 2 * (hd + 2));
+    c->hist_cap = std::max<size_t>(B * 4096, 1 << 16);
+    ALLOC(c->dhist, c->hist_cap);
+    ALLOC(c->dstep, 1);
+    // prefill scratch
+    const size_t P = c->d.max_prefill;
+    ALLOC(c->px, P * H);
+    ALLOC(c->px1, P * H);
+    ALLOC(c->pxn, P * H);
+    ALLOC(c->pqkv, P * c->qkv_rows);
+    ALLOC(c->pq, P * c->qd);
+    ALLOC(c->pk, P * c->kvd);
+    ALLOC(c->pv, P * c->kvd);
+    ALLOC(c->pattn, P * c->qd);
+    ALLOC(c->ph, P * I);
+    ALLOC(c->ptok, P);
+    ALLOC(c->derr, 1);
+#undef ALLOC
+    if ((rc = halloc(c, &c->herr, 1)) != ZYNFER_CU_OK) return rc;
+    if ((rc = halloc(c, &c->hio, 3 * B)) != ZYNFER_CU_OK) return rc;
+    if ((rc = halloc(c, &c->hids, B)) != ZYNFER_CU_OK) return rc;
+    cudaMemset(c->dkeys, 0, B * 8);
+    cudaMemset(c->dcnt, 0, B * m.n_kv * 4);
+    cudaMemset(c->derr, 0, 4);
+    cudaMemset(c->dstep, 0, 4);
+    ZC_CHECK(c, cudaDeviceSynchronize(), "model init");
+    c->ready = true;
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_upload_f32(ZynferCuCtx* c, const char* name, const float* data, uint64_t rows, uint64_t cols) {
+    if (!c || !c->ready || !name || !data) return c ? fail(c, ZYNFER_CU_INVALID, "bad upload arguments") : ZYNFER_CU_INVALID;
+    if (c->fail_upload) {
+        c->fail_upload = false;
+        return fail(c, ZYNFER_CU_INTERNAL, "injected upload failure (ZYNFER_CUDA_FAIL_AT=upload)");
+    }
+    cudaSetDevice(c->device);
+    Dest d = find_dest(c, name);
+    if (d.kind == Dest::None) return fail(c, ZYNFER_CU_INVALID, std::string("unknown tensor ") + name);
+    if ((uint64_t)d.rows * d.cols != rows * cols || (d.kind == Dest::Mat && (rows != (uint64_t)d.rows)))
+        return fail(c, ZYNFER_CU_INVALID, std::string("shape mismatch for ") + name);
+    float* tmp = nullptr;
+    ZC_CHECK(c, cudaMalloc(&tmp, rows * cols * 4), "upload staging");
+    cudaError_t e = cudaMemcpyAsync(tmp, data, rows * cols * 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) {
+        place_f32(c, d, tmp);
+        e = cudaStreamSynchronize(c->stream);
+    }
+    cudaFree(tmp);
+    if (e != cudaSuccess) return cuda_fail(c, e, "upload");
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_upload_bf16(ZynferCuCtx* c, const char* name, const uint16_t* data, uint64_t rows, uint64_t cols) {
+    if (!c || !c->ready || !name || !data) return c ? fail(c, ZYNFER_CU_INVALID, "bad upload arguments") : ZYNFER_CU_INVALID;
+    if (c->fail_upload) {
+        c->fail_upload = false;
+        return fail(c, ZYNFER_CU_INTERNAL, "injected upload failure (ZYNFER_CUDA_FAIL_AT=upload)");
+    }
+    cudaSetDevice(c->device);
+    Dest d = find_dest(c, name);
+    if (d.kind == Dest::None) return fail(c, ZYNFER_CU_INVALID, std::string("unknown tensor ") + name);
+    if ((uint64_t)d.rows * d.cols != rows * cols) return fail(c, ZYNFER_CU_INVALID, std::string("shape mismatch for ") + name);
+    uint16_t* tmp = nullptr;
+    float* tmpf = nullptr;
+    ZC_CHECK(c, cudaMalloc(&tmp, rows * cols * 2), "upload staging");
+    cudaError_t e = cudaMalloc(&tmpf, rows * cols * 4);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, data, rows * cols * 2, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) {
+        if (d.kind == Dest::Mat && c->wkind == kWBF16) {
+            launch_copy_rows_u16(tmp, d.rows, d.cols, reinterpret_cast<uint16_t*>(d.w), d.stride, d.offset, c->stream);
+        } else {
+            launch_bf16_to_f32(tmp, rows * cols, tmpf, c->stream);
+            place_f32(c, d, tmpf);
+        }
+        e = cudaStreamSynchronize(c->stream);
+    }
+    cudaFree(tmp);
+    if (tmpf) cudaFree(tmpf);
+    if (e != cudaSuccess) return cuda_fail(c, e, "upload");
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_upload_q8(ZynferCuCtx* c, const char* name, const int8_t* q, const float* scale, uint64_t rows,
+                        uint64_t cols) {
+    if (!c || !c->ready || !name || !q || !scale) return c ? fail(c, ZYNFER_CU_INVALID, "bad upload arguments") : ZYNFER_CU_INVALID;
+    if (c->fail_upload) {
+        c->fail_upload = false;
+        return fail(c, ZYNFER_CU_INTERNAL, "injected upload failure (ZYNFER_CUDA_FAIL_AT=upload)");
+    }
+    if (c->wkind != kWQ8) return fail(c, ZYNFER_CU_UNSUPPORTED, "int8 upload into a bf16 model");
+    cudaSetDevice(c->device);
+    Dest d = find_dest(c, name);
+    if (d.kind != Dest::Mat) return fail(c, ZYNFER_CU_INVALID, std::string("not an int8 matrix: ") + name);
+    if (rows != (uint64_t)d.rows || cols != (uint64_t)d.cols) return fail(c, ZYNFER_CU_INVALID, std::string("shape mismatch for ") + name);
+    int8_t* tq = nullptr;
+    float* ts = nullptr;
+    ZC_CHECK(c, cudaMalloc(&tq, rows * cols), "upload staging");
+    cudaError_t e = cudaMalloc(&ts, rows * 4);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tq, q, rows * cols, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(ts, scale, rows * 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) {
+        launch_copy_rows_i8(tq, ts, d.rows, d.cols, reinterpret_cast<int8_t*>(d.w), d.s, d.stride, d.offset, c->stream);
+        e = cudaStreamSynchronize(c->stream);
+    }
+    cudaFree(tq);
+    if (ts) cudaFree(ts);
+    if (e != cudaSuccess) return cuda_fail(c, e, "upload");
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_fill_synthetic(ZynferCuCtx* c, uint64_t seed, float w_std, float norm_std) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    const ZynferCuModelDesc& m = c->d;
+    const size_t maxn = std::max<size_t>((size_t)m.vocab * m.hidden, (size_t)2 * m.inter * m.hidden);
+    float* tmp = nullptr;
+    ZC_CHECK(c, cudaMalloc(&tmp, maxn * 4), "synthetic staging");
+    const float kw = (float)((double)w_std / ZS_IH4_SIGMA);
+    const float kn = (float)((double)norm_std / ZS_IH4_SIGMA);
+    auto gen = [&](const char* name, uint64_t stream, bool is_norm) {
+        Dest d = find_dest(c, name);
+        const size_t n = (size_t)d.rows * d.cols;
+        if (is_norm) {
+            if (norm_std == 0.0f) launch_fill(tmp, n, 1.0f, c->stream);
+            else launch_synth_normal(tmp, n, seed, stream, kn, 1.0f, c->stream);
+        } else {
+            launch_synth_normal(tmp, n, seed, stream, kw, 0.0f, c->stream);
+        }
+        if (c->wkind == kWBF16 && is_norm) {
+            // a bf16 checkpoint stores norm weights in bf16 too (widened on load)
+            uint16_t* t16 = reinterpret_cast<uint16_t*>(tmp + n);
+            launch_to_bf16_rows(tmp, (int)n, 1, t16, 1, 0, c->stream);
+            launch_bf16_to_f32(t16, n, tmp, c->stream);
+        }
+        place_f32(c, d, tmp);
+    };
+    gen("model.embed_tokens.weight", ZS_EMBED, false);
+    gen("model.norm.weight", ZS_FINAL_NORM, true);
+    static const char* names[11] = {"input_layernorm.weight", "self_attn.q_norm.weight", "self_attn.k_norm.weight",
+                                    "self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                                    "self_attn.o_proj.weight", "post_attention_layernorm.weight",
+                                    "mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight"};
+    static const int codes[11] = {ZS_INPUT_LN, ZS_Q_NORM, ZS_K_NORM, ZS_WQ, ZS_WK, ZS_WV, ZS_WO, ZS_POST_LN, ZS_WG, ZS_WU, ZS_WD};
+    static const bool norm[11] = {true, true, true, false, false, false, false, true, false, false, false};
+    char nm[160];
+    for (uint32_t l = 0; l < m.layers; ++l)
+        for (int t = 0; t < 11; ++t) {
+            snprintf(nm, sizeof(nm), "model.layers.%u.%s", l, names[t]);
+            gen(nm, zs_layer_stream(l, (uint32_t)codes[t]), norm[t]);
+        }
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return cuda_fail(c, e, "synthetic fill");
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "synthetic fill launch");
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_download_q8(ZynferCuCtx* c, const char* name, int8_t* q, float* scale, uint64_t rows, uint64_t cols) {
+    if (!c || !c->ready || !name || !q || !scale) return c ? fail(c, ZYNFER_CU_INVALID, "bad download arguments") : ZYNFER_CU_INVALID;
+    if (c->wkind != kWQ8) return fail(c, ZYNFER_CU_UNSUPPORTED, "not an int8 model");
+    cudaSetDevice(c->device);
+    Dest d = find_dest(c, name);
+    if (d.kind != Dest::Mat || rows != (uint64_t)d.rows || cols != (uint64_t)d.cols)
+        return fail(c, ZYNFER_CU_INVALID, std::string("bad tensor or shape: ") + name);
+    int8_t* tq = nullptr;
+    float* ts = nullptr;
+    ZC_CHECK(c, cudaMalloc(&tq, rows * cols), "download staging");
+    cudaError_t e = cudaMalloc(&ts, rows * 4);
+    if (e == cudaSuccess) {
+        launch_unpack_rows_i8(reinterpret_cast<const int8_t*>(d.w), d.s, d.rows, d.cols, tq, ts, d.stride, d.offset, c->stream);
+        e = cudaMemcpyAsync(q, tq, rows * cols, cudaMemcpyDeviceToHost, c->stream);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(scale, ts, rows * 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(tq);
+    if (ts) cudaFree(ts);
+    if (e != cudaSuccess) return cuda_fail(c, e, "download");
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_seq_reset(ZynferCuCtx* c, uint32_t seq) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    if (seq >= c->d.max_seqs) return fail(c, ZYNFER_CU_INVALID, "sequence id out of range");
+    release_seq(c, seq);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_seq_len(const ZynferCuCtx* c, uint32_t seq, uint32_t* len) {
+    if (!c || !c->ready || !len || seq >= c->d.max_seqs) return ZYNFER_CU_INVALID;
+    *len = c->seq_len[seq];
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_kv_read(ZynferCuCtx* c, uint32_t seq, uint32_t layer, int which_v, float* out) {
+    if (!c || !c->ready || !out) return c ? fail(c, ZYNFER_CU_INVALID, "bad arguments") : ZYNFER_CU_INVALID;
+    if (seq >= c->d.max_seqs || layer >= c->d.layers) return fail(c, ZYNFER_CU_INVALID, "index out of range");
+    cudaSetDevice(c->device);
+    const int d = c->d.head_dim, nkv = c->d.n_kv;
+    const uint32_t len = c->seq_len[seq];
+    std::vector<uint16_t> blk((size_t)kKvBlock * d);
+    for (uint32_t p0 = 0; p0 < len; p0 += kKvBlock) {
+        const int b = c->seq_blocks[seq][p0 / kKvBlock];
+        for (int h = 0; h < nkv; ++h) {
+            const uint16_t* src = c->kv + layer * c->kv_layer_elems + (((size_t)b * 2 + (which_v ? 1 : 0)) * nkv + h) * kKvBlock * d;
+            ZC_CHECK(c, cudaMemcpy(blk.data(), src, blk.size() * 2, cudaMemcpyDeviceToHost), "kv read");
+            for (uint32_t i = 0; i < (uint32_t)kKvBlock && p0 + i < len; ++i)
+                for (int e = 0; e < d; ++e) {
+                    const uint32_t u = (uint32_t)blk[(size_t)i * d + e] << 16;
+                    float f;
+                    memcpy(&f, &u, 4);
+                    out[((size_t)h * len + p0 + i) * d + e] = f;
+                }
+        }
+    }
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_prefill(ZynferCuCtx* c, uint32_t seq, const uint32_t* tokens, uint32_t n, float* last_logits,
+                      uint32_t* argmax) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    if (seq >= c->d.max_seqs) return fail(c, ZYNFER_CU_INVALID, "sequence id out of range");
+    if (n == 0 || !tokens) return fail(c, ZYNFER_CU_INVALID, "empty prompt");  // qwen_forward.zig:101
+    if (n > c->d.max_prefill || n > c->d.max_seq_len) return fail(c, ZYNFER_CU_INVALID, "prompt longer than max_prefill / max_seq_len");
+    for (uint32_t i = 0; i < n; ++i)
+        if (tokens[i] >= c->d.vocab) return fail(c, ZYNFER_CU_INVALID, "token id >= vocab");  // ops.zig:406
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    release_seq(c, seq);  // qwen_forward.zig:110 (reset)
+    int rc = ensure_blocks(c, seq, n);
+    if (rc) return rc;
+    if ((rc = upload_table_rows(c, &seq, 1))) return rc;
+    const ZynferCuModelDesc& m = c->d;
+    ZC_CHECK(c, cudaMemcpyAsync(c->ptok, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream), "prompt upload");
+    cudaEventRecord(c->ev0, c->stream);
+    launch_embed(c->embed, c->sembed, c->wkind, c->ptok, n, m.hidden, m.vocab, c->px, c->derr, c->stream);
+    enqueue_prefill_layers(c, seq, (int)n, 0, m.layers);
+    linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, m.vocab, m.hidden, c->px + (size_t)(n - 1) * m.hidden, 1,
+           last_logits ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
+    FinalizeArgs fa{};
+    fa.keys = c->dkeys; fa.ids_out = c->dids; fa.B = 1;
+    launch_finalize(fa, c->stream);
+    cudaEventRecord(c->ev1, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "prefill launch");
+    if (last_logits) ZC_CHECK(c, cudaMemcpyAsync(last_logits, c->dlogits, (size_t)m.vocab * 4, cudaMemcpyDeviceToHost, c->stream), "logits");
+    ZC_CHECK(c, cudaMemcpyAsync(c->hids, c->dids, 4, cudaMemcpyDeviceToHost, c->stream), "argmax");
+    if ((rc = check_device_error(c))) return rc;
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    c->last_step_ns = (uint64_t)(ms * 1e6);
+    if (argmax) *argmax = c->hids[0];
+    c->seq_len[seq] = n;
+    c->path = "prefill:simt";
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_decode_step(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* tokens, uint32_t batch,
+                          uint32_t* argmax, float* logits) {
+    if (!c) return ZYNFER_CU_INVALID;
+    if (!seqs || !tokens || !argmax) return fail(c, ZYNFER_CU_INVALID, "null argument");
+    int rc = validate_batch(c, seqs, batch, 1);
+    if (rc) return rc;
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    for (uint32_t i = 0; i < batch; ++i)
+        if ((rc = ensure_blocks(c, seqs[i], c->seq_len[seqs[i]] + 1))) return rc;
+    if ((rc = upload_table_rows(c, seqs, batch))) return rc;
+    set_io_views(c, (int)batch);
+    if ((rc = stage_batch(c, seqs, tokens, batch))) return rc;
+    ZC_CHECK(c, cudaMemsetAsync(c->dstep, 0, 4, c->stream), "step counter");
+    const bool eager = logits != nullptr || c->timing;
+    cudaEventRecord(c->ev0, c->stream);
+    if (eager) {
+        enqueue_decode(c, (int)batch, logits != nullptr);
+        c->path = batch <= 8 ? "decode:gemv:eager" : "decode:gemm:eager";
+    } else {
+        cudaGraphExec_t g;
+        if ((rc = get_graph(c, (int)batch, &g))) return rc;
+        ZC_CHECK(c, cudaGraphLaunch(g, c->stream), "graph launch");
+        c->path = batch <= 8 ? "decode:gemv:graph" : "decode:gemm:graph";
+    }
+    cudaEventRecord(c->ev1, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "decode launch");
+    ZC_CHECK(c, cudaMemcpyAsync(c->hids, c->dids, (size_t)batch * 4, cudaMemcpyDeviceToHost, c->stream), "argmax");
+    c->d2h_bytes += (size_t)batch * 4;
+    if (logits) {
+        ZC_CHECK(c, cudaMemcpyAsync(logits, c->dlogits, (size_t)batch * c->d.vocab * 4, cudaMemcpyDeviceToHost, c->stream), "logits");
+        c->d2h_bytes += (size_t)batch * c->d.vocab * 4;
+    }
+    if ((rc = check_device_error(c))) return rc;
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    c->last_step_ns = (uint64_t)(ms * 1e6);
+    for (uint32_t i = 0; i < batch; ++i) {
+        argmax[i] = c->hids[i];
+        c->seq_len[seqs[i]] += 1;
+    }
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_generate(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* first, uint32_t batch, uint32_t steps,
+                       uint32_t* out_ids, float* device_ms) {
+    if (!c) return ZYNFER_CU_INVALID;
+    if (!seqs || !first || !out_ids) return fail(c, ZYNFER_CU_INVALID, "null argument");
+    if (steps == 0) return ZYNFER_CU_OK;
+    int rc = validate_batch(c, seqs, batch, steps);
+    if (rc) return rc;
+    if ((size_t)steps * batch > c->hist_cap) return fail(c, ZYNFER_CU_INVALID, "steps * batch exceeds the on-device history");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    for (uint32_t i = 0; i < batch; ++i)
+        if ((rc = ensure_blocks(c, seqs[i], c->seq_len[seqs[i]] + steps))) return rc;
+    if ((rc = upload_table_rows(c, seqs, batch))) return rc;
+    set_io_views(c, (int)batch);
+    if ((rc = stage_batch(c, seqs, first, batch))) return rc;
+    ZC_CHECK(c, cudaMemsetAsync(c->dstep, 0, 4, c->stream), "step counter");
+    cudaGraphExec_t g = nullptr;
+    if (!c->timing && (rc = get_graph(c, (int)batch, &g))) return rc;
+    cudaEventRecord(c->ev0, c->stream);
+    for (uint32_t s = 0; s < steps; ++s) {
+        if (c->timing) enqueue_decode(c, (int)batch, false);
+        else ZC_CHECK(c, cudaGraphLaunch(g, c->stream), "graph launch");
+    }
+    cudaEventRecord(c->ev1, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "generate launch");
+    if ((rc = check_device_error(c))) return rc;
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    if (device_ms) *device_ms = ms;
+    c->last_step_ns = (uint64_t)(ms * 1e6 / steps);
+    ZC_CHECK(c, cudaMemcpy(out_ids, c->dhist, (size_t)steps * batch * 4, cudaMemcpyDeviceToHost), "history");
+    for (uint32_t i = 0; i < batch; ++i) c->seq_len[seqs[i]] += steps;
+    c->path = std::string(batch <= 8 ? "generate:gemv" : "generate:gemm") + (c->timing ? ":eager" : ":graph");
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_block_forward(ZynferCuCtx* c, uint32_t layer, uint32_t seq, const float* x, uint32_t t, float* out) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    if (!x || !out || t == 0) return fail(c, ZYNFER_CU_INVALID, "bad arguments");
+    if (layer >= c->d.layers || seq >= c->d.max_seqs) return fail(c, ZYNFER_CU_INVALID, "index out of range");
+    const uint32_t pos0 = c->seq_len[seq];
+    if (pos0 + t > c->d.max_seq_len) return fail(c, ZYNFER_CU_INVALID, "KV cache full");  // qwen_block.zig:176
+    if (pos0 == 0 && t > c->d.max_prefill) return fail(c, ZYNFER_CU_INVALID, "t > max_prefill");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    int rc = ensure_blocks(c, seq, pos0 + t);
+    if (rc) return rc;
+    if ((rc = upload_table_rows(c, &seq, 1))) return rc;
+    const ZynferCuModelDesc& m = c->d;
+    const int H = m.hidden;
+    if (pos0 == 0) {
+        ZC_CHECK(c, cudaMemcpyAsync(c->px, x, (size_t)t * H * 4, cudaMemcpyHostToDevice, c->stream), "x upload");
+        enqueue_prefill_layers(c, seq, (int)t, layer, layer + 1);
+        ZC_CHECK(c, cudaMemcpyAsync(out, c->px, (size_t)t * H * 4, cudaMemcpyDeviceToHost, c->stream), "out");
+    } else {
+        // tokens after a cached prefix go one at a time through the decode path
+        // (prefill == stepwise decode, tiny_block.zig:352-383)
+        const LayerDev& Ld = c->L[layer];
+        set_io_views(c, 1);
+        for (uint32_t i = 0; i < t; ++i) {
+            c->hio[0] = 0;
+            c->hio[1] = seq;
+            c->hio[2] = pos0 + i;
+            ZC_CHECK(c, cudaMemcpyAsync(c->dio, c->hio, 12, cudaMemcpyHostToDevice, c->stream), "stage");
+            ZC_CHECK(c, cudaMemcpyAsync(c->dx, x + (size_t)i * H, (size_t)H * 4, cudaMemcpyHostToDevice, c->stream), "x");
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, c->qkv_rows, H, c->dx, 1, c->dqkv, kEpiNone, nullptr, Ld.input_ln, nullptr);
+            QkvArgs qa{};
+            qa.qkv = c->dqkv; qa.T = 1; qa.n_q = m.n_q; qa.n_kv = m.n_kv; qa.d = m.head_dim;
+            qa.q_norm = Ld.q_norm; qa.k_norm = Ld.k_norm; qa.eps = m.eps; qa.rope = c->rope;
+            qa.rope_max_pos = m.max_seq_len; qa.row_pos = c->dpos; qa.row_seq = c->dseq;
+            qa.kv_layer = c->kv + layer * c->kv_layer_elems; qa.block_table = c->table_dev;
+            qa.max_blocks = c->max_blocks; qa.n_pool_blocks = c->n_blocks; qa.q_out = c->dq; qa.err = c->derr;
+            launch_qkv_post(qa, c->stream);
+            AttnDecodeArgs aa{};
+            aa.q = c->dq; aa.kv_layer = qa.kv_layer; aa.block_table = c->table_dev; aa.max_blocks = c->max_blocks;
+            aa.n_pool_blocks = c->n_blocks; aa.seq_of = c->dseq; aa.positions = c->dpos; aa.B = 1;
+            aa.n_q = m.n_q; aa.n_kv = m.n_kv; aa.d = m.head_dim; aa.chunk = decode_chunk(1);
+            aa.max_splits = (int)((m.max_seq_len + aa.chunk - 1) / aa.chunk); aa.partial = c->dpart;
+            aa.counters = c->dcnt; aa.out = c->dattn; aa.err = c->derr;
+            launch_attn_decode(aa, c->stream);
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, H, c->qd, c->dattn, 1, c->dx1, kEpiResid, c->dx, nullptr, nullptr);
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, 2 * m.inter, H, c->dx1, 1, c->dh, kEpiSwiGLU, nullptr, Ld.post_ln, nullptr);
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, H, m.inter, c->dh, 1, c->dx, kEpiResid, c->dx1, nullptr, nullptr);
+            ZC_CHECK(c, cudaMemcpyAsync(out + (size_t)i * H, c->dx, (size_t)H * 4, cudaMemcpyDeviceToHost, c->stream), "out");
+            ZC_CHECK(c, cudaStreamSynchronize(c->stream), "block step");
+        }
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "block launch");
+    if ((rc = check_device_error(c))) return rc;
+    c->seq_len[seq] = pos0 + t;
+    c->path = pos0 == 0 ? "block:prefill" : "block:decode";
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_linear(ZynferCuCtx* c, int wkind, const void* w, const float* scale, const float* x, uint32_t batch,
+                     uint32_t m, uint32_t k, float* y) {
+    if (!c || c->device < 0) return ZYNFER_CU_INVALID;
+    if (!w || !x || !y || batch == 0 || m == 0 || k == 0) return fail(c, ZYNFER_CU_INVALID, "bad linear arguments");
+    if (wkind != ZYNFER_CU_W_Q8 && wkind != ZYNFER_CU_W_BF16) return fail(c, ZYNFER_CU_INVALID, "unknown weight kind");
+    if (wkind == ZYNFER_CU_W_Q8 && !scale) return fail(c, ZYNFER_CU_INVALID, "int8 weights need scales");
+    if (k % 512) return fail(c, ZYNFER_CU_UNSUPPORTED, "k must be a multiple of 512");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    LinearArgs a;
+    a.w = w; a.scale = wkind == ZYNFER_CU_W_Q8 ? scale : nullptr; a.wkind = wkind == ZYNFER_CU_W_Q8 ? kWQ8 : kWBF16;
+    a.M = (int)m; a.K = (int)k; a.x = x; a.ldx = (int)k; a.N = (int)batch; a.y = y; a.ldy = (int)m;
+    a.epi = kEpiNone;
+    TimedEvent* te;
+    tbegin(c, ZYNFER_CU_K_LINEAR, &te);
+    if (batch <= 8) launch_gemv(a, c->stream);
+    else launch_gemm_simt(a, c->stream);
+    tend(c, te);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "linear launch");
+    c->path = batch <= 8 ? "linear:gemv" : "linear:gemm";
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_pack_q8(ZynferCuCtx* c, const float* w, uint32_t rows, uint32_t cols, int8_t* q, float* scale) {
+    if (!c || c->device < 0) return ZYNFER_CU_INVALID;
+    if (!w || !q || !scale || rows == 0 || cols == 0) return fail(c, ZYNFER_CU_INVALID, "bad pack arguments");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    launch_pack_q8_rows(w, (int)rows, (int)cols, q, scale, 1, 0, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "pack launch");
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_rmsnorm(ZynferCuCtx* c, const float* x, const float* w, uint32_t rows, uint32_t cols, float eps, float* y) {
+    if (!c || c->device < 0) return ZYNFER_CU_INVALID;
+    if (!x || !w || !y || rows == 0 || cols % 128) return fail(c, ZYNFER_CU_INVALID, "bad rmsnorm arguments");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    launch_rmsnorm(x, w, y, (int)rows, (int)cols, eps, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "rmsnorm launch");
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_set_timing(ZynferCuCtx* c, int enable) {
+    if (!c || c->device < 0) return ZYNFER_CU_INVALID;
+    cudaSetDevice(c->device);
+    if (enable && c->tev.empty()) {
+        c->tev.resize(8192);
+        for (auto& t : c->tev) {
+            cudaEventCreate(&t.a);
+            cudaEventCreate(&t.b);
+        }
+    }
+    if (enable) {
+        c->tev_used = 0;
+        for (int i = 0; i < 4; ++i) {
+            c->t_launch[i] = 0;
+            c->t_ms[i] = 0.0;
+        }
+    }
+    c->timing = enable != 0;
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_kernel_time(const ZynferCuCtx* cc, int cls, uint64_t* launches, double* total_ms) {
+    ZynferCuCtx* c = const_cast<ZynferCuCtx*>(cc);
+    if (!c || cls < 0 || cls > 3 || !launches || !total_ms) return ZYNFER_CU_INVALID;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    for (size_t i = 0; i < c->tev_used; ++i) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, c->tev[i].a, c->tev[i].b);
+        c->t_ms[c->tev[i].cls] += ms;
+        c->t_launch[c->tev[i].cls] += 1;
+    }
+    c->tev_used = 0;
+    *launches = c->t_launch[cls];
+    *total_ms = c->t_ms[cls];
+    return ZYNFER_CU_OK;
+}
+
+uint64_t zynfer_cu_last_step_ns(const ZynferCuCtx* c) { return c ? c->last_step_ns : 0; }
+
+int zynfer_cu_step_launches(const ZynferCuCtx* c) { return c ? c->step_launches : 0; }
+
+int zynfer_cu_io_bytes(ZynferCuCtx* c, uint64_t* h2d, uint64_t* d2h, int reset) {
+    if (!c || !h2d || !d2h) return ZYNFER_CU_INVALID;
+    *h2d = c->h2d_bytes;
+    *d2h = c->d2h_bytes;
+    if (reset) c->h2d_bytes = c->d2h_bytes = 0;
+    return ZYNFER_CU_OK;
+}
+
+}  // extern "C"
