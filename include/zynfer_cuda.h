@@ -158,6 +158,10 @@ ZYNFER_CU_API int zynfer_cu_block_forward(ZynferCuCtx *ctx, uint32_t layer, uint
 /* matvecQ8 / matmul over `batch` rows (ops.zig:181-197): y[b][m] = (W[m,:] . x[b,:]) * scale[m]. */
 ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, const float *scale,
                      const float *x, uint32_t batch, uint32_t m, uint32_t k, float *y);
+/* Kernel family for linear layers: "auto" (CUDA-core GEMV for <= 4 rows,
+ * tcgen05 tensor cores above), "gemv", "tcgen05", or "simt" (the CUDA-core
+ * tiled GEMM, kept for comparisons). Applies to later calls of this context. */
+ZYNFER_CU_API int zynfer_cu_set_linear_path(ZynferCuCtx *ctx, const char *path);
 /* packRowQ8 (ops.zig:145-162) on the device, bit-exact. */
 ZYNFER_CU_API int zynfer_cu_pack_q8(ZynferCuCtx *ctx, const float *w, uint32_t rows, uint32_t cols, int8_t *q,
                       float *scale);

@@ -86,6 +86,51 @@ def test_linear_q8_batches(gpu, batch):  # gemv (<= 8 rows) and the tiled GEMM (
         assert O.expect_close(O.matvec_q8(q, s, x[b]), got[b], 2e-4, 2e-4), b
 
 
+@pytest.mark.parametrize("path", ["tcgen05", "simt", "gemv"])
+@pytest.mark.parametrize("m,k,batch", [(4096, 1024, 1), (4096, 1024, 5), (1024, 3072, 8), (4096, 1024, 16),
+                                       (6144, 1024, 48), (1024, 2048, 64), (3072, 1024, 100), (1024, 1024, 200)])
+def test_linear_q8_each_path(gpu, path, m, k, batch):  # ops.zig:181-197 on every kernel family
+    if path == "gemv" and batch > 8:
+        pytest.skip("the GEMV takes at most 8 rows")
+    w = O.synth_normal(m * k, 31, m + k, 0.02).reshape(m, k)
+    q, s = O.pack_row_q8(w)
+    x = O.synth_normal(batch * k, 32, batch, 1.0).reshape(batch, k)
+    x[0, :7] *= 50.0  # one large-magnitude row: exercises the per-row fixed-point exponent
+    y = torch.empty((batch, m), dtype=torch.float32, device="cuda")
+    gpu.set_linear_path(path)
+    try:
+        gpu.linear(zc.W_Q8, dev(q), dev(s), dev(x), batch, m, k, y)
+        gpu.sync()
+        assert gpu.last_path == {"tcgen05": "linear:tcgen05", "simt": "linear:simt", "gemv": "linear:gemv"}[path]
+    finally:
+        gpu.set_linear_path("auto")
+    got = host(y)
+    for b in range(batch):
+        ref = O.matvec_q8(q, s, x[b])
+        d = O.diff(ref, got[b])
+        assert O.expect_close(ref, got[b], 2e-4, 2e-4), (path, b, d.max_abs, d.failing_index)
+
+
+@pytest.mark.parametrize("path", ["tcgen05", "simt"])
+@pytest.mark.parametrize("batch", [5, 64, 200])
+def test_linear_bf16_each_path(gpu, path, batch):  # ops.zig:133-141 on bf16-widened weights
+    from oracle import synth_np
+    m, k = 2048, 1024
+    w = synth_np.bf16_round(O.synth_normal(m * k, 6, 6, 0.02)).reshape(m, k)
+    bits = synth_np.bf16_bits(w)
+    x = O.synth_normal(batch * k, 7, 7, 1.0).reshape(batch, k)
+    y = torch.empty((batch, m), dtype=torch.float32, device="cuda")
+    gpu.set_linear_path(path)
+    try:
+        gpu.linear(zc.W_BF16, dev(bits.view(np.int16)), None, dev(x), batch, m, k, y)
+        gpu.sync()
+    finally:
+        gpu.set_linear_path("auto")
+    got = host(y)
+    for b in range(batch):
+        assert O.expect_close(O.matvec(w, x[b]), got[b], 1e-4, 1e-4), (path, b)
+
+
 @pytest.mark.parametrize("batch", [1, 4, 24])
 def test_linear_bf16_matches_matvec(gpu, batch):  # ops.zig:133-141 on bf16-widened weights
     from oracle import synth_np

@@ -1,0 +1,33 @@
+"""Stated tolerances for GPU-vs-oracle logits.
+
+F32_PATH: f32 accumulation and f32 K/V on both sides (bf16 weights are exact
+in both): the bar for f32-accumulate paths, max_abs 2e-3 and cosine 0.99999.
+
+BF16_KV: both sides store K/V in bf16. Each side rounds its own f32 K/V,
+which differ in the last f32 bits (different summation order), so a few
+percent of cached elements land one bf16 step (2^-8 relative) apart; the
+logits inherit that. Measured worst case on the small test model
+(w_std 0.05, 2 layers): 6.4e-3. Stated bound: max_abs 1.5e-2, cosine 0.9999,
+argmax compared only where the oracle's top-2 gap exceeds the bound.
+"""
+import numpy as np
+
+from oracle import oracle as O
+
+F32_PATH = dict(atol=2e-3, cos=0.99999, tie=2e-3)
+BF16_KV = dict(atol=1.5e-2, cos=0.9999, tie=1.5e-2)
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def check_logits(ref, got, what="", tol=BF16_KV):
+    d = O.diff(ref, got)
+    assert d.max_abs <= tol["atol"], f"{what} max_abs={d.max_abs} idx={d.failing_index}"
+    assert cosine(ref, got) >= tol["cos"], what
+    top2 = np.sort(ref)[-2:]
+    if top2[1] - top2[0] > tol["tie"]:
+        assert int(np.argmax(got)) == int(np.argmax(ref)), what

@@ -21,10 +21,16 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "synth_rng.h"
+#include "tc_gemm.h"
 
 using namespace zc;
 
 namespace {
+
+// Which kernel runs a linear layer: the CUDA-core GEMV (few rows), the
+// tensor-core tcgen05 path, or the CUDA-core tiled GEMM (kept for A/B checks).
+enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3 };
+constexpr int kGemvMaxRows = 4;  // auto policy: GEMV up to this many rows, tcgen05 above
 
 struct LayerDev {
     void* wqkv = nullptr;
@@ -39,6 +45,8 @@ struct LayerDev {
     float* post_ln = nullptr;
     float* q_norm = nullptr;
     float* k_norm = nullptr;
+    // TMA descriptors of the weight matrices (128-row x 128-byte boxes)
+    CUtensorMap tm_qkv, tm_o, tm_gu, tm_d;
 };
 
 struct TimedEvent {
@@ -85,7 +93,7 @@ struct ZynferCuCtx {
     int* table_dev = nullptr;
 
     // decode scratch (max_batch rows)
-    float *dx = nullptr, *dx1 = nullptr, *dxn = nullptr, *dqkv = nullptr, *dq = nullptr,
+    float *dx = nullptr, *dx1 = nullptr, *dqkv = nullptr, *dq = nullptr,
           *dattn = nullptr, *dh = nullptr, *dlogits = nullptr, *dpart = nullptr;
     uint32_t* dio = nullptr;  // [tokens B][seq B][pos B] contiguous
     uint32_t* dtok = nullptr;
@@ -98,7 +106,7 @@ struct ZynferCuCtx {
     int* dstep = nullptr;
     size_t hist_cap = 0;  // entries
     // prefill scratch (max_prefill rows)
-    float *px = nullptr, *px1 = nullptr, *pxn = nullptr, *pqkv = nullptr, *pq = nullptr,
+    float *px = nullptr, *px1 = nullptr, *pqkv = nullptr, *pq = nullptr,
           *pk = nullptr, *pv = nullptr, *pattn = nullptr, *ph = nullptr;
     uint32_t* ptok = nullptr;
     // device error word and pinned host staging
@@ -106,6 +114,21 @@ struct ZynferCuCtx {
     uint32_t* herr = nullptr;
     uint32_t* hio = nullptr;   // pinned [3 * max_batch]
     uint32_t* hids = nullptr;  // pinned [max_batch]
+
+    CUtensorMap tm_embed;
+    // tcgen05 linear scratch: activation planes, per-row exponents, split-K
+    // accumulator and tile counters, plus B-operand descriptors per (kind, K, NT)
+    uint8_t* planes = nullptr;
+    int* exps = nullptr;
+    void* tc_acc = nullptr;
+    unsigned* tc_cnt = nullptr;
+    int tc_tpad = 0, tc_kmax = 0;
+    size_t tc_acc_bytes = 0;
+    std::map<uint64_t, CUtensorMap> bmaps;
+    std::map<std::pair<const void*, uint64_t>, CUtensorMap> amaps;  // op-level weights
+    float* simt_xn = nullptr;  // normalised rows for the CUDA-core GEMM path
+    size_t simt_xn_elems = 0;
+    int path_policy = kPathAuto;
 
     std::map<int, cudaGraphExec_t> graphs;
     int step_launches = 0;  // kernels enqueued by the last decode step
@@ -285,18 +308,89 @@ void tend(ZynferCuCtx* c, TimedEvent* te) {
     if (te) cudaEventRecord(te->b, c->stream);
 }
 
-void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, int M, int K, const float* x, int N,
-            float* y, int epi, const float* resid, const float* norm_w, unsigned long long* keys) {
+// Grow the tcgen05 scratch to hold `t` activation rows of up to `kmax` columns.
+int ensure_tc_scratch(ZynferCuCtx* c, int t, int kmax, int mmax) {
+    const int tpad = ((t + 127) / 128) * 128;
+    // split-K partials: [split][kAccT rows][M] 8-byte values. K is split only
+    // when there are fewer (M, N) tiles than SMs, so splits * M stays below
+    // ~2 * 148 * 128; 32768 covers it (linear() falls back to one split otherwise).
+    (void)mmax;
+    const size_t acc_bytes = (size_t)kAccT * 8 * 32768;
+    if (tpad <= c->tc_tpad && kmax <= c->tc_kmax && acc_bytes <= c->tc_acc_bytes) return ZYNFER_CU_OK;
+    int rc;
+    const int nt = std::max(tpad, c->tc_tpad), nk = std::max(kmax, c->tc_kmax);
+    const size_t na = std::max(acc_bytes, c->tc_acc_bytes);
+    // superseded buffers stay in c->allocs until destroy (scratch only grows)
+    if ((rc = dalloc(c, &c->planes, (size_t)4 * nt * nk))) return rc;  // 3 int8 or 2 bf16 planes
+    if ((rc = dalloc(c, &c->exps, (size_t)nt))) return rc;
+    char* acc;
+    if ((rc = dalloc(c, &acc, na))) return rc;
+    c->tc_acc = acc;
+    if ((rc = dalloc(c, &c->tc_cnt, 8192))) return rc;
+    cudaMemset(c->tc_acc, 0, na);
+    cudaMemset(c->tc_cnt, 0, 8192 * 4);
+    c->tc_tpad = nt;
+    c->tc_kmax = nk;
+    c->tc_acc_bytes = na;
+    c->bmaps.clear();
+    return ZYNFER_CU_OK;
+}
+
+const CUtensorMap* b_map(ZynferCuCtx* c, int wkind, int K, int nt) {
+    const uint64_t key = ((uint64_t)wkind << 48) | ((uint64_t)K << 16) | (uint64_t)nt;
+    auto it = c->bmaps.find(key);
+    if (it != c->bmaps.end()) return &it->second;
+    CUtensorMap m;
+    const int P = wkind == kWQ8 ? 3 : 2;
+    if (!make_tmap_k_major(&m, c->planes, wkind, (uint64_t)K, (uint64_t)P * c->tc_tpad, (uint32_t)nt)) return nullptr;
+    return &(c->bmaps[key] = m);
+}
+
+// y = linear(norm_w ? rmsnorm(x) : x) with the epilogue `epi`, on the path the
+// policy picks: GEMV (x staged in shared memory) for a few rows, tcgen05 for more.
+void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtensorMap* tmA, int M, int K,
+            const float* x, int N, float* y, int epi, const float* resid, const float* norm_w,
+            unsigned long long* keys, int wkind = -1) {
+    if (wkind < 0) wkind = c->wkind;
     LinearArgs a;
-    a.w = w; a.scale = s; a.wkind = c->wkind; a.M = M; a.K = K; a.x = x; a.ldx = K; a.N = N;
+    a.w = w; a.scale = s; a.wkind = wkind; a.M = M; a.K = K; a.x = x; a.ldx = K; a.N = N;
     a.y = y; a.ldy = epi == kEpiSwiGLU ? M / 2 : M; a.epi = epi; a.resid = resid; a.norm_w = norm_w;
-    a.eps = c->d.eps; a.argmax_keys = keys;
+    a.eps = c->d.eps > 0.0f ? c->d.eps : 1e-6f; a.argmax_keys = keys;
+    int path = c->path_policy;
+    if (path == kPathAuto) path = N <= kGemvMaxRows ? kPathGemv : kPathTc;
+    if (path == kPathGemv && N > 8) path = kPathTc;
+    if (path == kPathTc && (!tmA || N > c->tc_tpad || K > c->tc_kmax)) path = kPathSimt;
     TimedEvent* te;
     tbegin(c, cls, &te);
-    if (N <= 8) launch_gemv(a, c->stream);
-    else launch_gemm_simt(a, c->stream);
+    if (path == kPathGemv) {
+        launch_gemv(a, c->stream);
+        c->step_launches += 1;
+    } else if (path == kPathSimt) {
+        if (norm_w) {
+            launch_rmsnorm(x, norm_w, c->simt_xn, N, K, a.eps, c->stream);
+            a.x = c->simt_xn;
+            a.norm_w = nullptr;
+            c->step_launches += 1;
+        }
+        launch_gemm_simt(a, c->stream);
+        c->step_launches += 1;
+    } else {
+        PlanesArgs pa{x, K, N, K, c->tc_tpad, wkind, norm_w, a.eps, c->planes, c->exps};
+        launch_prep_planes(pa, c->stream);
+        const int nt = tc_tile_tokens(wkind, N);
+        TcLaunch L;
+        L.tmA = tmA;
+        L.tmB = b_map(c, wkind, K, nt);
+        L.args = TcArgs{M, K, N, c->tc_tpad, wkind, epi, s, c->exps, y, a.ldy, resid, keys, c->tc_acc, c->tc_cnt,
+                        c->derr};
+        int splits = tc_splits(M, N, K, wkind, c->caps.sm_count > 0 ? c->caps.sm_count : 148);
+        if (N > kAccT || (size_t)splits * kAccT * M * 8 > c->tc_acc_bytes || (M / 128) * ((N + nt - 1) / nt) > 8192)
+            splits = 1;
+        L.splits = splits;
+        if (L.tmB) launch_tc_gemm(L, c->stream);
+        c->step_launches += 2;
+    }
     tend(c, te);
-    c->step_launches += 1;
 }
 
 // One decode step for the rows already staged in dtok/dseq/dpos.
@@ -313,15 +407,8 @@ void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
     c->step_launches += 1;
     for (uint32_t l = 0; l < m.layers; ++l) {
         const LayerDev& Ld = c->L[l];
-        if (B <= 8) {
-            linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, c->qkv_rows, H, c->dx, B, c->dqkv, kEpiNone,
-                   nullptr, Ld.input_ln, nullptr);
-        } else {
-            launch_rmsnorm(c->dx, Ld.input_ln, c->dxn, B, H, m.eps, c->stream);
-            c->step_launches += 1;
-            linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, c->qkv_rows, H, c->dxn, B, c->dqkv, kEpiNone,
-                   nullptr, nullptr, nullptr);
-        }
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, &Ld.tm_qkv, c->qkv_rows, H, c->dx, B, c->dqkv, kEpiNone,
+               nullptr, Ld.input_ln, nullptr);
         QkvArgs qa{};
         qa.qkv = c->dqkv; qa.T = B; qa.n_q = m.n_q; qa.n_kv = m.n_kv; qa.d = m.head_dim;
         qa.q_norm = Ld.q_norm; qa.k_norm = Ld.k_norm; qa.eps = m.eps;
@@ -344,29 +431,15 @@ void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
         launch_attn_decode(aa, c->stream);
         tend(c, te);
         c->step_launches += 1;
-        linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, H, c->qd, c->dattn, B, c->dx1, kEpiResid, c->dx,
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, &Ld.tm_o, H, c->qd, c->dattn, B, c->dx1, kEpiResid, c->dx,
                nullptr, nullptr);
-        if (B <= 8) {
-            linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, 2 * I, H, c->dx1, B, c->dh, kEpiSwiGLU, nullptr,
-                   Ld.post_ln, nullptr);
-        } else {
-            launch_rmsnorm(c->dx1, Ld.post_ln, c->dxn, B, H, m.eps, c->stream);
-            c->step_launches += 1;
-            linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, 2 * I, H, c->dxn, B, c->dh, kEpiSwiGLU, nullptr,
-                   nullptr, nullptr);
-        }
-        linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, H, I, c->dh, B, c->dx, kEpiResid, c->dx1, nullptr,
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, &Ld.tm_gu, 2 * I, H, c->dx1, B, c->dh, kEpiSwiGLU, nullptr,
+               Ld.post_ln, nullptr);
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, &Ld.tm_d, H, I, c->dh, B, c->dx, kEpiResid, c->dx1, nullptr,
                nullptr);
     }
-    if (B <= 8) {
-        linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, m.vocab, H, c->dx, B,
-               want_logits ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
-    } else {
-        launch_rmsnorm(c->dx, c->final_norm, c->dxn, B, H, m.eps, c->stream);
-        c->step_launches += 1;
-        linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, m.vocab, H, c->dxn, B,
-               want_logits ? c->dlogits : nullptr, kEpiArgmax, nullptr, nullptr, c->dkeys);
-    }
+    linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, &c->tm_embed, m.vocab, H, c->dx, B,
+           want_logits ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
     FinalizeArgs fa{};
     fa.keys = c->dkeys; fa.ids_out = c->dids; fa.next_tokens = c->dtok; fa.positions = c->dpos;
     fa.history = c->dhist; fa.step = c->dstep; fa.B = B;
@@ -469,9 +542,8 @@ void enqueue_prefill_layers(ZynferCuCtx* c, uint32_t seq, int T, uint32_t l0, ui
     const int H = m.hidden, I = m.inter;
     for (uint32_t l = l0; l < l1; ++l) {
         const LayerDev& Ld = c->L[l];
-        launch_rmsnorm(c->px, Ld.input_ln, c->pxn, T, H, m.eps, c->stream);
-        linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, c->qkv_rows, H, c->pxn, T, c->pqkv, kEpiNone,
-               nullptr, nullptr, nullptr);
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, &Ld.tm_qkv, c->qkv_rows, H, c->px, T, c->pqkv, kEpiNone,
+               nullptr, Ld.input_ln, nullptr);
         QkvArgs qa{};
         qa.qkv = c->pqkv; qa.T = T; qa.n_q = m.n_q; qa.n_kv = m.n_kv; qa.d = m.head_dim;
         qa.q_norm = Ld.q_norm; qa.k_norm = Ld.k_norm; qa.eps = m.eps;
@@ -486,12 +558,11 @@ void enqueue_prefill_layers(ZynferCuCtx* c, uint32_t seq, int T, uint32_t l0, ui
         pa.q = c->pq; pa.k = c->pk; pa.v = c->pv; pa.T = T; pa.n_q = m.n_q; pa.n_kv = m.n_kv;
         pa.d = m.head_dim; pa.out = c->pattn;
         launch_attn_prefill(pa, c->stream);
-        linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, H, c->qd, c->pattn, T, c->px1, kEpiResid, c->px,
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, &Ld.tm_o, H, c->qd, c->pattn, T, c->px1, kEpiResid, c->px,
                nullptr, nullptr);
-        launch_rmsnorm(c->px1, Ld.post_ln, c->pxn, T, H, m.eps, c->stream);
-        linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, 2 * I, H, c->pxn, T, c->ph, kEpiSwiGLU, nullptr,
-               nullptr, nullptr);
-        linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, H, I, c->ph, T, c->px, kEpiResid, c->px1, nullptr,
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, &Ld.tm_gu, 2 * I, H, c->px1, T, c->ph, kEpiSwiGLU, nullptr,
+               Ld.post_ln, nullptr);
+        linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, &Ld.tm_d, H, I, c->ph, T, c->px, kEpiResid, c->px1, nullptr,
                nullptr);
     }
 }
@@ -556,8 +627,9 @@ int zynfer_cu_create(int device, ZynferCuCtx** out) {
 
 void zynfer_cu_destroy(ZynferCuCtx* c) {
     if (!c) return;
-    if (c->device >= 0) {
-        cudaSetDevice(c->device);
+    // During process teardown the runtime may already be unloading: then the
+    // driver reclaims everything and no CUDA call may be made.
+    if (c->device >= 0 && cudaSetDevice(c->device) == cudaSuccess) {
         if (c->stream) cudaStreamSynchronize(c->stream);
         for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
         for (auto& t : c->tev) {
@@ -680,7 +752,6 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     const size_t B = m.max_batch;
     ALLOC(c->dx, B * H);
     ALLOC(c->dx1, B * H);
-    ALLOC(c->dxn, B * H);
     ALLOC(c->dqkv, B * c->qkv_rows);
     ALLOC(c->dq, B * c->qd);
     ALLOC(c->dattn, B * c->qd);
@@ -699,7 +770,6 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     const size_t P = c->d.max_prefill;
     ALLOC(c->px, P * H);
     ALLOC(c->px1, P * H);
-    ALLOC(c->pxn, P * H);
     ALLOC(c->pqkv, P * c->qkv_rows);
     ALLOC(c->pq, P * c->qd);
     ALLOC(c->pk, P * c->kvd);
@@ -708,7 +778,24 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     ALLOC(c->ph, P * I);
     ALLOC(c->ptok, P);
     ALLOC(c->derr, 1);
+    c->simt_xn_elems = std::max(B, P) * H;
+    ALLOC(c->simt_xn, c->simt_xn_elems);
 #undef ALLOC
+    {
+        const int kmax = std::max({(int)H, c->qd, (int)I});
+        const int mmax = std::max({c->qkv_rows, 2 * (int)I, (int)H});
+        if ((rc = ensure_tc_scratch(c, (int)std::max(B, P), kmax, mmax))) return rc;
+    }
+    // TMA descriptors of every weight matrix (K-major, 128-row x 128-byte boxes)
+    for (auto& Ld : c->L) {
+        if (!make_tmap_k_major(&Ld.tm_qkv, Ld.wqkv, c->wkind, H, c->qkv_rows, 128) ||
+            !make_tmap_k_major(&Ld.tm_o, Ld.wo, c->wkind, c->qd, H, 128) ||
+            !make_tmap_k_major(&Ld.tm_gu, Ld.wgu, c->wkind, H, 2 * I, 128) ||
+            !make_tmap_k_major(&Ld.tm_d, Ld.wd, c->wkind, I, H, 128))
+            return fail(c, ZYNFER_CU_INTERNAL, "cuTensorMapEncodeTiled failed for a weight matrix");
+    }
+    if (!make_tmap_k_major(&c->tm_embed, c->embed, c->wkind, H, V, 128))
+        return fail(c, ZYNFER_CU_INTERNAL, "cuTensorMapEncodeTiled failed for the embedding");
     if ((rc = halloc(c, &c->herr, 1)) != ZYNFER_CU_OK) return rc;
     if ((rc = halloc(c, &c->hio, 3 * B)) != ZYNFER_CU_OK) return rc;
     if ((rc = halloc(c, &c->hids, B)) != ZYNFER_CU_OK) return rc;
@@ -930,7 +1017,7 @@ int zynfer_cu_prefill(ZynferCuCtx* c, uint32_t seq, const uint32_t* tokens, uint
     cudaEventRecord(c->ev0, c->stream);
     launch_embed(c->embed, c->sembed, c->wkind, c->ptok, n, m.hidden, m.vocab, c->px, c->derr, c->stream);
     enqueue_prefill_layers(c, seq, (int)n, 0, m.layers);
-    linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, m.vocab, m.hidden, c->px + (size_t)(n - 1) * m.hidden, 1,
+    linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, &c->tm_embed, m.vocab, m.hidden, c->px + (size_t)(n - 1) * m.hidden, 1,
            last_logits ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
     FinalizeArgs fa{};
     fa.keys = c->dkeys; fa.ids_out = c->dids; fa.B = 1;
@@ -1061,7 +1148,7 @@ int zynfer_cu_block_forward(ZynferCuCtx* c, uint32_t layer, uint32_t seq, const 
             c->hio[2] = pos0 + i;
             ZC_CHECK(c, cudaMemcpyAsync(c->dio, c->hio, 12, cudaMemcpyHostToDevice, c->stream), "stage");
             ZC_CHECK(c, cudaMemcpyAsync(c->dx, x + (size_t)i * H, (size_t)H * 4, cudaMemcpyHostToDevice, c->stream), "x");
-            linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, c->qkv_rows, H, c->dx, 1, c->dqkv, kEpiNone, nullptr, Ld.input_ln, nullptr);
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, &Ld.tm_qkv, c->qkv_rows, H, c->dx, 1, c->dqkv, kEpiNone, nullptr, Ld.input_ln, nullptr);
             QkvArgs qa{};
             qa.qkv = c->dqkv; qa.T = 1; qa.n_q = m.n_q; qa.n_kv = m.n_kv; qa.d = m.head_dim;
             qa.q_norm = Ld.q_norm; qa.k_norm = Ld.k_norm; qa.eps = m.eps; qa.rope = c->rope;
@@ -1076,9 +1163,9 @@ int zynfer_cu_block_forward(ZynferCuCtx* c, uint32_t layer, uint32_t seq, const 
             aa.max_splits = (int)((m.max_seq_len + aa.chunk - 1) / aa.chunk); aa.partial = c->dpart;
             aa.counters = c->dcnt; aa.out = c->dattn; aa.err = c->derr;
             launch_attn_decode(aa, c->stream);
-            linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, H, c->qd, c->dattn, 1, c->dx1, kEpiResid, c->dx, nullptr, nullptr);
-            linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, 2 * m.inter, H, c->dx1, 1, c->dh, kEpiSwiGLU, nullptr, Ld.post_ln, nullptr);
-            linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, H, m.inter, c->dh, 1, c->dx, kEpiResid, c->dx1, nullptr, nullptr);
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, &Ld.tm_o, H, c->qd, c->dattn, 1, c->dx1, kEpiResid, c->dx, nullptr, nullptr);
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, &Ld.tm_gu, 2 * m.inter, H, c->dx1, 1, c->dh, kEpiSwiGLU, nullptr, Ld.post_ln, nullptr);
+            linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, &Ld.tm_d, H, m.inter, c->dh, 1, c->dx, kEpiResid, c->dx1, nullptr, nullptr);
             ZC_CHECK(c, cudaMemcpyAsync(out + (size_t)i * H, c->dx, (size_t)H * 4, cudaMemcpyDeviceToHost, c->stream), "out");
             ZC_CHECK(c, cudaStreamSynchronize(c->stream), "block step");
         }
@@ -1098,20 +1185,42 @@ int zynfer_cu_linear(ZynferCuCtx* c, int wkind, const void* w, const float* scal
     if (wkind != ZYNFER_CU_W_Q8 && wkind != ZYNFER_CU_W_BF16) return fail(c, ZYNFER_CU_INVALID, "unknown weight kind");
     if (wkind == ZYNFER_CU_W_Q8 && !scale) return fail(c, ZYNFER_CU_INVALID, "int8 weights need scales");
     if (k % 512) return fail(c, ZYNFER_CU_UNSUPPORTED, "k must be a multiple of 512");
+    if (m % 128) return fail(c, ZYNFER_CU_UNSUPPORTED, "m must be a multiple of 128");
     if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
     cudaSetDevice(c->device);
-    LinearArgs a;
-    a.w = w; a.scale = wkind == ZYNFER_CU_W_Q8 ? scale : nullptr; a.wkind = wkind == ZYNFER_CU_W_Q8 ? kWQ8 : kWBF16;
-    a.M = (int)m; a.K = (int)k; a.x = x; a.ldx = (int)k; a.N = (int)batch; a.y = y; a.ldy = (int)m;
-    a.epi = kEpiNone;
-    TimedEvent* te;
-    tbegin(c, ZYNFER_CU_K_LINEAR, &te);
-    if (batch <= 8) launch_gemv(a, c->stream);
-    else launch_gemm_simt(a, c->stream);
-    tend(c, te);
+    const int wk = wkind == ZYNFER_CU_W_Q8 ? kWQ8 : kWBF16;
+    int rc = ensure_tc_scratch(c, (int)batch, (int)k, (int)m);
+    if (rc) return rc;
+    if (c->simt_xn_elems < (size_t)batch * k) {
+        if ((rc = dalloc(c, &c->simt_xn, (size_t)batch * k))) return rc;
+        c->simt_xn_elems = (size_t)batch * k;
+    }
+    const auto key = std::make_pair(w, ((uint64_t)wk << 62) | ((uint64_t)m << 32) | (uint64_t)k);
+    auto it = c->amaps.find(key);
+    if (it == c->amaps.end()) {
+        CUtensorMap tm;
+        if (!make_tmap_k_major(&tm, w, wk, k, m, 128)) return fail(c, ZYNFER_CU_INTERNAL, "cuTensorMapEncodeTiled failed");
+        it = c->amaps.emplace(key, tm).first;
+    }
+    c->step_launches = 0;
+    linear(c, ZYNFER_CU_K_LINEAR, w, wk == kWQ8 ? scale : nullptr, &it->second, (int)m, (int)k, x, (int)batch, y,
+           kEpiNone, nullptr, nullptr, nullptr, wk);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "linear launch");
-    c->path = batch <= 8 ? "linear:gemv" : "linear:gemm";
+    const int p = c->path_policy == kPathAuto ? (batch <= (uint32_t)kGemvMaxRows ? kPathGemv : kPathTc) : c->path_policy;
+    c->path = p == kPathGemv && batch <= 8 ? "linear:gemv" : (p == kPathSimt ? "linear:simt" : "linear:tcgen05");
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_set_linear_path(ZynferCuCtx* c, const char* path) {
+    if (!c || !path) return ZYNFER_CU_INVALID;
+    if (!strcmp(path, "auto")) c->path_policy = kPathAuto;
+    else if (!strcmp(path, "gemv")) c->path_policy = kPathGemv;
+    else if (!strcmp(path, "simt")) c->path_policy = kPathSimt;
+    else if (!strcmp(path, "tcgen05")) c->path_policy = kPathTc;
+    else return fail(c, ZYNFER_CU_INVALID, std::string("unknown linear path ") + path);
+    for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);  // graphs bake the old choice
+    c->graphs.clear();
     return ZYNFER_CU_OK;
 }
 

@@ -1,0 +1,56 @@
+// tcgen05 weight-only linear (internal to libzynfer_cuda). See tc_gemm.cu.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+
+namespace zc {
+
+// Activation planes: rows [0, T) of X (f32, optionally RMS-normalised) ->
+// planes [P][t_pad][K]: int8 digits (P = 3, plus exps[T]) or bf16 hi/lo (P = 2).
+struct PlanesArgs {
+    const float* x;
+    int ldx;
+    int T, K, t_pad;
+    int wkind;
+    const float* norm_w;  // nullable
+    float eps;
+    void* planes;
+    int* exps;  // int8 only
+};
+
+constexpr int kAccT = 64;  // split-K accumulator rows per plane (split-K only for T <= 64)
+
+struct TcArgs {
+    int M, K, T, t_pad;
+    int wkind;
+    int epi;
+    const float* scale;  // [M] (int8) or nullptr
+    const int* exps;     // [T] (int8)
+    float* y;            // [T][ldy]
+    int ldy;
+    const float* resid;
+    unsigned long long* argmax_keys;
+    void* acc;               // split-K accumulator [P][kAccT][M] (zero between uses)
+    unsigned int* counters;  // split-K tile counters (zero between uses)
+    uint32_t* err;
+};
+
+struct TcLaunch {
+    const CUtensorMap* tmA;  // weights [M][K], box 128 B x 128 rows
+    const CUtensorMap* tmB;  // planes [P * t_pad][K], box 128 B x NT rows
+    TcArgs args;
+    int splits;
+};
+
+int tc_tile_tokens(int wkind, int T);  // NT: tokens per N tile
+int tc_splits(int M, int T, int K, int wkind, int sms);
+bool make_tmap_k_major(CUtensorMap* map, const void* base, int wkind, uint64_t k_elems, uint64_t rows,
+                       uint32_t box_rows);
+void launch_prep_planes(const PlanesArgs& a, cudaStream_t st);
+void launch_tc_gemm(const TcLaunch& L, cudaStream_t st);
+
+}  // namespace zc

@@ -7,8 +7,10 @@ in-tree library and nothing else: there is no CPU path here.
 """
 from __future__ import annotations
 
+import atexit
 import ctypes as C
 import os
+import weakref
 from dataclasses import dataclass
 
 import numpy as np
@@ -98,6 +100,7 @@ _SIGS = {
     "zynfer_cu_generate": (C.c_int, [VP, VP, VP, U32, U32, VP, C.POINTER(C.c_float)]),
     "zynfer_cu_block_forward": (C.c_int, [VP, U32, U32, VP, U32, VP]),
     "zynfer_cu_linear": (C.c_int, [VP, C.c_int, VP, VP, VP, U32, U32, U32, VP]),
+    "zynfer_cu_set_linear_path": (C.c_int, [VP, C.c_char_p]),
     "zynfer_cu_pack_q8": (C.c_int, [VP, VP, U32, U32, VP, VP]),
     "zynfer_cu_rmsnorm": (C.c_int, [VP, VP, VP, U32, U32, C.c_float, VP]),
     "zynfer_cu_set_timing": (C.c_int, [VP, C.c_int]),
@@ -155,8 +158,18 @@ class Arch:
 QWEN3_0_6B = Arch()
 
 
+_LIVE: "weakref.WeakSet[Gpu]" = weakref.WeakSet()
+
+
+@atexit.register
+def _close_live_contexts():
+    """Destroy contexts before interpreter teardown, while the CUDA runtime is still up."""
+    for g in list(_LIVE):
+        g.close()
+
+
 class Gpu:
-    """One context on one device (zynfer_cu_create / destroy)."""
+    """One context on one device (zynfer_cu_create / destroy). One model per context."""
 
     def __init__(self, device: int = 0):
         L = lib()
@@ -169,6 +182,7 @@ class Gpu:
                 L.zynfer_cu_destroy(h)
             self.h = None
             raise _ERRORS.get(rc, CudaError)(msg)
+        _LIVE.add(self)
 
     def check(self, rc: int):
         if rc != OK:
@@ -196,6 +210,10 @@ class Gpu:
     # op level (device pointers)
     def linear(self, wkind, w, scale, x, batch, m, k, y):
         self.check(lib().zynfer_cu_linear(self.h, wkind, _ptr(w), _ptr(scale), _ptr(x), batch, m, k, _ptr(y)))
+
+    def set_linear_path(self, path: str):
+        """"auto" | "gemv" | "tcgen05" | "simt"."""
+        self.check(lib().zynfer_cu_set_linear_path(self.h, path.encode()))
 
     def pack_q8(self, w, rows, cols, q, scale):
         self.check(lib().zynfer_cu_pack_q8(self.h, _ptr(w), rows, cols, _ptr(q), _ptr(scale)))
