@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnDecodeArgs
     __shared__ __align__(16) float red_acc[4][kG][kD];
     __shared__ int is_last;
 
+    pdl_launch_dependents();
+    pdl_wait();
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
     const int seq = a.seq_of[b];
@@ -254,6 +256,8 @@ __global__ void __launch_bounds__(PTHREADS) attn_prefill_kernel(AttnPrefillArgs 
     float* rowc = Ps + PK * PQ;           // [PQ] correction factors
     float* rowl = rowc + PQ;              // [PQ] final sums
 
+    pdl_launch_dependents();
+    pdl_wait();
     const int qt = blockIdx.x, h = blockIdx.y;
     const int kvh = h / (a.n_q / a.n_kv);
     const int q0 = qt * PQ;
@@ -367,30 +371,22 @@ __global__ void __launch_bounds__(PTHREADS) attn_prefill_kernel(AttnPrefillArgs 
 
 }  // namespace
 
+constexpr size_t kDecodeSmem = (size_t)2 * kStages * kStageElems * 2 + kStages * sizeof(uint64_t);
+constexpr size_t kPrefillSmem = ((size_t)kD * PQ + kD * PK + PK * kD + PK * PQ + 2 * PQ) * sizeof(float);
+
+void prepare_attn_kernels() {
+    configure_kernel((const void*)attn_decode_kernel, kDecodeSmem);
+    configure_kernel((const void*)attn_prefill_kernel, kPrefillSmem);
+}
+
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st) {
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const size_t smem = (size_t)2 * kStages * kStageElems * 2 + kStages * sizeof(uint64_t);
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
-        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr[dev] = true;
-    }
     dim3 grid(a.max_splits, a.n_kv, a.B);
-    attn_decode_kernel<<<grid, kDecThreads, smem, st>>>(a);
+    launch_pdl(attn_decode_kernel, grid, kDecThreads, kDecodeSmem, st, a);
 }
 
 void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st) {
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const size_t smem = ((size_t)kD * PQ + kD * PK + PK * kD + PK * PQ + 2 * PQ) * sizeof(float);
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
-        cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr[dev] = true;
-    }
     dim3 grid((a.T + PQ - 1) / PQ, a.n_q);
-    attn_prefill_kernel<<<grid, PTHREADS, smem, st>>>(a);
+    launch_pdl(attn_prefill_kernel, grid, PTHREADS, kPrefillSmem, st, a);
 }
 
 }  // namespace zc

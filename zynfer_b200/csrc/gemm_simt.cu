@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(LinearArgs a) {
     __shared__ __align__(16) float Ws[BK][WPAD];
     __shared__ __align__(16) float Xs[BK][XPAD];
     __shared__ unsigned long long best_s[BN];
+    pdl_launch_dependents();
+    pdl_wait();
     const int tid = threadIdx.x;
     const int tx = tid % 16, ty = tid / 16;
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
@@ -147,14 +149,25 @@ template <int WK>
 void launch_wk(const LinearArgs& a, cudaStream_t st) {
     dim3 grid((a.M + BM - 1) / BM, (a.N + BN - 1) / BN);
     switch (a.epi) {
-        case kEpiResid: gemm_simt_kernel<WK, kEpiResid><<<grid, THREADS, 0, st>>>(a); break;
-        case kEpiSwiGLU: gemm_simt_kernel<WK, kEpiSwiGLU><<<grid, THREADS, 0, st>>>(a); break;
-        case kEpiArgmax: gemm_simt_kernel<WK, kEpiArgmax><<<grid, THREADS, 0, st>>>(a); break;
-        default: gemm_simt_kernel<WK, kEpiNone><<<grid, THREADS, 0, st>>>(a); break;
+        case kEpiResid: launch_pdl(gemm_simt_kernel<WK, kEpiResid>, grid, THREADS, 0, st, a); break;
+        case kEpiSwiGLU: launch_pdl(gemm_simt_kernel<WK, kEpiSwiGLU>, grid, THREADS, 0, st, a); break;
+        case kEpiArgmax: launch_pdl(gemm_simt_kernel<WK, kEpiArgmax>, grid, THREADS, 0, st, a); break;
+        default: launch_pdl(gemm_simt_kernel<WK, kEpiNone>, grid, THREADS, 0, st, a); break;
     }
 }
 
 }  // namespace
+
+void prepare_gemm_simt_kernels() {
+    configure_kernel((const void*)gemm_simt_kernel<kWQ8, kEpiNone>, 0);
+    configure_kernel((const void*)gemm_simt_kernel<kWQ8, kEpiResid>, 0);
+    configure_kernel((const void*)gemm_simt_kernel<kWQ8, kEpiSwiGLU>, 0);
+    configure_kernel((const void*)gemm_simt_kernel<kWQ8, kEpiArgmax>, 0);
+    configure_kernel((const void*)gemm_simt_kernel<kWBF16, kEpiNone>, 0);
+    configure_kernel((const void*)gemm_simt_kernel<kWBF16, kEpiResid>, 0);
+    configure_kernel((const void*)gemm_simt_kernel<kWBF16, kEpiSwiGLU>, 0);
+    configure_kernel((const void*)gemm_simt_kernel<kWBF16, kEpiArgmax>, 0);
+}
 
 void launch_gemm_simt(const LinearArgs& a, cudaStream_t st) {
     if (a.wkind == kWQ8) launch_wk<kWQ8>(a, st);

@@ -43,6 +43,17 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
     __shared__ unsigned long long best_s[kWarps][NB];
     const int K = a.K;
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    pdl_launch_dependents();
+    {
+        // the weights do not depend on the previous kernel: pull this warp's
+        // first row group toward L2 while that kernel finishes
+        const int row_bytes = WK == kWQ8 ? K : 2 * K;
+        const int r0 = (blockIdx.x * kWarps + warp) * R;
+        const char* wb = reinterpret_cast<const char*>(a.w);
+        for (int r = 0; r < R && r0 + r < a.M; ++r)
+            for (int off = lane * 128; off < row_bytes; off += kWarp * 128) prefetch_l2(wb + (size_t)(r0 + r) * row_bytes + off);
+    }
+    pdl_wait();
 
     // ---- stage activations (RMSNorm prologue when norm_w is set)
     for (int b = 0; b < a.N; ++b) {
@@ -174,18 +185,10 @@ void launch_nb(const LinearArgs& a, cudaStream_t st) {
     const size_t smem = (size_t)NB * a.K * sizeof(float);
     const int groups = (a.M + R - 1) / R;
     auto pick = [&](auto kern) {
-        // The opt-in shared-memory ceiling is a per-device function attribute.
-        static bool attr_set[64] = {false};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 3072 * 4);
-            attr_set[dev] = true;
-        }
         // resident CTAs per SM: bounded by threads (2048 / 256) and shared memory
         const int per_sm = std::max(1, std::min(8, (int)((220 * 1024) / (smem + 2048))));
         const int want = (groups + kWarps - 1) / kWarps;
-        kern<<<std::min(want, per_sm * device_sm_count()), kThreads, smem, st>>>(a);
+        launch_pdl(kern, std::min(want, per_sm * device_sm_count()), kThreads, smem, st, a);
     };
     switch (a.epi) {
         case kEpiResid: pick(gemv_kernel<WK, NB, R, kEpiResid>); break;
@@ -203,7 +206,21 @@ void launch_wk(const LinearArgs& a, cudaStream_t st) {
     else launch_nb<WK, 8, 2>(a, st);
 }
 
+template <int WK, int NB, int R>
+void prepare_nb() {
+    constexpr size_t smem = (size_t)8 * 3072 * 4;  // 8 rows of the widest K (3072)
+    configure_kernel((const void*)gemv_kernel<WK, NB, R, kEpiNone>, smem);
+    configure_kernel((const void*)gemv_kernel<WK, NB, R, kEpiResid>, smem);
+    configure_kernel((const void*)gemv_kernel<WK, NB, R, kEpiSwiGLU>, smem);
+    configure_kernel((const void*)gemv_kernel<WK, NB, R, kEpiArgmax>, smem);
+}
+
 }  // namespace
+
+void prepare_gemv_kernels() {
+    prepare_nb<kWQ8, 1, 4>(); prepare_nb<kWQ8, 2, 4>(); prepare_nb<kWQ8, 4, 2>(); prepare_nb<kWQ8, 8, 2>();
+    prepare_nb<kWBF16, 1, 4>(); prepare_nb<kWBF16, 2, 4>(); prepare_nb<kWBF16, 4, 2>(); prepare_nb<kWBF16, 8, 2>();
+}
 
 void launch_gemv(const LinearArgs& a, cudaStream_t st) {
     if (a.wkind == kWQ8) launch_wk<kWQ8>(a, st);

@@ -36,6 +36,13 @@ struct LinearArgs {
 
 // synth.cu
 int device_sm_count();  // SMs of the current device (cached)
+void configure_kernel(const void* func, size_t dyn_smem);  // once per device, before any launch
+void prepare_all_kernels();  // configure every kernel of the library on the current device
+void prepare_norm_kernels();
+void prepare_gemv_kernels();
+void prepare_gemm_simt_kernels();
+void prepare_attn_kernels();
+void prepare_tc_kernels();
 void launch_synth_normal(float* out, size_t n, uint64_t seed, uint64_t stream, float k,
                          float add, cudaStream_t st);
 void launch_fill(float* out, size_t n, float v, cudaStream_t st);

@@ -10,6 +10,8 @@ namespace zc {
 // reference's sequential sum, within f32 rounding).
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                float* __restrict__ y, int rows, int cols, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) / kWarp;
     const int lane = threadIdx.x % kWarp;
     if (row >= rows) return;
@@ -38,7 +40,7 @@ void launch_rmsnorm(const float* x, const float* w, float* y, int rows, int cols
                     cudaStream_t st) {
     const int threads = 256;
     const int blocks = (rows * kWarp + threads - 1) / threads;
-    rmsnorm_kernel<<<blocks, threads, 0, st>>>(x, w, y, rows, cols, eps);
+    launch_pdl(rmsnorm_kernel, blocks, threads, 0, st, x, w, y, rows, cols, eps);
 }
 
 // Embedding rows (ops.zig:397-411). int8 tables are dequantised as
@@ -46,6 +48,8 @@ void launch_rmsnorm(const float* x, const float* w, float* y, int rows, int cols
 __global__ void embed_kernel(const void* __restrict__ table, const float* __restrict__ scale,
                              int wkind, const uint32_t* __restrict__ ids, int n, int H, int V,
                              float* __restrict__ x, uint32_t* err) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int row = blockIdx.x;
     if (row >= n) return;
     const uint32_t id = ids[row];
@@ -68,7 +72,7 @@ __global__ void embed_kernel(const void* __restrict__ table, const float* __rest
 void launch_embed(const void* table, const float* scale, int wkind, const uint32_t* ids, int n, int H,
                   int V, float* x, uint32_t* err, cudaStream_t st) {
     if (n <= 0) return;
-    embed_kernel<<<n, 256, 0, st>>>(table, scale, wkind, ids, n, H, V, x, err);
+    launch_pdl(embed_kernel, n, 256, 0, st, table, scale, wkind, ids, n, H, V, x, err);
 }
 
 // One warp per (row, head) over the fused QKV output. q and k heads get the
@@ -79,6 +83,8 @@ void launch_embed(const void* table, const float* scale, int wkind, const uint32
 // head_dim is 128: lane holds elements lane + 32 j, j = 0..3, so the RoPE
 // pairs (i, i + 64) sit in one lane.
 __global__ void qkv_post_kernel(QkvArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / kWarp;
     const int lane = threadIdx.x % kWarp;
     const int heads = a.n_q + 2 * a.n_kv;
@@ -145,12 +151,14 @@ __global__ void qkv_post_kernel(QkvArgs a) {
 void launch_qkv_post(const QkvArgs& a, cudaStream_t st) {
     const int warps = a.T * (a.n_q + 2 * a.n_kv);
     const int threads = 256;
-    qkv_post_kernel<<<(warps * kWarp + threads - 1) / threads, threads, 0, st>>>(a);
+    launch_pdl(qkv_post_kernel, (warps * kWarp + threads - 1) / threads, threads, 0, st, a);
 }
 
 // Turn argmax keys into ids, feed them to the next step, advance positions,
 // and append to the on-device history. One CTA.
 __global__ void finalize_kernel(FinalizeArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = threadIdx.x;
     const int row = a.history ? *a.step : 0;
     __syncthreads();
@@ -168,7 +176,7 @@ __global__ void finalize_kernel(FinalizeArgs a) {
 
 void launch_finalize(const FinalizeArgs& a, cudaStream_t st) {
     const int threads = ((a.B + 31) / 32) * 32;
-    finalize_kernel<<<1, threads, 0, st>>>(a);
+    launch_pdl(finalize_kernel, 1, threads, 0, st, a);
 }
 
 __global__ void bf16_to_f32_kernel(const uint16_t* __restrict__ src, size_t n, float* __restrict__ dst) {
@@ -181,6 +189,13 @@ void launch_bf16_to_f32(const uint16_t* src, size_t n, float* dst, cudaStream_t 
     size_t g = (n + 255) / 256;
     if (g > 148 * 64) g = 148 * 64;
     bf16_to_f32_kernel<<<(int)(g ? g : 1), 256, 0, st>>>(src, n, dst);
+}
+
+void prepare_norm_kernels() {
+    configure_kernel((const void*)rmsnorm_kernel, 0);
+    configure_kernel((const void*)embed_kernel, 0);
+    configure_kernel((const void*)qkv_post_kernel, 0);
+    configure_kernel((const void*)finalize_kernel, 0);
 }
 
 }  // namespace zc

@@ -119,7 +119,7 @@ struct ZynferCuCtx {
     // tcgen05 linear scratch: activation planes, per-row exponents, split-K
     // accumulator and tile counters, plus B-operand descriptors per (kind, K, NT)
     uint8_t* planes = nullptr;
-    int* exps = nullptr;
+    float* exps = nullptr;  // per-row 2^(e-22) of the int8 digit planes
     void* tc_acc = nullptr;
     unsigned* tc_cnt = nullptr;
     int tc_tpad = 0, tc_kmax = 0;
@@ -387,6 +387,7 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
         if (N > kAccT || (size_t)splits * kAccT * M * 8 > c->tc_acc_bytes || (M / 128) * ((N + nt - 1) / nt) > 8192)
             splits = 1;
         L.splits = splits;
+        L.sms = c->caps.sm_count > 0 ? c->caps.sm_count : 148;
         if (L.tmB) launch_tc_gemm(L, c->stream);
         c->step_launches += 2;
     }
@@ -620,6 +621,7 @@ int zynfer_cu_create(int device, ZynferCuCtx** out) {
     }
     cudaEventCreate(&c->ev0);
     cudaEventCreate(&c->ev1);
+    prepare_all_kernels();  // function attributes now, never during a graph capture
     parse_fail_spec(c, getenv("ZYNFER_CUDA_FAIL_AT"));
     *out = c;
     return ZYNFER_CU_OK;

@@ -4,6 +4,10 @@
 // the int8 weights and scales are bit-identical to the host oracle's:
 // max|w| is order-independent, and every other step is one IEEE f32 operation
 // (division, reciprocal, multiply, roundf, clamp).
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "synth_rng.h"
@@ -22,6 +26,29 @@ __global__ void fill_kernel(float* out, size_t n, float v) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)
         out[i] = v;
+}
+
+// Function attributes, set once per device before any launch (so never
+// during stream capture): the opt-in dynamic shared-memory ceiling, and the
+// same L1/shared split (maximum shared memory) for every kernel so that
+// consecutive kernels do not make the SM reconfigure its carveout.
+void configure_kernel(const void* func, size_t dyn_smem) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done.insert({dev, func}).second) return;
+    if (dyn_smem > 48 * 1024) cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_smem);
+    cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+}
+
+void prepare_all_kernels() {
+    prepare_norm_kernels();
+    prepare_gemv_kernels();
+    prepare_gemm_simt_kernels();
+    prepare_attn_kernels();
+    prepare_tc_kernels();
 }
 
 int device_sm_count() {

@@ -19,14 +19,17 @@
 // hi = bf16(x) and lo = bf16(x - hi) planes (x = hi + lo to 2^-16 relative);
 // the weights are exact bf16, so the product is f32-accumulate grade.
 //
-// Warp roles (192 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
-// issues MMAs (one elected lane), warps 2..5 drain TMEM (each reads its
-// 32-lane quarter) and run the epilogue. Shared-memory stages are recycled
-// through mbarriers (full: TMA transaction bytes; empty: tcgen05.commit). No
-// multicast anywhere. Every wait is bounded and reports through the device
-// error word. When there are too few (M, N) tiles to fill the GPU, K is split
-// across CTAs: int8 partial sums are added with integer atomics (exact, order
-// independent) and the last CTA of a tile runs the epilogue.
+// Persistent and warp-specialised (320 threads, one CTA per SM walking the
+// (M tile, N tile, K split) units): warp 0 issues TMA loads, warp 1 owns TMEM
+// and issues MMAs (one elected lane), warps 2..9 drain TMEM (two warps per
+// 32-lane quarter, alternate 16-token chunks) and run the epilogue. TMEM holds
+// two accumulators so the epilogue of one unit overlaps the loads and MMAs of
+// the next. Shared-memory stages are recycled through mbarriers (full: TMA
+// transaction bytes; empty: tcgen05.commit). No multicast anywhere. Every wait
+// is bounded and reports through the device error word. When there are too
+// few (M, N) tiles to fill the GPU, K is split: each unit stores its exact
+// 64-bit partial values with plain stores and the last unit of a tile to
+// finish sums them in split order (deterministic) before the epilogue.
 #include <cuda.h>
 
 #include <algorithm>
@@ -39,7 +42,7 @@ namespace zc {
 
 namespace {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int kBM = 128;      // weight rows per CTA (MMA M)
 constexpr int kKB = 128;      // bytes of K per stage (one 128-byte swizzle atom)
 
@@ -100,7 +103,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 
@@ -124,7 +127,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     constexpr int B_BYTES = N * kKB;
     constexpr int STAGE = A_BYTES + B_BYTES;
     constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
-    constexpr uint32_t TMEM_COLS = N <= 32 ? 32 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));
+    constexpr uint32_t ACC_COLS = N <= 32 ? 32 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));
+    constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;  // two accumulators: epilogue of one overlaps the next tile
     constexpr int KSTEP = 32;  // bytes of K per MMA instruction (i8: K = 32, bf16: K = 16)
     static_assert(NT % 16 == 0 && N <= 256 && STAGES >= 2, "tile shape");
 
@@ -132,24 +136,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
     uint64_t* empty = full + STAGES;
-    uint64_t* tmem_full = empty + STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+    uint64_t* tmem_full = empty + STAGES;   // [2]
+    uint64_t* tmem_empty = tmem_full + 2;   // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
     __shared__ unsigned long long best_s[NT];
     __shared__ int last_flag;
 
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-    const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;
-    const int m0 = m_tile * kBM, n0 = n_tile * NT;
+    pdl_launch_dependents();
+    const int m_tiles = a.M / kBM;
+    const int n_tiles = (a.T + NT - 1) / NT;
+    const int splits = a.splits;
+    const int units = m_tiles * n_tiles * splits;
     const int nkb = a.K * (WK == kWQ8 ? 1 : 2) / kKB;
-    const int kb0 = (int)((long)split * nkb / gridDim.z), kb1 = (int)((long)(split + 1) * nkb / gridDim.z);
-    const int nk = kb1 - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(tmem_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tmem_full[b], 1);
+            mbar_init(&tmem_empty[b], 8);  // one arrival per epilogue warp
+        }
         fence_barrier_init();
     }
     if constexpr (EPI == kEpiArgmax) {
@@ -164,152 +173,238 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem_d = *tmem_slot;
+    const uint32_t tmem_base = *tmem_slot;
+
+    // unit u -> (m_tile, n_tile, split); consecutive CTAs stream consecutive weight tiles
+    auto unit_coords = [&](int u, int& mt, int& nt, int& sp) {
+        mt = u % m_tiles;
+        nt = (u / m_tiles) % n_tiles;
+        sp = u / (m_tiles * n_tiles);
+    };
+    auto kb_range = [&](int sp, int& kb0, int& kb1) {
+        kb0 = (int)((long)sp * nkb / splits);
+        kb1 = (int)((long)(sp + 1) * nkb / splits);
+    };
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---------------- TMA producer
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % STAGES, round = i / STAGES;
-                if (!mbar_wait_bounded(&empty[s], (uint32_t)((round & 1) ^ 1), a.err)) break;
-                uint8_t* as = smem + s * STAGE;
-                uint8_t* bs = as + A_BYTES;
-                mbar_arrive_expect_tx(&full[s], STAGE);
-                const int kx = (kb0 + i) * (WK == kWQ8 ? kKB : kKB / 2);
-                tma_load_2d(as, &tmA, kx, m0, &full[s]);
+            // ---------------- TMA producer: every k-block of every unit of this CTA.
+            // The weights do not depend on the previous kernel, so the first
+            // STAGES weight tiles are requested before griddepcontrol.wait; the
+            // activation tiles (written by the previous kernel) only after it.
+            int npre = 0;
+            {
+                int u = blockIdx.x;
+                if (u < units) {
+                    int mt, nt, sp, kb0, kb1;
+                    unit_coords(u, mt, nt, sp);
+                    kb_range(sp, kb0, kb1);
+                    for (int kb = kb0; kb < kb1 && npre < STAGES; ++kb, ++npre) {
+                        mbar_arrive_expect_tx(&full[npre], STAGE);
+                        tma_load_2d(smem + npre * STAGE, &tmA, kb * (WK == kWQ8 ? kKB : kKB / 2), mt * kBM,
+                                    &full[npre]);
+                    }
+                }
+            }
+            pdl_wait();
+            int i = 0;
+            bool alive = true;
+            for (int u = blockIdx.x; u < units && alive; u += gridDim.x) {
+                int mt, nt, sp, kb0, kb1;
+                unit_coords(u, mt, nt, sp);
+                kb_range(sp, kb0, kb1);
+                for (int kb = kb0; kb < kb1; ++kb, ++i) {
+                    const int s = i % STAGES, round = i / STAGES;
+                    uint8_t* as = smem + s * STAGE;
+                    uint8_t* bs = as + A_BYTES;
+                    const int kx = kb * (WK == kWQ8 ? kKB : kKB / 2);
+                    if (i >= npre) {
+                        if (!mbar_wait_bounded(&empty[s], (uint32_t)((round & 1) ^ 1), a.err)) {
+                            alive = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[s], STAGE);
+                        tma_load_2d(as, &tmA, kx, mt * kBM, &full[s]);
+                    }
 #pragma unroll
-                for (int p = 0; p < P; ++p) tma_load_2d(bs + p * NT * kKB, &tmB, kx, p * a.t_pad + n0, &full[s]);
+                    for (int p = 0; p < P; ++p)
+                        tma_load_2d(bs + p * NT * kKB, &tmB, kx, p * a.t_pad + nt * NT, &full[s]);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer
             constexpr uint32_t idesc = make_idesc<WK>(N);
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % STAGES, round = i / STAGES;
-                if (!mbar_wait_bounded(&full[s], (uint32_t)(round & 1), a.err)) break;
+            int i = 0, j = 0;
+            bool alive = true;
+            for (int u = blockIdx.x; u < units && alive; u += gridDim.x, ++j) {
+                int mt, nt, sp, kb0, kb1;
+                unit_coords(u, mt, nt, sp);
+                kb_range(sp, kb0, kb1);
+                const int acc = j & 1;
+                if (!mbar_wait_bounded(&tmem_empty[acc], (uint32_t)(((j >> 1) & 1) ^ 1), a.err)) break;
                 tc_fence_after();
-                const uint32_t as = smem_addr(smem + s * STAGE);
-                const uint32_t bs = as + A_BYTES;
+                const uint32_t tmem_d = tmem_base + acc * ACC_COLS;
+                for (int kb = kb0; kb < kb1; ++kb, ++i) {
+                    const int s = i % STAGES, round = i / STAGES;
+                    if (!mbar_wait_bounded(&full[s], (uint32_t)(round & 1), a.err)) {
+                        alive = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t as = smem_addr(smem + s * STAGE);
+                    const uint32_t bs = as + A_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < kKB / KSTEP; ++kk)
-                    mma_issue<WK>(tmem_d, sdesc_sw128(as + kk * KSTEP), sdesc_sw128(bs + kk * KSTEP), idesc,
-                                  (i > 0 || kk > 0) ? 1u : 0u);
-                mma_commit(&empty[s]);
+                    for (int kk = 0; kk < kKB / KSTEP; ++kk)
+                        mma_issue<WK>(tmem_d, sdesc_sw128(as + kk * KSTEP), sdesc_sw128(bs + kk * KSTEP), idesc,
+                                      (kb > kb0 || kk > 0) ? 1u : 0u);
+                    mma_commit(&empty[s]);
+                }
+                mma_commit(&tmem_full[acc]);
             }
-            mma_commit(tmem_full);
         }
     } else {
-        // ---------------- epilogue (warps 2..5; TMEM lane quarter = warp % 4)
-        const int q = warp & 3;
-        const int row = m0 + q * 32 + lane;
-        const bool ok = mbar_wait_bounded(tmem_full, 0u, a.err);
-        tc_fence_after();
-        const uint32_t tbase = tmem_d + ((uint32_t)(q * 32) << 16);
-        const float sc = (a.scale && row < a.M) ? a.scale[row] : 1.0f;
-        const bool split_k = gridDim.z > 1;
-        // Per (token, row) value of this CTA's K range, exact: int8 digits
-        // recombined in 64-bit integers; bf16 hi + lo planes summed in f64.
-        auto tile_values = [&](int t0, long long (&v)[16]) {
-            uint32_t r[P][16];
+        // ---------------- epilogue (warps 2..9; TMEM lane quarter = warp % 4).
+        // Reads the activations' row scales and the residual, written by
+        // earlier kernels: wait for them first.
+        pdl_wait();
+        const int q = warp & 3;          // TMEM lane quarter
+        const int h = (warp - 2) >> 2;   // which half of the 16-token chunks
+        int j = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+            int mt, nt, sp;
+            unit_coords(u, mt, nt, sp);
+            const int m0 = mt * kBM, n0 = nt * NT;
+            const int acc = j & 1;
+            const int row = m0 + q * 32 + lane;
+            const bool ok = mbar_wait_bounded(&tmem_full[acc], (uint32_t)((j >> 1) & 1), a.err);
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + acc * ACC_COLS + ((uint32_t)(q * 32) << 16);
+            const float sc = (a.scale && row < a.M) ? a.scale[row] : 1.0f;
+            const bool split_k = splits > 1;
+            // Per (token, row) value of this unit's K range, exact: int8 digits
+            // recombined in 64-bit integers; bf16 hi + lo planes summed in f64.
+            auto tile_values = [&](int t0, long long (&v)[16]) {
+                uint32_t r[P][16];
 #pragma unroll
-            for (int p = 0; p < P; ++p) tmem_ld16(tbase + p * NT + t0, r[p]);
-            tmem_wait_ld();
+                for (int p = 0; p < P; ++p) tmem_ld16(tbase + p * NT + t0, r[p]);
+                tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                if constexpr (WK == kWQ8) {
-                    v[j] = (long long)(int)r[0][j] * 65536ll + (long long)(int)r[1][j] * 256ll + (long long)(int)r[2][j];
-                } else {
-                    v[j] = __double_as_longlong((double)__uint_as_float(r[0][j]) + (double)__uint_as_float(r[1][j]));
-                }
-            }
-        };
-        bool do_final = !split_k;
-        long long* part = reinterpret_cast<long long*>(a.acc);
-        if (split_k) {
-            // store this split's values (plain coalesced stores), then the last
-            // CTA of the tile sums the splits in split order
-            for (int t0 = 0; t0 < NT; t0 += 16) {
-                long long v[16];
-                tile_values(t0, v);
-                if (ok && row < a.M) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int t = n0 + t0 + j;
-                        if (t < a.T) part[((size_t)split * kAccT + t) * a.M + row] = v[j];
-                    }
-                }
-            }
-            __threadfence();
-            epi_bar();
-            if (threadIdx.x == 64) {
-                const unsigned prev = atomicAdd(a.counters + (size_t)n_tile * gridDim.x + m_tile, 1u);
-                last_flag = prev == gridDim.z - 1;
-            }
-            epi_bar();
-            do_final = last_flag != 0;
-            if (do_final) __threadfence();
-        }
-        if (do_final) {
-            for (int t0 = 0; t0 < NT; t0 += 16) {
-                long long v[16];
-                if (!split_k) {
-                    tile_values(t0, v);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int t = min(n0 + t0 + j, a.T - 1);
-                        long long si = 0;
-                        double sd = 0.0;
-                        for (int s = 0; s < (int)gridDim.z; ++s) {
-                            const long long e = __ldcg(part + ((size_t)s * kAccT + t) * a.M + row);
-                            if constexpr (WK == kWQ8) si += e;
-                            else sd += __longlong_as_double(e);
-                        }
-                        v[j] = WK == kWQ8 ? si : __double_as_longlong(sd);
-                    }
-                }
-                float y[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int t = min(n0 + t0 + j, a.T - 1);
-                    if constexpr (WK == kWQ8) y[j] = __fmul_rn(ldexpf(__ll2float_rn(v[j]), a.exps[t] - 22), sc);
-                    else y[j] = (float)__longlong_as_double(v[j]);
-                }
-                if (!ok) continue;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int t = n0 + t0 + j;
-                    const bool live = t < a.T && row < a.M;
-                    if constexpr (EPI == kEpiSwiGLU) {
-                        const float up = __shfl_xor_sync(0xFFFFFFFFu, y[j], 1);
-                        if (live && (lane & 1) == 0) a.y[(size_t)t * a.ldy + (row >> 1)] = __fmul_rn(silu(y[j]), up);
-                    } else if constexpr (EPI == kEpiResid) {
-                        if (live) {
-                            const size_t o = (size_t)t * a.ldy + row;
-                            a.y[o] = __fadd_rn(a.resid[o], y[j]);
-                        }
-                    } else if constexpr (EPI == kEpiArgmax) {
-                        if (live && a.y) a.y[(size_t)t * a.ldy + row] = y[j];
-                        unsigned long long key = live ? argmax_key(y[j], (uint32_t)row) : 0ull;
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) {
-                            const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, key, o);
-                            key = other > key ? other : key;
-                        }
-                        if (lane == 0 && key) atomicMax(&best_s[t0 + j], key);
+                for (int jj = 0; jj < 16; ++jj) {
+                    if constexpr (WK == kWQ8) {
+                        v[jj] = (long long)(int)r[0][jj] * 65536ll + (long long)(int)r[1][jj] * 256ll +
+                                (long long)(int)r[2][jj];
                     } else {
-                        if (live) a.y[(size_t)t * a.ldy + row] = y[j];
+                        v[jj] = __double_as_longlong((double)__uint_as_float(r[0][jj]) +
+                                                     (double)__uint_as_float(r[1][jj]));
                     }
                 }
-            }
-            if constexpr (EPI == kEpiArgmax) {
+            };
+            auto release_acc = [&]() {  // TMEM buffer free for the MMA of the unit after next
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+            };
+            bool do_final = !split_k;
+            long long* part = reinterpret_cast<long long*>(a.acc);
+            if (split_k) {
+                // store this unit's values (plain coalesced stores); the last unit
+                // of the tile to finish sums the splits in split order
+                for (int t0 = 16 * h; t0 < NT; t0 += 32) {
+                    long long v[16];
+                    tile_values(t0, v);
+                    if (ok && row < a.M) {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) {
+                            const int t = n0 + t0 + jj;
+                            if (t < a.T) part[((size_t)sp * kAccT + t) * a.M + row] = v[jj];
+                        }
+                    }
+                }
+                release_acc();
+                __threadfence();
                 epi_bar();
-                const int e = threadIdx.x - 64;
-                for (int t = e; t < NT; t += 128)
-                    if (n0 + t < a.T && best_s[t]) atomicMax(a.argmax_keys + n0 + t, best_s[t]);
+                if (threadIdx.x == 64) {
+                    const unsigned prev = atomicAdd(a.counters + (size_t)nt * m_tiles + mt, 1u);
+                    last_flag = prev == (unsigned)(splits - 1);
+                }
+                epi_bar();
+                do_final = last_flag != 0;
+                if (do_final) __threadfence();
             }
-            if (split_k && threadIdx.x == 64) a.counters[(size_t)n_tile * gridDim.x + m_tile] = 0u;
+            if (do_final) {
+                for (int t0 = 16 * h; t0 < NT; t0 += 32) {
+                    long long v[16];
+                    if (!split_k) {
+                        tile_values(t0, v);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) {
+                            const int t = min(n0 + t0 + jj, a.T - 1);
+                            long long si = 0;
+                            double sd = 0.0;
+                            for (int s = 0; s < splits; ++s) {
+                                const long long e = __ldcg(part + ((size_t)s * kAccT + t) * a.M + row);
+                                if constexpr (WK == kWQ8) si += e;
+                                else sd += __longlong_as_double(e);
+                            }
+                            v[jj] = WK == kWQ8 ? si : __double_as_longlong(sd);
+                        }
+                    }
+                    // every load of the chunk is issued before any store (the
+                    // output may alias the residual, which blocks reordering)
+                    float y[16], rs[16];
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int t = min(n0 + t0 + jj, a.T - 1);
+                        if constexpr (WK == kWQ8) y[jj] = __ldg(a.xscale + t);
+                        if constexpr (EPI == kEpiResid) rs[jj] = a.resid[(size_t)t * a.ldy + row];
+                    }
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        if constexpr (WK == kWQ8) y[jj] = __fmul_rn(__fmul_rn(__ll2float_rn(v[jj]), y[jj]), sc);
+                        else y[jj] = (float)__longlong_as_double(v[jj]);
+                    }
+                    if (!ok) continue;
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int t = n0 + t0 + jj;
+                        const bool live = t < a.T && row < a.M;
+                        if constexpr (EPI == kEpiSwiGLU) {
+                            const float up = __shfl_xor_sync(0xFFFFFFFFu, y[jj], 1);
+                            if (live && (lane & 1) == 0)
+                                a.y[(size_t)t * a.ldy + (row >> 1)] = __fmul_rn(silu(y[jj]), up);
+                        } else if constexpr (EPI == kEpiResid) {
+                            if (live) a.y[(size_t)t * a.ldy + row] = __fadd_rn(rs[jj], y[jj]);
+                        } else if constexpr (EPI == kEpiArgmax) {
+                            if (live && a.y) a.y[(size_t)t * a.ldy + row] = y[jj];
+                            // warp argmax over 32 rows with two redux.sync: the
+                            // largest orderable value, then the lowest row among
+                            // lanes holding it (key low word = ~row)
+                            const unsigned long long key = live ? argmax_key(y[jj], (uint32_t)row) : 0ull;
+                            const uint32_t hi = (uint32_t)(key >> 32);
+                            const uint32_t mx = __reduce_max_sync(0xFFFFFFFFu, hi);
+                            const uint32_t lo = __reduce_max_sync(0xFFFFFFFFu, hi == mx ? (uint32_t)key : 0u);
+                            const unsigned long long best = ((unsigned long long)mx << 32) | lo;
+                            if (lane == 0 && mx) atomicMax(&best_s[t0 + jj], best);
+                        } else {
+                            if (live) a.y[(size_t)t * a.ldy + row] = y[jj];
+                        }
+                    }
+                }
+                if (!split_k) release_acc();
+                if constexpr (EPI == kEpiArgmax) {
+                    epi_bar();
+                    const int e = threadIdx.x - 64;  // 0 .. 255
+                    for (int t = e; t < NT; t += 256) {
+                        if (n0 + t < a.T && best_s[t]) atomicMax(a.argmax_keys + n0 + t, best_s[t]);
+                        best_s[t] = 0ull;
+                    }
+                    epi_bar();
+                }
+                if (split_k && threadIdx.x == 64) a.counters[(size_t)nt * m_tiles + mt] = 0u;
+            }
         }
     }
 
@@ -317,15 +412,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                      : "memory");
     }
 }
+
 
 // --------------------------------------------------- activation planes
 
 template <int WK>
 __global__ void __launch_bounds__(256) prep_planes_kernel(PlanesArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int t = blockIdx.x;
     const int K = a.K;
     const float* xr = a.x + (size_t)t * a.ldx;
@@ -366,7 +464,7 @@ __global__ void __launch_bounds__(256) prep_planes_kernel(PlanesArgs a) {
         __syncthreads();
         int e = 0;
         if (bcast > 0.0f) frexpf(bcast, &e);  // max|x| < 2^e
-        if (threadIdx.x == 0) a.exps[t] = e;
+        if (threadIdx.x == 0) a.xscale[t] = ldexpf(1.0f, e - 22);  // exact power of two
         int8_t* p0 = reinterpret_cast<int8_t*>(a.planes) + (size_t)t * K;
         const size_t plane = (size_t)a.t_pad * K;
         for (int k = threadIdx.x; k < K; k += 256) {
@@ -392,22 +490,32 @@ __global__ void __launch_bounds__(256) prep_planes_kernel(PlanesArgs a) {
     }
 }
 
-template <int WK, int NT, int EPI>
-void launch_tile(const TcLaunch& L, cudaStream_t st) {
+template <int WK, int NT>
+constexpr size_t tile_smem() {
     constexpr int P = WK == kWQ8 ? 3 : 2;
     constexpr int STAGE = kBM * kKB + P * NT * kKB;
     constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
-    const size_t smem = (size_t)STAGES * STAGE + 1024 + (2 * STAGES + 1) * 8 + 16;
+    return (size_t)STAGES * STAGE + 1024 + (2 * STAGES + 4) * 8 + 16;
+}
+
+template <int WK, int NT>
+void prepare_tile() {
+    configure_kernel((const void*)tc_gemm_kernel<WK, NT, kEpiNone>, tile_smem<WK, NT>());
+    configure_kernel((const void*)tc_gemm_kernel<WK, NT, kEpiResid>, tile_smem<WK, NT>());
+    configure_kernel((const void*)tc_gemm_kernel<WK, NT, kEpiSwiGLU>, tile_smem<WK, NT>());
+    configure_kernel((const void*)tc_gemm_kernel<WK, NT, kEpiArgmax>, tile_smem<WK, NT>());
+}
+
+template <int WK, int NT, int EPI>
+void launch_tile(const TcLaunch& L, cudaStream_t st) {
+    constexpr size_t smem = tile_smem<WK, NT>();
     auto kern = tc_gemm_kernel<WK, NT, EPI>;
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr[dev] = true;
-    }
-    dim3 grid(L.args.M / kBM, (L.args.T + NT - 1) / NT, L.splits);
-    kern<<<grid, kTcThreads, smem, st>>>(*L.tmA, *L.tmB, L.args);
+    // persistent: one CTA per SM (at most one per work unit) walks the units
+    TcArgs args = L.args;
+    args.splits = L.splits;
+    const int units = (args.M / kBM) * ((args.T + NT - 1) / NT) * L.splits;
+    const int grid = std::min(units, L.sms > 0 ? L.sms : 148);
+    launch_pdl(kern, grid, kTcThreads, smem, st, *L.tmA, *L.tmB, args);
 }
 
 template <int WK, int NT>
@@ -423,13 +531,21 @@ void launch_epi(const TcLaunch& L, cudaStream_t st) {
 }  // namespace
 
 int tc_tile_tokens(int wkind, int T) {
-    if (wkind == kWQ8) return T <= 16 ? 16 : (T <= 32 ? 32 : 64);
-    return T <= 16 ? 16 : (T <= 32 ? 32 : (T <= 64 ? 64 : 128));
+    if (T <= 16) return 16;
+    if (T <= 32) return 32;
+    return (wkind == kWQ8 || T <= 64) ? 64 : 128;
+}
+
+void prepare_tc_kernels() {
+    prepare_tile<kWQ8, 16>(); prepare_tile<kWQ8, 32>(); prepare_tile<kWQ8, 64>();
+    prepare_tile<kWBF16, 16>(); prepare_tile<kWBF16, 32>(); prepare_tile<kWBF16, 64>(); prepare_tile<kWBF16, 128>();
+    configure_kernel((const void*)prep_planes_kernel<kWQ8>, 0);
+    configure_kernel((const void*)prep_planes_kernel<kWBF16>, 0);
 }
 
 void launch_prep_planes(const PlanesArgs& a, cudaStream_t st) {
-    if (a.wkind == kWQ8) prep_planes_kernel<kWQ8><<<a.T, 256, 0, st>>>(a);
-    else prep_planes_kernel<kWBF16><<<a.T, 256, 0, st>>>(a);
+    if (a.wkind == kWQ8) launch_pdl(prep_planes_kernel<kWQ8>, a.T, 256, 0, st, a);
+    else launch_pdl(prep_planes_kernel<kWBF16>, a.T, 256, 0, st, a);
 }
 
 void launch_tc_gemm(const TcLaunch& L, cudaStream_t st) {
@@ -489,9 +605,12 @@ int tc_splits(int M, int T, int K, int wkind, int sms) {
     const int nt = tc_tile_tokens(wkind, T);
     const int tiles = (M / kBM) * ((T + nt - 1) / nt);
     const int nkb = K * (wkind == kWQ8 ? 1 : 2) / kKB;
+    // The last unit of a tile re-reads splits x NT partial values per row on
+    // its critical path, so split only narrow tiles, and only a few ways.
+    if (nt > 16) return 1;
     int s = (sms + tiles - 1) / tiles;
     s = std::min(s, std::max(1, nkb / 2));  // at least two K blocks per split
-    return std::max(1, std::min(s, 16));
+    return std::max(1, std::min(s, 4));
 }
 
 }  // namespace zc

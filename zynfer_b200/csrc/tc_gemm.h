@@ -19,7 +19,7 @@ struct PlanesArgs {
     const float* norm_w;  // nullable
     float eps;
     void* planes;
-    int* exps;  // int8 only
+    float* xscale;  // int8 only: 2^(e - 22) per row
 };
 
 constexpr int kAccT = 64;  // split-K accumulator rows per plane (split-K only for T <= 64)
@@ -29,7 +29,7 @@ struct TcArgs {
     int wkind;
     int epi;
     const float* scale;  // [M] (int8) or nullptr
-    const int* exps;     // [T] (int8)
+    const float* xscale; // [T] (int8): 2^(e - 22) of each activation row
     float* y;            // [T][ldy]
     int ldy;
     const float* resid;
@@ -37,6 +37,7 @@ struct TcArgs {
     void* acc;               // split-K accumulator [P][kAccT][M] (zero between uses)
     unsigned int* counters;  // split-K tile counters (zero between uses)
     uint32_t* err;
+    int splits;              // K splits per (M, N) tile (set by the launcher)
 };
 
 struct TcLaunch {
@@ -44,6 +45,7 @@ struct TcLaunch {
     const CUtensorMap* tmB;  // planes [P * t_pad][K], box 128 B x NT rows
     TcArgs args;
     int splits;
+    int sms;  // persistent grid size
 };
 
 int tc_tile_tokens(int wkind, int T);  // NT: tokens per N tile
