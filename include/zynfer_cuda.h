@@ -162,6 +162,27 @@ ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, c
  * tcgen05 tensor cores above), "gemv", "tcgen05", or "simt" (the CUDA-core
  * tiled GEMM, kept for comparisons). Applies to later calls of this context. */
 ZYNFER_CU_API int zynfer_cu_set_linear_path(ZynferCuCtx *ctx, const char *path);
+/* Allocation-free int8 linear (no counterpart in the reference; an addition
+ * of this backend). Same result as zynfer_cu_linear with ZYNFER_CU_W_Q8:
+ * y[b][i] = (W[i,:] . x[b,:]) * scale[i], computed on the tcgen05 path, for
+ * callers that cannot call cudaMalloc: an embedding application that owns
+ * every device allocation, a custom allocator that must not be bypassed, or
+ * code running where allocation is forbidden. It takes no context and calls
+ * no cudaMalloc, cudaFree or allocating library routine; all pointers are
+ * caller-owned device memory and `stream` is a cudaStream_t (NULL = the
+ * default stream). Its only scratch (the activations' int8 digit planes and
+ * row scales, 768 KiB) is a file-scope device array that every GPU loading
+ * the library holds until the process exits.
+ * Limits: batch <= ZYNFER_CU_STATIC_MAX_ROWS, k <= ZYNFER_CU_STATIC_MAX_K,
+ * k and m multiples of 128; otherwise ZYNFER_CU_INVALID.
+ * The first call on a device resolves the array's device address and sets
+ * kernel attributes on that device; make it before any stream capture. All
+ * calls share the array, so calls that overlap on the GPU (other streams,
+ * other threads) race: serialise them. */
+#define ZYNFER_CU_STATIC_MAX_ROWS 64
+#define ZYNFER_CU_STATIC_MAX_K 4096
+ZYNFER_CU_API int zynfer_cu_linear_q8_static(const int8_t *w, const float *scale, const float *x,
+                                             uint32_t batch, uint32_t m, uint32_t k, float *y, void *stream);
 /* packRowQ8 (ops.zig:145-162) on the device, bit-exact. */
 ZYNFER_CU_API int zynfer_cu_pack_q8(ZynferCuCtx *ctx, const float *w, uint32_t rows, uint32_t cols, int8_t *q,
                       float *scale);

@@ -101,6 +101,7 @@ _SIGS = {
     "zynfer_cu_block_forward": (C.c_int, [VP, U32, U32, VP, U32, VP]),
     "zynfer_cu_linear": (C.c_int, [VP, C.c_int, VP, VP, VP, U32, U32, U32, VP]),
     "zynfer_cu_set_linear_path": (C.c_int, [VP, C.c_char_p]),
+    "zynfer_cu_linear_q8_static": (C.c_int, [VP, VP, VP, U32, U32, U32, VP, VP]),
     "zynfer_cu_pack_q8": (C.c_int, [VP, VP, U32, U32, VP, VP]),
     "zynfer_cu_rmsnorm": (C.c_int, [VP, VP, VP, U32, U32, C.c_float, VP]),
     "zynfer_cu_set_timing": (C.c_int, [VP, C.c_int]),
@@ -138,6 +139,19 @@ def _ptr(a) -> C.c_void_p | None:
     if hasattr(a, "data_ptr"):  # torch tensor (device pointer)
         return C.c_void_p(a.data_ptr())
     return a.ctypes.data_as(C.c_void_p)
+
+
+STATIC_MAX_ROWS, STATIC_MAX_K = 64, 4096
+
+
+def linear_q8_static(w, scale, x, batch: int, m: int, k: int, y, stream=None):
+    """zynfer_cu_linear_q8_static: the int8 linear that allocates nothing (no
+    context; device pointers; scratch in a library-owned device array)."""
+    if stream is not None and hasattr(stream, "cuda_stream"):  # a torch.cuda.Stream
+        stream = int(stream.cuda_stream)
+    rc = lib().zynfer_cu_linear_q8_static(_ptr(w), _ptr(scale), _ptr(x), batch, m, k, _ptr(y), _ptr(stream))
+    if rc != OK:
+        raise _ERRORS.get(rc, CudaError)(f"zynfer_cu_linear_q8_static failed with status {rc}")
 
 
 @dataclass
