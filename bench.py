@@ -217,8 +217,10 @@ def run_ours(args):
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.2)
+    torch.cuda.profiler.start()  # a profiler run with --profile-from-start off sees the timed steps only
     out, dev_ms = model.generate(slots, nxt, args.steps)
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     clk = clocks.stop()
     barrier()
     nxt = out[-1].tolist()

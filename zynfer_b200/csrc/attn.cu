@@ -12,231 +12,382 @@ namespace {
 
 // ------------------------------------------------------------- decode
 //
-// Grid (split, kv_head, batch row); 128 threads. Each CTA owns `chunk`
-// positions of one sequence's K/V for one kv head and both query heads of its
-// GQA group. K/V arrive by untiled bulk copies (cp.async.bulk, 4 KB per
-// 16-token block and head) into a 4-stage shared-memory ring of 32-token
-// stages, completed on mbarriers; warps then compute scores and an online
-// softmax over their 8 tokens per stage (4 lanes per token, 32 dims each).
-// The CTA writes a partial (max, sum, acc[d]) per query head; the last CTA of
-// a (row, kv head) to finish (atomic counter) merges the splits:
+// Persistent and warp-granular. The work of one launch is the list of
+// (batch row, kv head, 16-token KV block) triples, row-major; every warp of
+// the grid takes an equal contiguous range of it (at least
+// kMinBlocksPerWarp), so each block of K/V is read exactly once and all
+// warps stream the same number of bytes whatever the context lengths. A warp
+// owns a private ring of kRing 8 KB slots (K then V of one block and head)
+// filled by cp.async.bulk on per-slot mbarriers; there is no barrier between
+// warps in the main loop.
+//
+// Per block, on the tensor cores (mma.sync m16n8k16, bf16 in, f32 out):
+//   S[16 tok][8] = K[16 tok][128] . Qcols[128][8], columns (h0 hi, h0 lo,
+//       h1 hi, h1 lo, 0...): q is split into two bf16 terms, q = hi + lo,
+//       |q - hi - lo| <= 2^-18 |q|, and K is exact bf16, so every product is
+//       exact and the dot products carry f32 accuracy;
+//   online softmax per query head in f32 (max, exp, sum);
+//   O[4 rows][128] += P[4 rows][16 tok] . V[16 tok][128], rows (h0 hi, h0 lo,
+//       h1 hi, h1 lo): p is split the same way.
+// A range boundary inside a (row, kv head) leaves partial results
+// (max, sum, acc[d]) per query head; the last warp to finish one (atomic
+// counter) merges them in segment order:
 //   m = max m_s,  l = sum l_s e^(m_s - m),  o = sum acc_s e^(m_s - m) / l.
-constexpr int kD = 128, kG = 2, kStageTok = 32, kStages = 4, kDecThreads = 128;
-constexpr int kBlockElems = kKvBlock * kD;                 // 2048 bf16 = 4 KB
-constexpr int kStageElems = kStageTok * kD;                // per K (or V) stage
+//
+// KV blocks are stored with their 16-byte chunks XOR-swizzled by token
+// (kv_swizzle), so the ldmatrix reads of K rows and the transposing reads of
+// V rows hit 32 distinct banks.
+constexpr int kD = 128, kG = 2;
+constexpr int kDecWarps = 8, kDecThreads = kDecWarps * kWarp;
+constexpr int kRing = 3;                                     // slots per warp
+constexpr int kBlockElems = kKvBlock * kD;                   // 2048 bf16 = 4 KB
+constexpr int kBlockBytes = kBlockElems * 2;
+constexpr int kSlotBytes = 2 * kBlockBytes;                  // K + V
+constexpr int kMaxBatch = 1024;
+constexpr size_t kRingBytes = (size_t)kDecWarps * kRing * kSlotBytes;
+constexpr size_t kDecodeSmem = kRingBytes + kDecWarps * kRing * sizeof(uint64_t) + (kMaxBatch + 1) * sizeof(int);
+static_assert(kD == 128 && kKvBlock == 16, "the fragment mapping assumes 16-token blocks of 128 dims");
 
-__global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(AttnDecodeArgs a) {
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    uint16_t* ks = reinterpret_cast<uint16_t*>(smem_raw);            // [kStages][32][128]
-    uint16_t* vs = ks + kStages * kStageElems;                        // [kStages][32][128]
-    uint64_t* full = reinterpret_cast<uint64_t*>(vs + kStages * kStageElems);
-    __shared__ float red_m[4][kG], red_l[4][kG];
-    __shared__ __align__(16) float red_acc[4][kG][kD];
-    __shared__ int is_last;
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+// D = A . B + D for one m16n8k16 tile; A rows 8..15 are zero when a1 = a3 = 0.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// One bf16 term of x: the rounded value (lo_part = 0) or the rounded remainder.
+__device__ __forceinline__ uint32_t bf16_term(float x, bool lo_part) {
+    const uint16_t hi = f32_to_bf16_rne(x);
+    if (!lo_part) return hi;
+    return f32_to_bf16_rne(x - __uint_as_float((uint32_t)hi << 16));
+}
+__device__ __forceinline__ uint32_t pack_terms(float x0, float x1, bool lo_part) {
+    return bf16_term(x0, lo_part) | (bf16_term(x1, lo_part) << 16);
+}
+
+struct BlockCursor {
+    int b, head, blk, nblk;
+};
+
+__global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    unsigned char* ring = smem_raw + (size_t)warp * kRing * kSlotBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kRingBytes) + warp * kRing;
+    int* pref = reinterpret_cast<int*>(smem_raw + kRingBytes + kDecWarps * kRing * sizeof(uint64_t));
+    constexpr unsigned kAll = 0xFFFFFFFFu;
 
     pdl_launch_dependents();
-    pdl_wait();
-    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
-    const int seq = a.seq_of[b];
-    const int kv_len = a.positions[b] + 1;
-    const int nsplit = (kv_len + a.chunk - 1) / a.chunk;
-    if (split >= nsplit) return;
-    const int t0 = split * a.chunk;
-    const int t1 = min(t0 + a.chunk, kv_len);
-    const int nstage = (t1 - t0 + kStageTok - 1) / kStageTok;
-    const int last_blk = (kv_len - 1) / kKvBlock;
-    const int* table = a.block_table + (size_t)seq * a.max_blocks;
-
-    if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    const int B = a.B;
+    const int max_len = a.max_blocks * kKvBlock;
+    // Row-major prefix of KV block counts. Positions and block tables are
+    // written before the step starts, never by the kernels this launch may
+    // overlap, so they are read before griddepcontrol.wait.
+    if (warp == 0) {
+        int carry = 0;
+        for (int base = 0; base < B; base += kWarp) {
+            const int b = base + lane;
+            int n = 0;
+            if (b < B) {
+                const int len = a.positions[b] + 1;
+                if ((len < 1 || len > max_len) && a.err) atomicOr(a.err, kErrBadIndex);
+                n = (min(max(len, 1), max_len) + kKvBlock - 1) / kKvBlock;
+            }
+            int x = n;
+#pragma unroll
+            for (int o = 1; o < kWarp; o <<= 1) {
+                const int y = __shfl_up_sync(kAll, x, o);
+                if (lane >= o) x += y;
+            }
+            if (b < B) pref[b + 1] = carry + x;
+            carry += __shfl_sync(kAll, x, kWarp - 1);
+        }
+        if (lane == 0) pref[0] = 0;
+    }
+    if (lane == 0) {
+        for (int s = 0; s < kRing; ++s) mbar_init(&full[s], 1);
         fence_barrier_init();
     }
     __syncthreads();
 
-    auto issue = [&](int s) {  // thread 0 only
-        const int buf = s % kStages;
-        const int bi0 = (t0 + s * kStageTok) / kKvBlock;
-        uint32_t bytes = 0;
-        int blks[2];
-        for (int j = 0; j < 2; ++j) {
-            const int bi = bi0 + j;
-            blks[j] = -1;
-            if (bi <= last_blk && bi < a.max_blocks) {
-                const int blk = table[bi];
-                if (blk >= 0 && blk < a.n_pool_blocks) {
-                    blks[j] = blk;
-                    bytes += 2 * kBlockElems * 2;
-                } else if (a.err) {
-                    atomicOr(a.err, kErrBadIndex);
-                }
-            }
+    const int total = pref[B] * a.n_kv;
+    const int nwarps = gridDim.x * kDecWarps;
+    const int per = max((total + nwarps - 1) / nwarps, kMinBlocksPerWarp);
+    const int w = warp * gridDim.x + blockIdx.x;  // active warps spread over all SMs
+    const int lo = w * per;
+    const int n = min(total, lo + per) - lo;
+    if (n <= 0) return;
+
+    auto locate = [&](int f, BlockCursor& c) {
+        int l = 0, h = B - 1;
+        while (l < h) {
+            const int mid = (l + h + 1) / 2;
+            if (a.n_kv * pref[mid] <= f) l = mid;
+            else h = mid - 1;
         }
-        mbar_arrive_expect_tx(&full[buf], bytes);
-        for (int j = 0; j < 2; ++j) {
-            if (blks[j] < 0) continue;
-            const uint16_t* kp = a.kv_layer + (((size_t)blks[j] * 2 + 0) * a.n_kv + kvh) * kBlockElems;
-            const uint16_t* vp = a.kv_layer + (((size_t)blks[j] * 2 + 1) * a.n_kv + kvh) * kBlockElems;
-            bulk_g2s(ks + buf * kStageElems + j * kBlockElems, kp, kBlockElems * 2, &full[buf]);
-            bulk_g2s(vs + buf * kStageElems + j * kBlockElems, vp, kBlockElems * 2, &full[buf]);
-        }
+        c.b = l;
+        c.nblk = pref[l + 1] - pref[l];
+        const int r = f - a.n_kv * pref[l];
+        c.head = r / c.nblk;
+        c.blk = r % c.nblk;
     };
-    if (tid == 0)
-        for (int s = 0; s < min(kStages, nstage); ++s) issue(s);
-
-    // lane -> (token slot tq, dim quarter j): dims 32 i + 8 j + e, i = 0..3, e = 0..7
-    const int tq = lane / 4, j = lane % 4;
-    float q[kG][32];
-#pragma unroll
-    for (int g = 0; g < kG; ++g) {
-        const float* qp = a.q + ((size_t)b * a.n_q + kvh * kG + g) * kD;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float4 v0 = *reinterpret_cast<const float4*>(qp + 32 * i + 8 * j);
-            const float4 v1 = *reinterpret_cast<const float4*>(qp + 32 * i + 8 * j + 4);
-            q[g][8 * i + 0] = v0.x; q[g][8 * i + 1] = v0.y; q[g][8 * i + 2] = v0.z; q[g][8 * i + 3] = v0.w;
-            q[g][8 * i + 4] = v1.x; q[g][8 * i + 5] = v1.y; q[g][8 * i + 6] = v1.z; q[g][8 * i + 7] = v1.w;
+    auto advance = [&](BlockCursor& c) {
+        if (++c.blk < c.nblk) return;
+        c.blk = 0;
+        if (++c.head < a.n_kv) return;
+        c.head = 0;
+        do {
+            ++c.b;
+            c.nblk = c.b < B ? pref[c.b + 1] - pref[c.b] : 1;
+        } while (c.nblk == 0);
+    };
+    auto issue = [&](const BlockCursor& c, int s) {  // lane 0
+        const int seq = a.seq_of[c.b];
+        int id = a.block_table[(size_t)seq * a.max_blocks + c.blk];
+        if (id < 0 || id >= a.n_pool_blocks) {
+            if (a.err) atomicOr(a.err, kErrBadIndex);
+            id = 0;  // keep the pipeline whole; the error word reports the launch
         }
+        const uint16_t* kp = a.kv_layer + (((size_t)id * 2) * a.n_kv + c.head) * kBlockElems;
+        const uint16_t* vp = kp + (size_t)a.n_kv * kBlockElems;
+        unsigned char* dst = ring + s * kSlotBytes;
+        mbar_arrive_expect_tx(&full[s], kSlotBytes);
+        bulk_g2s(dst, kp, kBlockBytes, &full[s]);
+        bulk_g2s(dst + kBlockBytes, vp, kBlockBytes, &full[s]);
+    };
+
+    // Fill the ring. Only the last block of a row receives this step's K/V
+    // (from the kernel before this one), so the fill stops there until
+    // griddepcontrol.wait has returned.
+    BlockCursor ci, cc;
+    locate(lo, ci);
+    cc = ci;
+    const int first = min(kRing, n);
+    int issued = 0;
+    while (issued < first && ci.blk != ci.nblk - 1) {
+        if (lane == 0) issue(ci, issued);
+        advance(ci);
+        ++issued;
     }
+    pdl_wait();
+    for (; issued < first; ++issued) {
+        if (lane == 0) issue(ci, issued);
+        advance(ci);
+    }
+
+    const int g = lane >> 2, t = lane & 3;
+    const int mi = lane >> 3, ri = lane & 7;
+    const int tok_a = ri + (mi & 1) * 8;                // row this lane addresses for ldmatrix
+    const int hsel = (lane >> 3) & 1;                   // head of this lane's P / O rows (lanes < 16)
     const float scale = 1.0f / sqrtf((float)kD);
-    float m[kG], l[kG], acc[kG][32];
-#pragma unroll
-    for (int g = 0; g < kG; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) acc[g][e] = 0.0f;
-    }
 
-    for (int s = 0; s < nstage; ++s) {
-        const int buf = s % kStages;
-        const bool ok = mbar_wait_bounded(&full[buf], (uint32_t)((s / kStages) & 1), a.err);
-        if (__syncthreads_or(!ok)) return;  // timed out: error flag set, nothing merged
-        const int tok = t0 + s * kStageTok + warp * 8 + tq;
-        const bool valid = tok < t1;
-        const uint16_t* kr = ks + buf * kStageElems + (warp * 8 + tq) * kD;
-        const uint16_t* vr = vs + buf * kStageElems + (warp * 8 + tq) * kD;
-        float dot[kG] = {0.0f, 0.0f};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint4 kv = *reinterpret_cast<const uint4*>(kr + 32 * i + 8 * j);
-            const float kf[8] = {bf16lo(kv.x), bf16hi(kv.x), bf16lo(kv.y), bf16hi(kv.y),
-                                 bf16lo(kv.z), bf16hi(kv.z), bf16lo(kv.w), bf16hi(kv.w)};
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-#pragma unroll
-                for (int g = 0; g < kG; ++g) dot[g] = fmaf(q[g][8 * i + e], kf[e], dot[g]);
-        }
-        float p[kG];
-#pragma unroll
-        for (int g = 0; g < kG; ++g) {
-            dot[g] += __shfl_xor_sync(0xFFFFFFFFu, dot[g], 1);
-            dot[g] += __shfl_xor_sync(0xFFFFFFFFu, dot[g], 2);
-            const float sc = valid ? dot[g] * scale : -INFINITY;
-            float mx = sc;
-            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 4));
-            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
-            const float m_new = fmaxf(m[g], mx);
-            const float corr = m_new == -INFINITY ? 1.0f : expf(m[g] - m_new);
-            p[g] = valid ? expf(sc - m_new) : 0.0f;
-            l[g] = l[g] * corr + p[g];
-            m[g] = m_new;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) acc[g][e] *= corr;
-        }
-        if (valid) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint4 vv = *reinterpret_cast<const uint4*>(vr + 32 * i + 8 * j);
-                const float vf[8] = {bf16lo(vv.x), bf16hi(vv.x), bf16lo(vv.y), bf16hi(vv.y),
-                                     bf16lo(vv.z), bf16hi(vv.z), bf16lo(vv.w), bf16hi(vv.w)};
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-#pragma unroll
-                    for (int g = 0; g < kG; ++g) acc[g][8 * i + e] = fmaf(p[g], vf[e], acc[g][8 * i + e]);
-            }
-        }
-        __syncthreads();  // stage buffer free
-        if (tid == 0 && s + kStages < nstage) issue(s + kStages);
-    }
+    uint32_t qf[8][2];
+    float acc[16][4];
+    float m_run = -INFINITY, l_run = 0.0f;
+    int kv_len = 0;
+    bool seg_start = true;
 
-    // reduce the 8 token slots of each warp (lanes with equal j)
+    for (int i = 0; i < n; ++i) {
+        const int s = i % kRing;
+        if (seg_start) {
+            // B operand of S: column g = (head g/2, term g%2), k = dims 16 ks + 2t (+1, +8, +9)
+            if (g < 4) {
+                const float* qp = a.q + ((size_t)cc.b * a.n_q + cc.head * kG + (g >> 1)) * kD;
+                const bool lo_part = g & 1;
 #pragma unroll
-    for (int g = 0; g < kG; ++g) {
+                for (int ks = 0; ks < 8; ++ks) {
+                    const float2 x0 = *reinterpret_cast<const float2*>(qp + 16 * ks + 2 * t);
+                    const float2 x1 = *reinterpret_cast<const float2*>(qp + 16 * ks + 2 * t + 8);
+                    qf[ks][0] = pack_terms(x0.x, x0.y, lo_part);
+                    qf[ks][1] = pack_terms(x1.x, x1.y, lo_part);
+                }
+            } else {
 #pragma unroll
-        for (int o = 4; o < 32; o <<= 1) l[g] += __shfl_xor_sync(0xFFFFFFFFu, l[g], o);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            float v = acc[g][e];
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-            acc[g][e] = v;
-        }
-    }
-    if (lane < 4) {
-#pragma unroll
-        for (int g = 0; g < kG; ++g) {
-            if (lane == 0) {
-                red_m[warp][g] = m[g];
-                red_l[warp][g] = l[g];
+                for (int ks = 0; ks < 8; ++ks) qf[ks][0] = qf[ks][1] = 0u;
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+            m_run = -INFINITY;
+            l_run = 0.0f;
+            kv_len = min(max(a.positions[cc.b] + 1, 1), max_len);
+            seg_start = false;
+        }
+        const bool ok = __all_sync(kAll, mbar_wait_bounded(&full[s], (uint32_t)((i / kRing) & 1), a.err));
+        if (!ok) {
+            // let every copy still in flight land before the warp leaves
+            if (lane == 0)
+                for (int j = i; j < min(n, i + kRing); ++j)
+                    mbar_wait_bounded(&full[j % kRing], (uint32_t)((j / kRing) & 1), nullptr);
+            __syncwarp();
+            return;
+        }
+        unsigned char* kb = ring + s * kSlotBytes;
+        const int nv = min(kKvBlock, kv_len - cc.blk * kKvBlock);  // valid tokens in this block
+        if (nv < kKvBlock) {
+            // rows past the end of the sequence: p = 0 there, but 0 * (stale NaN) is NaN
+            uint4* vrow = reinterpret_cast<uint4*>(kb + kBlockBytes + nv * kD * 2);
+            for (int x = lane; x < (kKvBlock - nv) * (kD * 2 / 16); x += kWarp) vrow[x] = make_uint4(0, 0, 0, 0);
+            __syncwarp();
+        }
+
+        // S = K . Qcols
+        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const uint32_t kbase = smem_addr(kb), vbase = kbase + kBlockBytes;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) red_acc[warp][g][32 * i + 8 * lane + e] = acc[g][8 * i + e];
+        for (int ks = 0; ks < 8; ++ks) {
+            const int ch = 2 * ks + (mi >> 1);
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(kbase + tok_a * (kD * 2) + ((ch ^ ri) << 4), a0, a1, a2, a3);
+            mma_bf16(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
         }
-    }
-    __syncthreads();
-
-    // combine the 4 warps: thread = (g, dim); 2 x 128 = 256 > 128 threads, loop g
-    float* part = a.partial + (((size_t)b * a.n_kv + kvh) * a.max_splits + split) * kG * (kD + 2);
-    for (int g = 0; g < kG; ++g) {
-        float M = -INFINITY;
-        for (int w = 0; w < 4; ++w) M = fmaxf(M, red_m[w][g]);
-        float L = 0.0f, A = 0.0f;
-        for (int w = 0; w < 4; ++w) {
-            const float c = red_m[w][g] == -INFINITY ? 0.0f : expf(red_m[w][g] - M);
-            L += red_l[w][g] * c;
-            A += red_acc[w][g][tid] * c;
+        // lanes t = 0, 1 hold head t's scores for tokens g and g + 8
+        float s0 = 0.0f, s1 = 0.0f;
+        if (t < 2) {
+            s0 = g < nv ? (sc[0] + sc[1]) * scale : -INFINITY;
+            s1 = g + 8 < nv ? (sc[2] + sc[3]) * scale : -INFINITY;
         }
-        if (nsplit == 1) {
-            a.out[((size_t)b * a.n_q + kvh * kG + g) * kD + tid] = A / L;
-        } else {
-            float* pg = part + g * (kD + 2);
-            if (tid == 0) {
-                pg[0] = M;
-                pg[1] = L;
+        float mt = fmaxf(s0, s1);
+        mt = fmaxf(mt, __shfl_xor_sync(kAll, mt, 4));
+        mt = fmaxf(mt, __shfl_xor_sync(kAll, mt, 8));
+        mt = fmaxf(mt, __shfl_xor_sync(kAll, mt, 16));
+        const float m_new = fmaxf(m_run, mt);
+        if (__any_sync(kAll, m_new > m_run)) {
+            const float corr = expf(m_run - m_new);
+            l_run *= corr;
+            const float ca = __shfl_sync(kAll, corr, hsel);
+#pragma unroll
+            for (int nt = 0; nt < 16; ++nt) {
+                acc[nt][0] *= ca;
+                acc[nt][1] *= ca;
             }
-            pg[2 + tid] = A;
+            m_run = m_new;
         }
-    }
-    if (nsplit == 1) return;
+        const float p0 = expf(s0 - m_run), p1 = expf(s1 - m_run);
+        l_run += p0 + p1;
 
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const unsigned prev = atomicAdd(a.counters + (size_t)b * a.n_kv + kvh, 1u);
-        is_last = prev == (unsigned)(nsplit - 1);
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    const float* base = a.partial + ((size_t)b * a.n_kv + kvh) * a.max_splits * kG * (kD + 2);
-    for (int g = 0; g < kG; ++g) {
-        float M = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(base + (sp * kG + g) * (kD + 2)));
-        float L = 0.0f, A = 0.0f;
-        for (int sp = 0; sp < nsplit; ++sp) {
-            const float* pg = base + (sp * kG + g) * (kD + 2);
-            const float ms = __ldcg(pg);
-            const float c = ms == -INFINITY ? 0.0f : expf(ms - M);
-            L += __ldcg(pg + 1) * c;
-            A += __ldcg(pg + 2 + tid) * c;
+        // P as the A operand: lane (g < 4, t) holds row g = (head g/2, term g%2)
+        // at tokens 2t, 2t+1 (a0) and 2t+8, 2t+9 (a2); p(h, tok) sits in lane
+        // 4 (tok % 8) + h, register p0 (tok < 8) or p1.
+        const int src0 = 8 * t + hsel, src1 = src0 + 4;
+        const float x0 = __shfl_sync(kAll, p0, src0), x8 = __shfl_sync(kAll, p1, src0);
+        const float x1 = __shfl_sync(kAll, p0, src1), x9 = __shfl_sync(kAll, p1, src1);
+        uint32_t pa0 = 0u, pa2 = 0u;
+        if (lane < 16) {
+            pa0 = pack_terms(x0, x1, g & 1);
+            pa2 = pack_terms(x8, x9, g & 1);
         }
-        a.out[((size_t)b * a.n_q + kvh * kG + g) * kD + tid] = A / L;
+        // O += P . V, two 8-dim tiles per transposing ldmatrix
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+            const int ch = 2 * np + (mi >> 1);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_trans(vbase + tok_a * (kD * 2) + ((ch ^ ri) << 4), b0, b1, b2, b3);
+            mma_bf16(acc[2 * np], pa0, 0u, pa2, 0u, b0, b1);
+            mma_bf16(acc[2 * np + 1], pa0, 0u, pa2, 0u, b2, b3);
+        }
+        if (nv < kKvBlock) fence_proxy_async_smem();  // generic writes above, bulk copy next
+        __syncwarp();
+        if (i + kRing < n) {
+            if (lane == 0) issue(ci, s);
+            advance(ci);
+        }
+
+        if (cc.blk == cc.nblk - 1 || i == n - 1) {
+            // ---- end of this warp's share of (row b, kv head)
+            const int b = cc.b, head = cc.head;
+            float L = l_run;
+            L += __shfl_xor_sync(kAll, L, 4);
+            L += __shfl_xor_sync(kAll, L, 8);
+            L += __shfl_xor_sync(kAll, L, 16);
+            const float Lh = __shfl_sync(kAll, L, hsel);
+            const float Mh = __shfl_sync(kAll, m_run, hsel);
+#pragma unroll
+            for (int nt = 0; nt < 16; ++nt) {  // rows hi + lo of the same head
+                acc[nt][0] += __shfl_xor_sync(kAll, acc[nt][0], 4);
+                acc[nt][1] += __shfl_xor_sync(kAll, acc[nt][1], 4);
+            }
+            const bool writer = lane < 16 && (g & 1) == 0;  // lanes 0-3: head 0, 8-11: head 1
+            const int f0 = a.n_kv * pref[b] + head * cc.nblk;
+            const int fw = f0 / per, lw = (f0 + cc.nblk - 1) / per;
+            const int nseg = lw - fw + 1, seg = w - fw;
+            if (nseg == 1) {
+                if (writer) {
+                    float* op = a.out + ((size_t)b * a.n_q + head * kG + hsel) * kD + 2 * t;
+                    const float inv = 1.0f / Lh;
+#pragma unroll
+                    for (int nt = 0; nt < 16; ++nt)
+                        *reinterpret_cast<float2*>(op + nt * 8) = make_float2(acc[nt][0] * inv, acc[nt][1] * inv);
+                }
+            } else if (seg < a.max_segs && nseg <= a.max_segs) {
+                float* base = a.partial + ((size_t)b * a.n_kv + head) * a.max_segs * (kG * (kD + 2));
+                float* pg = base + (size_t)seg * (kG * (kD + 2)) + hsel * (kD + 2);
+                if (writer) {
+                    if (t == 0) {
+                        pg[0] = Mh;
+                        pg[1] = Lh;
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < 16; ++nt)
+                        *reinterpret_cast<float2*>(pg + 2 + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
+                }
+                __threadfence();
+                __syncwarp();
+                unsigned prev = 0;
+                if (lane == 0) prev = atomicAdd(a.counters + (size_t)b * a.n_kv + head, 1u);
+                prev = __shfl_sync(kAll, prev, 0);
+                if (prev == (unsigned)(nseg - 1)) {
+                    __threadfence();
+                    // merge: lane owns dims 4 lane .. 4 lane + 3 of both query heads
+#pragma unroll
+                    for (int h = 0; h < kG; ++h) {
+                        float M = -INFINITY;
+                        for (int sp = 0; sp < nseg; ++sp)
+                            M = fmaxf(M, __ldcg(base + (size_t)sp * (kG * (kD + 2)) + h * (kD + 2)));
+                        float Lm = 0.0f;
+                        float4 A = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        for (int sp = 0; sp < nseg; ++sp) {
+                            const float* ps = base + (size_t)sp * (kG * (kD + 2)) + h * (kD + 2);
+                            const float ms = __ldcg(ps);
+                            const float c = ms == -INFINITY ? 0.0f : expf(ms - M);
+                            Lm += __ldcg(ps + 1) * c;
+                            const float2 u0 = __ldcg(reinterpret_cast<const float2*>(ps + 2 + 4 * lane));
+                            const float2 u1 = __ldcg(reinterpret_cast<const float2*>(ps + 2 + 4 * lane + 2));
+                            A.x += u0.x * c;
+                            A.y += u0.y * c;
+                            A.z += u1.x * c;
+                            A.w += u1.y * c;
+                        }
+                        const float inv = 1.0f / Lm;
+                        float* op = a.out + ((size_t)b * a.n_q + head * kG + h) * kD + 4 * lane;
+                        *reinterpret_cast<float4*>(op) = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+                    }
+                    if (lane == 0) a.counters[(size_t)b * a.n_kv + head] = 0u;
+                }
+            } else if (lane == 0 && a.err) {
+                atomicOr(a.err, kErrBadIndex);
+            }
+            seg_start = true;
+        }
+        advance(cc);
     }
-    if (tid == 0) a.counters[(size_t)b * a.n_kv + kvh] = 0u;
 }
 
 // ------------------------------------------------------------ prefill
@@ -371,7 +522,6 @@ __global__ void __launch_bounds__(PTHREADS) attn_prefill_kernel(AttnPrefillArgs 
 
 }  // namespace
 
-constexpr size_t kDecodeSmem = (size_t)2 * kStages * kStageElems * 2 + kStages * sizeof(uint64_t);
 constexpr size_t kPrefillSmem = ((size_t)kD * PQ + kD * PK + PK * kD + PK * PQ + 2 * PQ) * sizeof(float);
 
 void prepare_attn_kernels() {
@@ -380,8 +530,7 @@ void prepare_attn_kernels() {
 }
 
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st) {
-    dim3 grid(a.max_splits, a.n_kv, a.B);
-    launch_pdl(attn_decode_kernel, grid, kDecThreads, kDecodeSmem, st, a);
+    launch_pdl(attn_decode_kernel, device_sm_count(), kDecThreads, kDecodeSmem, st, a);
 }
 
 void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st) {

@@ -10,6 +10,15 @@ namespace zc {
 constexpr int kWarp = 32;
 constexpr int kKvBlock = 16;  // tokens per paged KV block
 
+// Element index of (token t, dim e) inside one paged block of K (or V) for
+// one kv head: 16 rows of 128 bf16 (256 B) whose 16-byte chunks are
+// XOR-swizzled by (t & 7). Eight consecutive tokens then keep any logical
+// chunk in eight different bank groups, so row-wise and transposing
+// ldmatrix reads of a block are free of bank conflicts.
+__host__ __device__ __forceinline__ int kv_swizzle(int t, int e) {
+    return t * 128 + ((((e >> 3) ^ (t & 7)) << 3) | (e & 7));
+}
+
 // Device error word, set instead of trapping. Codes (bitwise OR):
 enum : uint32_t {
     kErrTimeout = 1u,       // a bounded mbarrier wait ran out

@@ -76,7 +76,7 @@ struct QkvArgs {
     const int* row_seq;
     int seq0;
     // paged bf16 cache
-    uint16_t* kv_layer;         // this layer's pool base: [blocks][2][n_kv][16][d]
+    uint16_t* kv_layer;         // this layer's pool base: [blocks][2][n_kv][16][d], kv_swizzle rows
     const int* block_table;     // [seqs][max_blocks]
     int max_blocks;
     int n_pool_blocks;
@@ -107,18 +107,21 @@ void launch_gemv(const LinearArgs& a, cudaStream_t st);
 void launch_gemm_simt(const LinearArgs& a, cudaStream_t st);
 
 // attn.cu
+// Decode attention splits each (row, kv head) into at most
+// decode_max_segs(max_blocks) warp shares of >= kMinBlocksPerWarp blocks.
+constexpr int kMinBlocksPerWarp = 4;
+inline int decode_max_segs(int max_blocks) { return max_blocks / kMinBlocksPerWarp + 2; }
 struct AttnDecodeArgs {
     const float* q;             // [B][n_q][d]
-    const uint16_t* kv_layer;   // [blocks][2][n_kv][16][d]
+    const uint16_t* kv_layer;   // [blocks][2][n_kv][16][d], rows chunk-swizzled (kv_swizzle)
     const int* block_table;     // [seqs][max_blocks]
     int max_blocks;
     int n_pool_blocks;
     const int* seq_of;          // [B] sequence slot per batch row
     const int* positions;       // [B] position of the current token (kv_len = pos + 1)
-    int B, n_q, n_kv, d;
-    int chunk;                  // tokens per split (multiple of 32)
-    int max_splits;
-    float* partial;             // [B][n_kv][max_splits][group][d + 2]
+    int B, n_q, n_kv, d;        // B <= 1024, d = 128, n_q = 2 n_kv
+    int max_segs;               // decode_max_segs(max_blocks)
+    float* partial;             // [B][n_kv][max_segs][group][d + 2]
     unsigned int* counters;     // [B][n_kv], zero between launches
     float* out;                 // [B][n_q][d]
     uint32_t* err;

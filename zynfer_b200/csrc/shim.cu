@@ -282,7 +282,6 @@ int check_device_error(ZynferCuCtx* c) {
     return fail(c, ZYNFER_CU_INVALID, "device index check failed (token id, position or KV block)");
 }
 
-int decode_chunk(int B) { return B <= 2 ? 64 : (B <= 16 ? 128 : 256); }
 
 // --------------------------------------------------------- timing helpers
 void tbegin(ZynferCuCtx* c, int cls, TimedEvent** te) {
@@ -398,8 +397,6 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
 void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
     const ZynferCuModelDesc& m = c->d;
     const int H = m.hidden, I = m.inter;
-    const int chunk = decode_chunk(B);
-    const int max_splits = (int)((m.max_seq_len + chunk - 1) / chunk);
     c->step_launches = 0;
     TimedEvent* te;
     tbegin(c, ZYNFER_CU_K_OTHER, &te);
@@ -426,7 +423,7 @@ void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
         aa.q = c->dq; aa.kv_layer = qa.kv_layer; aa.block_table = c->table_dev;
         aa.max_blocks = c->max_blocks; aa.n_pool_blocks = c->n_blocks;
         aa.seq_of = c->dseq; aa.positions = c->dpos; aa.B = B; aa.n_q = m.n_q; aa.n_kv = m.n_kv;
-        aa.d = m.head_dim; aa.chunk = chunk; aa.max_splits = max_splits; aa.partial = c->dpart;
+        aa.d = m.head_dim; aa.max_segs = decode_max_segs(c->max_blocks); aa.partial = c->dpart;
         aa.counters = c->dcnt; aa.out = c->dattn; aa.err = c->derr;
         tbegin(c, ZYNFER_CU_K_ATTN, &te);
         launch_attn_decode(aa, c->stream);
@@ -763,8 +760,7 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     ALLOC(c->dkeys, B);
     ALLOC(c->dids, B);
     ALLOC(c->dcnt, B * m.n_kv);
-    const size_t max_splits = (m.max_seq_len + 63) / 64;
-    ALLOC(c->dpart, B * m.n_kv * max_splits * 2 * (hd + 2));
+    ALLOC(c->dpart, B * m.n_kv * (size_t)decode_max_segs(c->max_blocks) * 2 * (hd + 2));
     c->hist_cap = std::max<size_t>(B * 4096, 1 << 16);
     ALLOC(c->dhist, c->hist_cap);
     ALLOC(c->dstep, 1);
@@ -990,7 +986,7 @@ int zynfer_cu_kv_read(ZynferCuCtx* c, uint32_t seq, uint32_t layer, int which_v,
             ZC_CHECK(c, cudaMemcpy(blk.data(), src, blk.size() * 2, cudaMemcpyDeviceToHost), "kv read");
             for (uint32_t i = 0; i < (uint32_t)kKvBlock && p0 + i < len; ++i)
                 for (int e = 0; e < d; ++e) {
-                    const uint32_t u = (uint32_t)blk[(size_t)i * d + e] << 16;
+                    const uint32_t u = (uint32_t)blk[kv_swizzle((int)i, e)] << 16;
                     float f;
                     memcpy(&f, &u, 4);
                     out[((size_t)h * len + p0 + i) * d + e] = f;
@@ -1161,8 +1157,8 @@ int zynfer_cu_block_forward(ZynferCuCtx* c, uint32_t layer, uint32_t seq, const 
             AttnDecodeArgs aa{};
             aa.q = c->dq; aa.kv_layer = qa.kv_layer; aa.block_table = c->table_dev; aa.max_blocks = c->max_blocks;
             aa.n_pool_blocks = c->n_blocks; aa.seq_of = c->dseq; aa.positions = c->dpos; aa.B = 1;
-            aa.n_q = m.n_q; aa.n_kv = m.n_kv; aa.d = m.head_dim; aa.chunk = decode_chunk(1);
-            aa.max_splits = (int)((m.max_seq_len + aa.chunk - 1) / aa.chunk); aa.partial = c->dpart;
+            aa.n_q = m.n_q; aa.n_kv = m.n_kv; aa.d = m.head_dim;
+            aa.max_segs = decode_max_segs(c->max_blocks); aa.partial = c->dpart;
             aa.counters = c->dcnt; aa.out = c->dattn; aa.err = c->derr;
             launch_attn_decode(aa, c->stream);
             linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, &Ld.tm_o, H, c->qd, c->dattn, 1, c->dx1, kEpiResid, c->dx, nullptr, nullptr);

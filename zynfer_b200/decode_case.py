@@ -1,0 +1,81 @@
+"""Decode microbenchmark: one fixed batch of sequences at one context length.
+
+    python -m zynfer_b200.decode_case --seqs 32 --ctx 2048 --layers 2 --steps 3
+
+Builds an int8 Qwen3-0.6B-shaped model (optionally with fewer layers, so a
+profile of one layer's kernels holds only a few GB), prefills every sequence
+with a seeded prompt of `ctx` tokens, warms the decode graph, then times
+`steps` greedy steps on the device (CUDA events) and, in a second pass, every
+kernel class with per-launch events. The steps run between
+cudaProfilerStart/Stop, so a profiler started with `--profile-from-start off`
+sees only the decode launches. Prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import json
+
+KV_BYTES_PER_TOKEN_HEAD = 2 * 128 * 2  # K and V rows, bf16
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--seqs", type=int, default=64)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--path", default="auto", help="linear kernel family (auto, gemv, tcgen05, simt)")
+    args = ap.parse_args()
+
+    import torch
+
+    from . import cuda as zc
+    from . import workload
+
+    arch = dataclasses.replace(zc.QWEN3_0_6B, layers=args.layers)
+    B = args.seqs
+    total = args.warmup + 2 * args.steps + 2
+    gpu = zc.Gpu(0)
+    model = zc.Model(gpu, arch, zc.W_Q8, max_batch=B, max_seqs=B, max_seq_len=args.ctx + total + 16,
+                     max_prefill=args.ctx)
+    model.fill_synthetic(args.seed, 0.02, 0.0)
+    gpu.set_linear_path(args.path)
+    first = [model.prefill(s, workload.prompt(s, args.ctx, args.seed), want_logits=False) for s in range(B)]
+    slots = list(range(B))
+    out, _ = model.generate(slots, first, args.warmup)
+    nxt = out[-1].tolist()
+    gpu.sync()
+
+    torch.cuda.profiler.start()
+    out, ms = model.generate(slots, nxt, args.steps)
+    torch.cuda.profiler.stop()
+    nxt = out[-1].tolist()
+
+    ctx = [model.seq_len(s) for s in slots]
+    gpu.set_timing(True)
+    model.generate(slots, nxt, args.steps)
+    times = {name: gpu.kernel_time(cls) for name, cls in
+             (("attention", zc.K_ATTN), ("linear", zc.K_LINEAR), ("lm_head", zc.K_LMHEAD), ("other", zc.K_OTHER))}
+    gpu.set_timing(False)
+
+    kv_tok = sum(sum(c + 1 + s for c in ctx) for s in range(args.steps)) / args.steps
+    attn_bytes = kv_tok * KV_BYTES_PER_TOKEN_HEAD * arch.n_kv + B * 2 * arch.n_q * arch.head_dim * 4
+    n_attn, ms_attn = times["attention"]
+    line = {
+        "seqs": B, "ctx": args.ctx, "layers": args.layers, "steps": args.steps, "path": args.path,
+        "ms_per_step": round(ms / args.steps, 4), "tok_s": round(B * args.steps / (ms / 1e3), 1),
+        "launches_per_step": gpu.step_launches,
+        "kernel_ms_per_step": {k: round(v[1] / args.steps, 4) for k, v in times.items()},
+        "launches": {k: v[0] for k, v in times.items()},
+        "attn_bytes_per_launch": int(attn_bytes),
+        "attn_gbs": round(attn_bytes / (ms_attn / max(1, n_attn) / 1e3) / 1e9, 1) if n_attn else None,
+    }
+    print(json.dumps(line), flush=True)
+    gpu.close()
+
+
+if __name__ == "__main__":
+    main()
