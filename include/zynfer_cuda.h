@@ -162,6 +162,14 @@ ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, c
  * tcgen05 tensor cores above), "gemv", "tcgen05", or "simt" (the CUDA-core
  * tiled GEMM, kept for comparisons). Applies to later calls of this context. */
 ZYNFER_CU_API int zynfer_cu_set_linear_path(ZynferCuCtx *ctx, const char *path);
+/* Decode schedule for zynfer_cu_decode_step / zynfer_cu_generate: "kernels"
+ * (one kernel per op, captured in a CUDA graph per batch size), "persistent"
+ * (the whole step as one cooperative persistent kernel with grid barriers;
+ * int8 models of hidden 1024, intermediate 3072, 16 x 128 query dims, batch
+ * <= 8; ZYNFER_CU_UNSUPPORTED otherwise), or "auto" (persistent for batch 1
+ * where it applies, kernels otherwise). Both follow qwen_block.forward (qwen_block.zig:161-235) per layer
+ * and qwen_forward's tied LM head + topK(1) (qwen_forward.zig:163-193). */
+ZYNFER_CU_API int zynfer_cu_set_decode_schedule(ZynferCuCtx *ctx, const char *schedule);
 /* Allocation-free int8 linear (no counterpart in the reference; an addition
  * of this backend). Same result as zynfer_cu_linear with ZYNFER_CU_W_Q8:
  * y[b][i] = (W[i,:] . x[b,:]) * scale[i], computed on the tcgen05 path, for
@@ -196,6 +204,12 @@ ZYNFER_CU_API int zynfer_cu_set_timing(ZynferCuCtx *ctx, int enable);
 enum { ZYNFER_CU_K_ATTN = 0, ZYNFER_CU_K_LINEAR = 1, ZYNFER_CU_K_LMHEAD = 2, ZYNFER_CU_K_OTHER = 3 };
 ZYNFER_CU_API int zynfer_cu_kernel_time(const ZynferCuCtx *ctx, int kernel_class, uint64_t *launches, double *total_ms);
 ZYNFER_CU_API uint64_t zynfer_cu_last_step_ns(const ZynferCuCtx *ctx);
+/* Phase timestamps of the last persistent decode step run with timing on
+ * (signpost intervals, src/backends/apple/gpu.zig:91-106 pattern): globaltimer
+ * ns as seen by CTA 0: [0] start, then (start, end) per phase (QKV, ATT, O,
+ * GU, D per layer, then the LM head), then the finish. Copies up to `cap`
+ * entries into out and returns how many exist (0 when there is no trace). */
+ZYNFER_CU_API int zynfer_cu_phase_trace(const ZynferCuCtx *ctx, uint64_t *out, int cap);
 /* Kernels one decode step enqueues (the last one built). */
 ZYNFER_CU_API int zynfer_cu_step_launches(const ZynferCuCtx *ctx);
 /* Host->device and device->host bytes copied by decode/generate/prefill calls

@@ -1,0 +1,129 @@
+"""The persistent decode schedule (one cooperative kernel per step) against the
+oracle and against the multi-kernel schedule (B200 only).
+
+The persistent kernel is built for Qwen3-0.6B widths (hidden 1024,
+intermediate 3072, 16 x 128 query dims, 8 kv heads), so these tests use those
+widths with 2 layers and a 8192-token vocabulary, which keeps the oracle fast.
+Tolerances: BF16_KV (both sides keep a bf16 KV cache).
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from zynfer_b200 import cuda as zc
+
+from tolerances import BF16_KV, check_logits
+
+pytestmark = pytest.mark.gpu
+
+WIDE = dict(vocab=8192, hidden=1024, inter=3072, layers=2, n_q=16, n_kv=8, head_dim=128, max_pos=4096,
+            eps=1e-6, theta=1_000_000.0)
+SEED, WSTD, NSTD = 5, 0.02, 0.1
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    g = zc.Gpu(0)
+    yield g
+    g.close()
+
+
+@pytest.fixture(scope="module")
+def wide(gpu):
+    m = zc.Model(gpu, zc.Arch(**WIDE), zc.W_Q8, max_batch=8, max_seqs=12, max_seq_len=1024)
+    m.fill_synthetic(SEED, WSTD, NSTD)
+    gpu.set_decode_schedule("persistent")
+    return m
+
+
+@pytest.fixture(scope="module")
+def oracle_wide():
+    return O.Model(O.Arch(**WIDE), O.W_Q8, kv_bf16=True, seed=SEED, w_std=WSTD, norm_std=NSTD, threads=8)
+
+
+def test_single_sequence_teacher_forced(wide, oracle_wide):  # qwen_block.zig:161-235 per layer, t = 1
+    ids = O.synth_tokens(27, SEED, 3, WIDE["vocab"])
+    wide.prefill(0, ids, want_logits=False)
+    s = oracle_wide.session(128)
+    s.forward(ids, want_logits=False)
+    feed = O.synth_tokens(9, SEED, 4, WIDE["vocab"])  # crosses the 32-token block boundary
+    for i, tok in enumerate(feed):
+        am, logits = wide.decode_step([0], [tok], want_logits=True)
+        assert wide.gpu.last_path == "decode:persistent"
+        ref = s.forward([tok])
+        check_logits(ref, logits[0], f"step {i}")
+        assert int(am[0]) == int(np.argmax(logits[0]))
+    assert wide.seq_len(0) == 36
+
+
+def test_kv_append_matches_oracle(wide, oracle_wide):  # kv_cache.zig:49-73
+    ids = O.synth_tokens(14, SEED, 5, WIDE["vocab"])
+    wide.prefill(1, ids, want_logits=False)
+    s = oracle_wide.session(64)
+    s.forward(ids, want_logits=False)
+    for tok in O.synth_tokens(4, SEED, 6, WIDE["vocab"]):
+        wide.decode_step([1], [tok])
+        s.forward([tok], want_logits=False)
+    for layer in range(WIDE["layers"]):
+        for which_v in (False, True):
+            got, ref = wide.kv(1, layer, which_v), s.kv(layer, which_v)
+            # bf16 values: equal, or one bf16 step apart where the f32 inputs of the
+            # two sides straddle a rounding edge (more of them at this width)
+            np.testing.assert_allclose(got, ref, rtol=1.6e-2, atol=1e-3)
+            assert np.mean(got == ref) > 0.9
+
+
+@pytest.mark.parametrize("batch", [2, 5, 8])
+def test_batched_rows_match_oracle(wide, oracle_wide, batch):
+    seqs = list(range(2, 2 + batch))
+    sessions = []
+    for j, sq in enumerate(seqs):
+        ids = O.synth_tokens(3 + 17 * j, SEED + sq, 7, WIDE["vocab"])
+        wide.prefill(sq, ids, want_logits=False)
+        ses = oracle_wide.session(256)
+        ses.forward(ids, want_logits=False)
+        sessions.append(ses)
+    for step in range(3):
+        toks = O.synth_tokens(batch, 200 + step, 3, WIDE["vocab"])
+        am, logits = wide.decode_step(seqs, toks, want_logits=True)
+        for r in range(batch):
+            check_logits(sessions[r].forward([toks[r]]), logits[r], f"B={batch} row {r} step {step}")
+
+
+def test_generate_equals_stepwise(wide):
+    ids = O.synth_tokens(40, SEED, 21, WIDE["vocab"])
+    wide.prefill(10, ids, want_logits=False)
+    stepwise, tok = [], 17
+    for _ in range(12):
+        tok = int(wide.decode_step([10], [tok])[0])
+        stepwise.append(tok)
+    wide.prefill(10, ids, want_logits=False)
+    out, ms = wide.generate([10], [17], 12)
+    assert wide.gpu.last_path == "generate:persistent"
+    assert out[:, 0].tolist() == stepwise
+    assert ms > 0.0
+
+
+def test_persistent_and_kernel_schedules_agree(wide):
+    ids = O.synth_tokens(50, SEED, 23, WIDE["vocab"])
+    feed = O.synth_tokens(6, SEED, 24, WIDE["vocab"])
+    runs = {}
+    for sched in ("persistent", "kernels"):
+        wide.gpu.set_decode_schedule(sched)
+        wide.prefill(11, ids, want_logits=False)
+        runs[sched] = [wide.decode_step([11], [t], want_logits=True)[1][0] for t in feed]
+    wide.gpu.set_decode_schedule("persistent")
+    for i, (a, b) in enumerate(zip(runs["persistent"], runs["kernels"])):
+        check_logits(b, a, f"schedules step {i}", BF16_KV)
+
+
+def test_schedule_names_and_shape_limits(gpu, wide):
+    with pytest.raises(zc.InvalidArgument):
+        gpu.set_decode_schedule("bogus")
+    g2 = zc.Gpu(0)
+    small = dict(WIDE, hidden=512, inter=1024, n_q=4, n_kv=2)
+    zc.Model(g2, zc.Arch(**small), zc.W_Q8, max_batch=1, max_seqs=1, max_seq_len=64)
+    with pytest.raises(zc.Unsupported):
+        g2.set_decode_schedule("persistent")
+    g2.set_decode_schedule("kernels")
+    g2.close()

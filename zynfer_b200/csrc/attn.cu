@@ -3,6 +3,7 @@
 // log-sum-exp merge, and a tiled f32 prefill kernel.
 #include <algorithm>
 
+#include "attn_common.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -37,51 +38,23 @@ namespace {
 // KV blocks are stored with their 16-byte chunks XOR-swizzled by token
 // (kv_swizzle), so the ldmatrix reads of K rows and the transposing reads of
 // V rows hit 32 distinct banks.
-constexpr int kD = 128, kG = 2;
+using attn::kBlockBytes;
+using attn::kBlockElems;
+using attn::kD;
+using attn::kG;
+using attn::kSlotBytes;
+using attn::ldsm_x4;
+using attn::ldsm_x4_trans;
+using attn::mma_bf16;
+using attn::fence_proxy_async_smem;
+using attn::pack_terms;
 constexpr int kDecWarps = 8, kDecThreads = kDecWarps * kWarp;
 constexpr int kRing = 3;                                     // slots per warp
-constexpr int kBlockElems = kKvBlock * kD;                   // 2048 bf16 = 4 KB
-constexpr int kBlockBytes = kBlockElems * 2;
-constexpr int kSlotBytes = 2 * kBlockBytes;                  // K + V
 constexpr int kMaxBatch = 1024;
 constexpr size_t kRingBytes = (size_t)kDecWarps * kRing * kSlotBytes;
-constexpr size_t kDecodeSmem = kRingBytes + kDecWarps * kRing * sizeof(uint64_t) + (kMaxBatch + 1) * sizeof(int);
-static_assert(kD == 128 && kKvBlock == 16, "the fragment mapping assumes 16-token blocks of 128 dims");
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr)
-                 : "memory");
-}
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                              uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr)
-                 : "memory");
-}
-// D = A . B + D for one m16n8k16 tile; A rows 8..15 are zero when a1 = a3 = 0.
-__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-// One bf16 term of x: the rounded value (lo_part = 0) or the rounded remainder.
-__device__ __forceinline__ uint32_t bf16_term(float x, bool lo_part) {
-    const uint16_t hi = f32_to_bf16_rne(x);
-    if (!lo_part) return hi;
-    return f32_to_bf16_rne(x - __uint_as_float((uint32_t)hi << 16));
-}
-__device__ __forceinline__ uint32_t pack_terms(float x0, float x1, bool lo_part) {
-    return bf16_term(x0, lo_part) | (bf16_term(x1, lo_part) << 16);
-}
+constexpr int kIdRing = 64;                                 // per-warp ring of block addresses (2 chunks of 32)
+constexpr size_t kDecodeSmem = kRingBytes + kDecWarps * kRing * sizeof(uint64_t) + (kMaxBatch + 1) * sizeof(int) +
+                               kDecWarps * kIdRing * sizeof(uint32_t);
 
 struct BlockCursor {
     int b, head, blk, nblk;
@@ -93,6 +66,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
     unsigned char* ring = smem_raw + (size_t)warp * kRing * kSlotBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kRingBytes) + warp * kRing;
     int* pref = reinterpret_cast<int*>(smem_raw + kRingBytes + kDecWarps * kRing * sizeof(uint64_t));
+    uint32_t* kidx = reinterpret_cast<uint32_t*>(pref + kMaxBatch + 1) + warp * kIdRing;
     constexpr unsigned kAll = 0xFFFFFFFFu;
 
     pdl_launch_dependents();
@@ -159,14 +133,31 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
             c.nblk = c.b < B ? pref[c.b + 1] - pref[c.b] : 1;
         } while (c.nblk == 0);
     };
-    auto issue = [&](const BlockCursor& c, int s) {  // lane 0
-        const int seq = a.seq_of[c.b];
-        int id = a.block_table[(size_t)seq * a.max_blocks + c.blk];
-        if (id < 0 || id >= a.n_pool_blocks) {
-            if (a.err) atomicOr(a.err, kErrBadIndex);
-            id = 0;  // keep the pipeline whole; the error word reports the launch
+    // Block addresses of this warp's range, 32 at a time, one lane per block:
+    // kidx = K block index in units of kBlockElems (V follows n_kv blocks
+    // later), bit 31 = last block of its row.
+    constexpr uint32_t kLastBit = 0x80000000u;
+    auto fill_chunk = [&](int c) {
+        const int j = kWarp * c + lane;
+        if (j < n) {
+            BlockCursor x;
+            locate(lo + j, x);
+            const int seq = a.seq_of[x.b];
+            int id = a.block_table[(size_t)seq * a.max_blocks + x.blk];
+            if (id < 0 || id >= a.n_pool_blocks) {
+                if (a.err) atomicOr(a.err, kErrBadIndex);
+                id = 0;  // keep the pipeline whole; the error word reports the launch
+            }
+            kidx[j % kIdRing] = ((uint32_t)id * 2u * (uint32_t)a.n_kv + (uint32_t)x.head) |
+                                (x.blk == x.nblk - 1 ? kLastBit : 0u);
         }
-        const uint16_t* kp = a.kv_layer + (((size_t)id * 2) * a.n_kv + c.head) * kBlockElems;
+        __syncwarp();
+    };
+    auto block_k = [&](int j) -> const uint16_t* {
+        return a.kv_layer + (size_t)(kidx[j % kIdRing] & ~kLastBit) * kBlockElems;
+    };
+    auto issue = [&](int j, int s) {  // lane 0: block j of the range into slot s
+        const uint16_t* kp = block_k(j);
         const uint16_t* vp = kp + (size_t)a.n_kv * kBlockElems;
         unsigned char* dst = ring + s * kSlotBytes;
         mbar_arrive_expect_tx(&full[s], kSlotBytes);
@@ -177,21 +168,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
     // Fill the ring. Only the last block of a row receives this step's K/V
     // (from the kernel before this one), so the fill stops there until
     // griddepcontrol.wait has returned.
-    BlockCursor ci, cc;
-    locate(lo, ci);
-    cc = ci;
+    BlockCursor cc;
+    locate(lo, cc);
+    fill_chunk(0);
     const int first = min(kRing, n);
     int issued = 0;
-    while (issued < first && ci.blk != ci.nblk - 1) {
-        if (lane == 0) issue(ci, issued);
-        advance(ci);
+    while (issued < first && !(kidx[issued] & kLastBit)) {
+        if (lane == 0) issue(issued, issued);
         ++issued;
     }
     pdl_wait();
-    for (; issued < first; ++issued) {
-        if (lane == 0) issue(ci, issued);
-        advance(ci);
-    }
+    for (; issued < first; ++issued)
+        if (lane == 0) issue(issued, issued);
 
     const int g = lane >> 2, t = lane & 3;
     const int mi = lane >> 3, ri = lane & 7;
@@ -249,15 +237,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
         }
 
         // S = K . Qcols
-        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sd[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // even / odd k-steps
         const uint32_t kbase = smem_addr(kb), vbase = kbase + kBlockBytes;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
             const int ch = 2 * ks + (mi >> 1);
             uint32_t a0, a1, a2, a3;
             ldsm_x4(kbase + tok_a * (kD * 2) + ((ch ^ ri) << 4), a0, a1, a2, a3);
-            mma_bf16(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+            if (ks & 1) mma_bf16(sd, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+            else mma_bf16(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
         }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[e] += sd[e];
         // lanes t = 0, 1 hold head t's scores for tokens g and g + 8
         float s0 = 0.0f, s1 = 0.0f;
         if (t < 2) {
@@ -305,85 +296,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
         }
         if (nv < kKvBlock) fence_proxy_async_smem();  // generic writes above, bulk copy next
         __syncwarp();
-        if (i + kRing < n) {
-            if (lane == 0) issue(ci, s);
-            advance(ci);
+        {
+            const int jn = i + kRing;  // next block for this slot
+            if (jn < n && jn % kWarp == 0) fill_chunk(jn / kWarp);
+            if (lane == 0 && jn < n) issue(jn, s);
         }
 
         if (cc.blk == cc.nblk - 1 || i == n - 1) {
             // ---- end of this warp's share of (row b, kv head)
-            const int b = cc.b, head = cc.head;
-            float L = l_run;
-            L += __shfl_xor_sync(kAll, L, 4);
-            L += __shfl_xor_sync(kAll, L, 8);
-            L += __shfl_xor_sync(kAll, L, 16);
-            const float Lh = __shfl_sync(kAll, L, hsel);
-            const float Mh = __shfl_sync(kAll, m_run, hsel);
-#pragma unroll
-            for (int nt = 0; nt < 16; ++nt) {  // rows hi + lo of the same head
-                acc[nt][0] += __shfl_xor_sync(kAll, acc[nt][0], 4);
-                acc[nt][1] += __shfl_xor_sync(kAll, acc[nt][1], 4);
-            }
-            const bool writer = lane < 16 && (g & 1) == 0;  // lanes 0-3: head 0, 8-11: head 1
-            const int f0 = a.n_kv * pref[b] + head * cc.nblk;
+            const int f0 = a.n_kv * pref[cc.b] + cc.head * cc.nblk;
             const int fw = f0 / per, lw = (f0 + cc.nblk - 1) / per;
-            const int nseg = lw - fw + 1, seg = w - fw;
-            if (nseg == 1) {
-                if (writer) {
-                    float* op = a.out + ((size_t)b * a.n_q + head * kG + hsel) * kD + 2 * t;
-                    const float inv = 1.0f / Lh;
-#pragma unroll
-                    for (int nt = 0; nt < 16; ++nt)
-                        *reinterpret_cast<float2*>(op + nt * 8) = make_float2(acc[nt][0] * inv, acc[nt][1] * inv);
-                }
-            } else if (seg < a.max_segs && nseg <= a.max_segs) {
-                float* base = a.partial + ((size_t)b * a.n_kv + head) * a.max_segs * (kG * (kD + 2));
-                float* pg = base + (size_t)seg * (kG * (kD + 2)) + hsel * (kD + 2);
-                if (writer) {
-                    if (t == 0) {
-                        pg[0] = Mh;
-                        pg[1] = Lh;
-                    }
-#pragma unroll
-                    for (int nt = 0; nt < 16; ++nt)
-                        *reinterpret_cast<float2*>(pg + 2 + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
-                }
-                __threadfence();
-                __syncwarp();
-                unsigned prev = 0;
-                if (lane == 0) prev = atomicAdd(a.counters + (size_t)b * a.n_kv + head, 1u);
-                prev = __shfl_sync(kAll, prev, 0);
-                if (prev == (unsigned)(nseg - 1)) {
-                    __threadfence();
-                    // merge: lane owns dims 4 lane .. 4 lane + 3 of both query heads
-#pragma unroll
-                    for (int h = 0; h < kG; ++h) {
-                        float M = -INFINITY;
-                        for (int sp = 0; sp < nseg; ++sp)
-                            M = fmaxf(M, __ldcg(base + (size_t)sp * (kG * (kD + 2)) + h * (kD + 2)));
-                        float Lm = 0.0f;
-                        float4 A = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                        for (int sp = 0; sp < nseg; ++sp) {
-                            const float* ps = base + (size_t)sp * (kG * (kD + 2)) + h * (kD + 2);
-                            const float ms = __ldcg(ps);
-                            const float c = ms == -INFINITY ? 0.0f : expf(ms - M);
-                            Lm += __ldcg(ps + 1) * c;
-                            const float2 u0 = __ldcg(reinterpret_cast<const float2*>(ps + 2 + 4 * lane));
-                            const float2 u1 = __ldcg(reinterpret_cast<const float2*>(ps + 2 + 4 * lane + 2));
-                            A.x += u0.x * c;
-                            A.y += u0.y * c;
-                            A.z += u1.x * c;
-                            A.w += u1.y * c;
-                        }
-                        const float inv = 1.0f / Lm;
-                        float* op = a.out + ((size_t)b * a.n_q + head * kG + h) * kD + 4 * lane;
-                        *reinterpret_cast<float4*>(op) = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
-                    }
-                    if (lane == 0) a.counters[(size_t)b * a.n_kv + head] = 0u;
-                }
-            } else if (lane == 0 && a.err) {
-                atomicOr(a.err, kErrBadIndex);
-            }
+            attn::flush_share(acc, l_run, m_run, cc.b, cc.head, lw - fw + 1, w - fw, a.max_segs, a.n_q, a.n_kv,
+                              a.partial, a.counters, a.out, a.err);
             seg_start = true;
         }
         advance(cc);

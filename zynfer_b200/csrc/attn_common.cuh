@@ -1,0 +1,175 @@
+// Pieces shared by the decode attention kernel (attn.cu) and the persistent
+// decode kernel (decode_persistent.cu): tensor-core fragment helpers and the
+// end-of-share flush with its log-sum-exp merge (attentionInto,
+// src/backends/cpu/ops.zig:285-354, split over KV blocks).
+#pragma once
+
+#include "common.cuh"
+
+namespace zc {
+namespace attn {
+
+constexpr int kD = 128, kG = 2;                  // head dim, query heads per kv head
+constexpr int kBlockElems = kKvBlock * kD;       // 2048 bf16 = 4 KB (K or V of one block and head)
+constexpr int kBlockBytes = kBlockElems * 2;
+constexpr int kSlotBytes = 2 * kBlockBytes;      // K then V
+// Partial result of one share, per query head: [m, l, -, -, acc[128]] so the
+// accumulator is 16-byte aligned; a share holds kG of them.
+constexpr int kPartHead = kD + 4;
+constexpr int kPartStride = kG * kPartHead;
+static_assert(kD == 128 && kKvBlock == 16, "the fragment mapping assumes 16-token blocks of 128 dims");
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+// D = A . B + D for one m16n8k16 tile; A rows 8..15 are zero when a1 = a3 = 0.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Two f32 -> packed bf16x2 (x0 in the low half), round to nearest even.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float x0, float x1) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+// One bf16 term of (x0, x1): the rounded values (lo_part = 0) or the rounded
+// remainders x - bf16(x) (lo_part = 1); hi + lo carries x to 2^-18 relative.
+__device__ __forceinline__ uint32_t pack_terms(float x0, float x1, bool lo_part) {
+    const uint32_t h = cvt_bf16x2(x0, x1);
+    if (!lo_part) return h;
+    return cvt_bf16x2(x0 - __uint_as_float(h << 16), x1 - __uint_as_float(h & 0xFFFF0000u));
+}
+
+// End of a warp's share (segment `seg` of `nseg`) of one (batch row b, kv
+// head). acc / l_run / m_run are the fragment-layout state of the block loop:
+// lanes (g < 4, t) hold O rows g = (head g/2, term g%2) at dims 8 nt + 2t
+// (+1); lanes with t < 2 hold query head t's running max and partial sums.
+// A share that is the whole row stores o = acc / l directly; otherwise it
+// stores its partial and the last share to finish (atomic counter) merges
+// all of them in segment order:
+//   m = max m_s,  l = sum l_s e^(m_s - m),  o = sum acc_s e^(m_s - m) / l.
+__device__ __forceinline__ void flush_share(float (&acc)[16][4], float l_run, float m_run, int b, int head,
+                                            int nseg, int seg, int max_segs, int n_q, int n_kv, float* partial,
+                                            unsigned* counters, float* out, uint32_t* err) {
+    constexpr unsigned kAll = 0xFFFFFFFFu;
+    const int lane = threadIdx.x % kWarp;
+    const int g = lane >> 2, t = lane & 3, hsel = (lane >> 3) & 1;
+    float L = l_run;
+    L += __shfl_xor_sync(kAll, L, 4);
+    L += __shfl_xor_sync(kAll, L, 8);
+    L += __shfl_xor_sync(kAll, L, 16);
+    const float Lh = __shfl_sync(kAll, L, hsel);
+    const float Mh = __shfl_sync(kAll, m_run, hsel);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {  // rows hi + lo of the same head
+        acc[nt][0] += __shfl_xor_sync(kAll, acc[nt][0], 4);
+        acc[nt][1] += __shfl_xor_sync(kAll, acc[nt][1], 4);
+    }
+    const bool writer = lane < 16 && (g & 1) == 0;  // lanes 0-3: head 0, 8-11: head 1
+    if (nseg == 1) {
+        if (writer) {
+            float* op = out + ((size_t)b * n_q + head * kG + hsel) * kD + 2 * t;
+            const float inv = 1.0f / Lh;
+#pragma unroll
+            for (int nt = 0; nt < 16; ++nt)
+                *reinterpret_cast<float2*>(op + nt * 8) = make_float2(acc[nt][0] * inv, acc[nt][1] * inv);
+        }
+        return;
+    }
+    if (seg >= max_segs || nseg > max_segs) {
+        if (lane == 0 && err) atomicOr(err, kErrBadIndex);
+        return;
+    }
+    float* base = partial + ((size_t)b * n_kv + head) * max_segs * kPartStride;
+    float* pg = base + (size_t)seg * kPartStride + hsel * kPartHead;
+    if (writer) {
+        if (t == 0) {
+            pg[0] = Mh;
+            pg[1] = Lh;
+        }
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt)
+            *reinterpret_cast<float2*>(pg + 4 + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
+    }
+    __threadfence();
+    __syncwarp();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(counters + (size_t)b * n_kv + head, 1u);
+    prev = __shfl_sync(kAll, prev, 0);
+    if (prev != (unsigned)(nseg - 1)) return;
+    __threadfence();
+    // Merge. Segment statistics one segment per lane; then every lane owns
+    // dims 4 lane .. 4 lane + 3 of both query heads and sums the segments
+    // with eight of them in flight at a time.
+    float M0 = -INFINITY, M1 = -INFINITY;
+    for (int s = lane; s < nseg; s += kWarp) {
+        M0 = fmaxf(M0, __ldcg(base + (size_t)s * kPartStride));
+        M1 = fmaxf(M1, __ldcg(base + (size_t)s * kPartStride + kPartHead));
+    }
+    M0 = warp_max(M0);
+    M1 = warp_max(M1);
+    float L0 = 0.0f, L1 = 0.0f;
+    float4 A0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), A1 = A0;
+    for (int s0 = 0; s0 < nseg; s0 += kWarp) {
+        float c0 = 0.0f, c1 = 0.0f;
+        if (s0 + lane < nseg) {
+            const float* ps = base + (size_t)(s0 + lane) * kPartStride;
+            const float m0 = __ldcg(ps), l0 = __ldcg(ps + 1);
+            const float m1 = __ldcg(ps + kPartHead), l1 = __ldcg(ps + kPartHead + 1);
+            c0 = m0 == -INFINITY ? 0.0f : expf(m0 - M0);
+            c1 = m1 == -INFINITY ? 0.0f : expf(m1 - M1);
+            L0 += l0 * c0;
+            L1 += l1 * c1;
+        }
+        const int cnt = min(kWarp, nseg - s0);
+        const float* pa = base + (size_t)s0 * kPartStride + 4 + 4 * lane;
+        for (int j0 = 0; j0 < cnt; j0 += 8) {
+            // eight segments' accumulators in flight before any is used
+            float4 u0[8], u1[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int jj = min(j0 + j, cnt - 1);
+                u0[j] = __ldcg(reinterpret_cast<const float4*>(pa + (size_t)jj * kPartStride));
+                u1[j] = __ldcg(reinterpret_cast<const float4*>(pa + (size_t)jj * kPartStride + kPartHead));
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const bool live = j0 + j < cnt;
+                const float cj0 = __shfl_sync(kAll, c0, (j0 + j) & (kWarp - 1));
+                const float cj1 = __shfl_sync(kAll, c1, (j0 + j) & (kWarp - 1));
+                if (live) {
+                    A0.x += u0[j].x * cj0; A0.y += u0[j].y * cj0; A0.z += u0[j].z * cj0; A0.w += u0[j].w * cj0;
+                    A1.x += u1[j].x * cj1; A1.y += u1[j].y * cj1; A1.z += u1[j].z * cj1; A1.w += u1[j].w * cj1;
+                }
+            }
+        }
+    }
+    L0 = warp_sum(L0);
+    L1 = warp_sum(L1);
+    const float i0 = 1.0f / L0, i1 = 1.0f / L1;
+    float* op = out + ((size_t)b * n_q + head * kG) * kD + 4 * lane;
+    *reinterpret_cast<float4*>(op) = make_float4(A0.x * i0, A0.y * i0, A0.z * i0, A0.w * i0);
+    *reinterpret_cast<float4*>(op + kD) = make_float4(A1.x * i1, A1.y * i1, A1.z * i1, A1.w * i1);
+    if (lane == 0) counters[(size_t)b * n_kv + head] = 0u;
+}
+
+}  // namespace attn
+}  // namespace zc

@@ -42,6 +42,7 @@ void prepare_norm_kernels();
 void prepare_gemv_kernels();
 void prepare_gemm_simt_kernels();
 void prepare_attn_kernels();
+void prepare_persistent_kernels();
 void prepare_tc_kernels();
 void launch_synth_normal(float* out, size_t n, uint64_t seed, uint64_t stream, float k,
                          float add, cudaStream_t st);
@@ -121,12 +122,53 @@ struct AttnDecodeArgs {
     const int* positions;       // [B] position of the current token (kv_len = pos + 1)
     int B, n_q, n_kv, d;        // B <= 1024, d = 128, n_q = 2 n_kv
     int max_segs;               // decode_max_segs(max_blocks)
-    float* partial;             // [B][n_kv][max_segs][group][d + 2]
+    float* partial;             // [B][n_kv][max_segs][group][d + 4] (m, l, pad, pad, acc)
     unsigned int* counters;     // [B][n_kv], zero between launches
     float* out;                 // [B][n_q][d]
     uint32_t* err;
 };
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st);
+
+// decode_persistent.cu: one decode step of 1..kPersistentMaxBatch rows as one
+// cooperative persistent kernel (int8 weights, hidden 1024, intermediate
+// 3072, 16 x 128 query dims).
+constexpr int kPersistentMaxBatch = 8;
+struct PersistentLayer {
+    const int8_t *wqkv, *wo, *wgu, *wd;
+    const float *sqkv, *so, *sgu, *sd;
+    const float *input_ln, *post_ln, *q_norm, *k_norm;
+};
+struct PersistentArgs {
+    int B, H, I, V, L, n_q, n_kv;
+    float eps;
+    const PersistentLayer* layers;  // device array [L]
+    const int8_t* embed;            // tied embedding / LM head [V][H]
+    const float* sembed;
+    const float* final_norm;
+    const float2* rope;
+    int rope_max_pos;
+    uint16_t* kv;                   // pool base; layer l at l * kv_layer_elems
+    size_t kv_layer_elems;
+    const int* block_table;
+    int max_blocks, n_pool_blocks, max_segs;
+    uint32_t* tok;                  // [B] input ids, replaced by the argmax ids
+    const int* seq_of;              // [B]
+    int* positions;                 // [B], advanced by one
+    unsigned long long* keys;       // [B] argmax keys, zero between steps
+    uint32_t* ids_out;              // [B]
+    uint32_t* history;              // nullable [steps][B]
+    int* step;
+    float *x, *x1, *qkv, *attn, *h, *partial;
+    float* logits;                  // nullable [B][V]
+    unsigned* counters;             // [B][n_kv] attention merge counters, zero between launches
+    unsigned* sync;                 // [3]: barrier arrivals, finished CTAs, abort flag; zero between launches
+    uint32_t* err;
+    uint64_t* trace;                // nullable [4 + 10 L] globaltimer ns: start, then per phase (start, end) as
+                                    // seen by CTA 0 (phases QKV, ATT, O, GU, D per layer, then HEAD), then finish
+};
+inline int persistent_trace_len(int layers) { return 4 + 10 * layers; }
+bool persistent_supported(int device);
+cudaError_t launch_decode_persistent(const PersistentArgs& a, cudaStream_t st);
 struct AttnPrefillArgs {
     const float* q;   // [n_q][T][d]
     const float* k;   // [n_kv][T][d]

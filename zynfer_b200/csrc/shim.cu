@@ -30,7 +30,12 @@ namespace {
 // Which kernel runs a linear layer: the CUDA-core GEMV (few rows), the
 // tensor-core tcgen05 path, or the CUDA-core tiled GEMM (kept for A/B checks).
 enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3 };
-constexpr int kGemvMaxRows = 4;  // auto policy: GEMV up to this many rows, tcgen05 above
+// Decode schedule: separate kernels per op (graph-captured), or one persistent
+// kernel per step for small int8 batches; auto picks the persistent kernel
+// whenever it applies.
+enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2 };
+constexpr int kGemvMaxRows = 4;  // auto policy: GEMV up to this many rows, tcgen05 above ...
+constexpr int kGemvMaxRowsWideM = 16384;  // ... and up to 8 rows for matrices of at most this many outputs
 
 struct LayerDev {
     void* wqkv = nullptr;
@@ -129,6 +134,12 @@ struct ZynferCuCtx {
     float* simt_xn = nullptr;  // normalised rows for the CUDA-core GEMM path
     size_t simt_xn_elems = 0;
     int path_policy = kPathAuto;
+    int schedule = kSchedAuto;
+    bool persistent_ok = false;          // model shape and device allow the persistent decode kernel
+    PersistentLayer* dlayers = nullptr;  // [layers] weight pointers for it
+    unsigned* psync = nullptr;           // [3] its grid-barrier / finish / abort words
+    uint64_t* ptrace = nullptr;          // its phase timestamps when timing is on
+    std::vector<uint64_t> ptrace_host;
 
     std::map<int, cudaGraphExec_t> graphs;
     int step_launches = 0;  // kernels enqueued by the last decode step
@@ -277,6 +288,8 @@ int check_device_error(ZynferCuCtx* c) {
     if (!e) return ZYNFER_CU_OK;
     cudaMemsetAsync(c->derr, 0, 4, c->stream);
     cudaMemsetAsync(c->dcnt, 0, (size_t)c->d.max_batch * c->d.n_kv * 4, c->stream);
+    if (c->psync) cudaMemsetAsync(c->psync, 0, 3 * sizeof(unsigned), c->stream);
+    cudaMemsetAsync(c->dkeys, 0, (size_t)c->d.max_batch * 8, c->stream);
     cudaStreamSynchronize(c->stream);
     if (e & kErrTimeout) return fail(c, ZYNFER_CU_TIMEOUT, "device wait timed out (bounded mbarrier wait)");
     return fail(c, ZYNFER_CU_INVALID, "device index check failed (token id, position or KV block)");
@@ -356,7 +369,7 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
     a.y = y; a.ldy = epi == kEpiSwiGLU ? M / 2 : M; a.epi = epi; a.resid = resid; a.norm_w = norm_w;
     a.eps = c->d.eps > 0.0f ? c->d.eps : 1e-6f; a.argmax_keys = keys;
     int path = c->path_policy;
-    if (path == kPathAuto) path = N <= kGemvMaxRows ? kPathGemv : kPathTc;
+    if (path == kPathAuto) path = (N <= kGemvMaxRows || (N <= 8 && M <= kGemvMaxRowsWideM)) ? kPathGemv : kPathTc;
     if (path == kPathGemv && N > 8) path = kPathTc;
     if (path == kPathTc && (!tmA || N > c->tc_tpad || K > c->tc_kmax)) path = kPathSimt;
     TimedEvent* te;
@@ -394,7 +407,62 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
 }
 
 // One decode step for the rows already staged in dtok/dseq/dpos.
+// "auto" takes the persistent kernel at batch 1 only: its linear phases run
+// on CUDA cores, which fall behind the graph of GEMV kernels from batch 2 up.
+constexpr int kPersistentAutoMaxBatch = 1;
+bool use_persistent(const ZynferCuCtx* c, int B) {
+    if (!c->persistent_ok || B > kPersistentMaxBatch) return false;
+    if (c->schedule == kSchedKernels) return false;
+    return c->schedule == kSchedPersistent || B <= kPersistentAutoMaxBatch;
+}
+
+void enqueue_decode_persistent(ZynferCuCtx* c, int B, bool want_logits) {
+    const ZynferCuModelDesc& m = c->d;
+    PersistentArgs a{};
+    a.B = B; a.H = (int)m.hidden; a.I = (int)m.inter; a.V = (int)m.vocab; a.L = (int)m.layers;
+    a.n_q = (int)m.n_q; a.n_kv = (int)m.n_kv; a.eps = m.eps;
+    a.layers = c->dlayers;
+    a.embed = static_cast<const int8_t*>(c->embed); a.sembed = c->sembed; a.final_norm = c->final_norm;
+    a.rope = c->rope; a.rope_max_pos = (int)m.max_seq_len;
+    a.kv = c->kv; a.kv_layer_elems = c->kv_layer_elems;
+    a.block_table = c->table_dev; a.max_blocks = c->max_blocks; a.n_pool_blocks = c->n_blocks;
+    a.max_segs = decode_max_segs(c->max_blocks);
+    a.tok = c->dtok; a.seq_of = c->dseq; a.positions = c->dpos;
+    a.keys = c->dkeys; a.ids_out = c->dids; a.history = c->dhist; a.step = c->dstep;
+    a.x = c->dx; a.x1 = c->dx1; a.qkv = c->dqkv; a.attn = c->dattn; a.h = c->dh; a.partial = c->dpart;
+    a.logits = want_logits ? c->dlogits : nullptr;
+    a.counters = c->dcnt; a.sync = c->psync; a.err = c->derr;
+    const int tl = persistent_trace_len((int)m.layers);
+    if (c->timing && !c->ptrace && dalloc(c, &c->ptrace, (size_t)tl) != ZYNFER_CU_OK) c->ptrace = nullptr;
+    a.trace = c->timing ? c->ptrace : nullptr;
+    launch_decode_persistent(a, c->stream);
+    c->step_launches = 1;
+    if (a.trace) {
+        // phase p lasts from its start to the next phase's start (its grid barrier included)
+        c->ptrace_host.resize(tl);
+        if (cudaMemcpyAsync(c->ptrace_host.data(), c->ptrace, tl * 8, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
+            cudaStreamSynchronize(c->stream) != cudaSuccess)
+            return;
+        const uint64_t* t = c->ptrace_host.data();
+        const int phases = 5 * (int)m.layers + 1;
+        auto add = [&](int cls, uint64_t t0, uint64_t t1) {
+            c->t_ms[cls] += t1 > t0 ? (double)(t1 - t0) * 1e-6 : 0.0;
+            c->t_launch[cls] += 1;
+        };
+        add(ZYNFER_CU_K_OTHER, t[0], t[1]);
+        for (int p = 0; p < phases; ++p) {
+            const uint64_t start = t[1 + 2 * p], next = p + 1 < phases ? t[1 + 2 * (p + 1)] : t[3 + 2 * (phases - 1)];
+            const int cls = p == phases - 1 ? ZYNFER_CU_K_LMHEAD : (p % 5 == 1 ? ZYNFER_CU_K_ATTN : ZYNFER_CU_K_LINEAR);
+            add(cls, start, next);
+        }
+    }
+}
+
 void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
+    if (use_persistent(c, B)) {
+        enqueue_decode_persistent(c, B, want_logits);
+        return;
+    }
     const ZynferCuModelDesc& m = c->d;
     const int H = m.hidden, I = m.inter;
     c->step_launches = 0;
@@ -760,7 +828,7 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     ALLOC(c->dkeys, B);
     ALLOC(c->dids, B);
     ALLOC(c->dcnt, B * m.n_kv);
-    ALLOC(c->dpart, B * m.n_kv * (size_t)decode_max_segs(c->max_blocks) * 2 * (hd + 2));
+    ALLOC(c->dpart, B * m.n_kv * (size_t)decode_max_segs(c->max_blocks) * 2 * (hd + 4));
     c->hist_cap = std::max<size_t>(B * 4096, 1 << 16);
     ALLOC(c->dhist, c->hist_cap);
     ALLOC(c->dstep, 1);
@@ -794,6 +862,22 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     }
     if (!make_tmap_k_major(&c->tm_embed, c->embed, c->wkind, H, V, 128))
         return fail(c, ZYNFER_CU_INTERNAL, "cuTensorMapEncodeTiled failed for the embedding");
+    // persistent decode kernel: weight pointers per layer and its sync words
+    c->persistent_ok = q8 && H == 1024 && I == 3072 && c->qd == 2048 && persistent_supported(c->device);
+    if (c->persistent_ok) {
+        std::vector<PersistentLayer> pl(m.layers);
+        for (uint32_t l = 0; l < m.layers; ++l) {
+            const LayerDev& Ld = c->L[l];
+            pl[l] = PersistentLayer{static_cast<const int8_t*>(Ld.wqkv), static_cast<const int8_t*>(Ld.wo),
+                                    static_cast<const int8_t*>(Ld.wgu), static_cast<const int8_t*>(Ld.wd),
+                                    Ld.sqkv, Ld.so, Ld.sgu, Ld.sd, Ld.input_ln, Ld.post_ln, Ld.q_norm, Ld.k_norm};
+        }
+        if ((rc = dalloc(c, &c->dlayers, pl.size())) != ZYNFER_CU_OK) return rc;
+        ZC_CHECK(c, cudaMemcpy(c->dlayers, pl.data(), pl.size() * sizeof(PersistentLayer), cudaMemcpyHostToDevice),
+                 "persistent layer table");
+        if ((rc = dalloc(c, &c->psync, 3)) != ZYNFER_CU_OK) return rc;
+        cudaMemset(c->psync, 0, 3 * sizeof(unsigned));
+    }
     if ((rc = halloc(c, &c->herr, 1)) != ZYNFER_CU_OK) return rc;
     if ((rc = halloc(c, &c->hio, 3 * B)) != ZYNFER_CU_OK) return rc;
     if ((rc = halloc(c, &c->hids, B)) != ZYNFER_CU_OK) return rc;
@@ -1049,11 +1133,12 @@ int zynfer_cu_decode_step(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* 
     set_io_views(c, (int)batch);
     if ((rc = stage_batch(c, seqs, tokens, batch))) return rc;
     ZC_CHECK(c, cudaMemsetAsync(c->dstep, 0, 4, c->stream), "step counter");
-    const bool eager = logits != nullptr || c->timing;
+    const bool persistent = use_persistent(c, (int)batch);
+    const bool eager = logits != nullptr || c->timing || persistent;
     cudaEventRecord(c->ev0, c->stream);
     if (eager) {
         enqueue_decode(c, (int)batch, logits != nullptr);
-        c->path = batch <= 8 ? "decode:gemv:eager" : "decode:gemm:eager";
+        c->path = persistent ? "decode:persistent" : (batch <= 8 ? "decode:gemv:eager" : "decode:gemm:eager");
     } else {
         cudaGraphExec_t g;
         if ((rc = get_graph(c, (int)batch, &g))) return rc;
@@ -1096,11 +1181,12 @@ int zynfer_cu_generate(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* fir
     set_io_views(c, (int)batch);
     if ((rc = stage_batch(c, seqs, first, batch))) return rc;
     ZC_CHECK(c, cudaMemsetAsync(c->dstep, 0, 4, c->stream), "step counter");
+    const bool persistent = use_persistent(c, (int)batch);
     cudaGraphExec_t g = nullptr;
-    if (!c->timing && (rc = get_graph(c, (int)batch, &g))) return rc;
+    if (!c->timing && !persistent && (rc = get_graph(c, (int)batch, &g))) return rc;
     cudaEventRecord(c->ev0, c->stream);
     for (uint32_t s = 0; s < steps; ++s) {
-        if (c->timing) enqueue_decode(c, (int)batch, false);
+        if (c->timing || persistent) enqueue_decode(c, (int)batch, false);
         else ZC_CHECK(c, cudaGraphLaunch(g, c->stream), "graph launch");
     }
     cudaEventRecord(c->ev1, c->stream);
@@ -1113,7 +1199,8 @@ int zynfer_cu_generate(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* fir
     c->last_step_ns = (uint64_t)(ms * 1e6 / steps);
     ZC_CHECK(c, cudaMemcpy(out_ids, c->dhist, (size_t)steps * batch * 4, cudaMemcpyDeviceToHost), "history");
     for (uint32_t i = 0; i < batch; ++i) c->seq_len[seqs[i]] += steps;
-    c->path = std::string(batch <= 8 ? "generate:gemv" : "generate:gemm") + (c->timing ? ":eager" : ":graph");
+    c->path = persistent ? std::string("generate:persistent")
+                         : std::string(batch <= 8 ? "generate:gemv" : "generate:gemm") + (c->timing ? ":eager" : ":graph");
     return ZYNFER_CU_OK;
 }
 
@@ -1222,6 +1309,21 @@ int zynfer_cu_set_linear_path(ZynferCuCtx* c, const char* path) {
     return ZYNFER_CU_OK;
 }
 
+int zynfer_cu_set_decode_schedule(ZynferCuCtx* c, const char* schedule) {
+    if (!c || !schedule) return ZYNFER_CU_INVALID;
+    if (!strcmp(schedule, "auto")) c->schedule = kSchedAuto;
+    else if (!strcmp(schedule, "kernels")) c->schedule = kSchedKernels;
+    else if (!strcmp(schedule, "persistent")) {
+        if (c->ready && !c->persistent_ok)
+            return fail(c, ZYNFER_CU_UNSUPPORTED, "the persistent decode kernel needs int8 weights, hidden 1024, "
+                                                  "intermediate 3072, 2048 query dims and cooperative launch");
+        c->schedule = kSchedPersistent;
+    } else {
+        return fail(c, ZYNFER_CU_INVALID, std::string("unknown decode schedule ") + schedule);
+    }
+    return ZYNFER_CU_OK;
+}
+
 int zynfer_cu_pack_q8(ZynferCuCtx* c, const float* w, uint32_t rows, uint32_t cols, int8_t* q, float* scale) {
     if (!c || c->device < 0) return ZYNFER_CU_INVALID;
     if (!w || !q || !scale || rows == 0 || cols == 0) return fail(c, ZYNFER_CU_INVALID, "bad pack arguments");
@@ -1283,6 +1385,14 @@ int zynfer_cu_kernel_time(const ZynferCuCtx* cc, int cls, uint64_t* launches, do
 }
 
 uint64_t zynfer_cu_last_step_ns(const ZynferCuCtx* c) { return c ? c->last_step_ns : 0; }
+
+int zynfer_cu_phase_trace(const ZynferCuCtx* c, uint64_t* out, int cap) {
+    if (!c) return 0;
+    const int n = (int)c->ptrace_host.size();
+    if (out)
+        for (int i = 0; i < n && i < cap; ++i) out[i] = c->ptrace_host[i];
+    return n;
+}
 
 int zynfer_cu_step_launches(const ZynferCuCtx* c) { return c ? c->step_launches : 0; }
 

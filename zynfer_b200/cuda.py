@@ -101,6 +101,8 @@ _SIGS = {
     "zynfer_cu_block_forward": (C.c_int, [VP, U32, U32, VP, U32, VP]),
     "zynfer_cu_linear": (C.c_int, [VP, C.c_int, VP, VP, VP, U32, U32, U32, VP]),
     "zynfer_cu_set_linear_path": (C.c_int, [VP, C.c_char_p]),
+    "zynfer_cu_set_decode_schedule": (C.c_int, [VP, C.c_char_p]),
+    "zynfer_cu_phase_trace": (C.c_int, [VP, VP, C.c_int]),
     "zynfer_cu_linear_q8_static": (C.c_int, [VP, VP, VP, U32, U32, U32, VP, VP]),
     "zynfer_cu_pack_q8": (C.c_int, [VP, VP, U32, U32, VP, VP]),
     "zynfer_cu_rmsnorm": (C.c_int, [VP, VP, VP, U32, U32, C.c_float, VP]),
@@ -228,6 +230,18 @@ class Gpu:
     def set_linear_path(self, path: str):
         """"auto" | "gemv" | "tcgen05" | "simt"."""
         self.check(lib().zynfer_cu_set_linear_path(self.h, path.encode()))
+
+    def phase_trace(self):
+        """Phase timestamps (ns) of the last persistent decode step run with timing on."""
+        n = lib().zynfer_cu_phase_trace(self.h, None, 0)
+        out = np.zeros(max(n, 0), np.uint64)
+        if n > 0:
+            lib().zynfer_cu_phase_trace(self.h, _ptr(out), n)
+        return out
+
+    def set_decode_schedule(self, schedule: str):
+        """"auto" | "kernels" | "persistent" (one cooperative kernel per decode step)."""
+        self.check(lib().zynfer_cu_set_decode_schedule(self.h, schedule.encode()))
 
     def pack_q8(self, w, rows, cols, q, scale):
         self.check(lib().zynfer_cu_pack_q8(self.h, _ptr(w), rows, cols, _ptr(q), _ptr(scale)))
