@@ -155,7 +155,8 @@ ZYNFER_CU_API int zynfer_cu_block_forward(ZynferCuCtx *ctx, uint32_t layer, uint
                             uint32_t t, float *out);
 
 /* ---- op level (device pointers; run on the context stream) ---- */
-/* matvecQ8 / matmul over `batch` rows (ops.zig:181-197): y[b][m] = (W[m,:] . x[b,:]) * scale[m]. */
+/* matvecQ8 / matmul over `batch` rows (ops.zig:181-197): y[b][m] = (W[m,:] . x[b,:]) * scale[m].
+ * x must be 16-byte aligned and y 8-byte aligned. */
 ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, const float *scale,
                      const float *x, uint32_t batch, uint32_t m, uint32_t k, float *y);
 /* Kernel family for linear layers: "auto" (CUDA-core GEMV for <= 4 rows,
@@ -182,7 +183,7 @@ ZYNFER_CU_API int zynfer_cu_set_decode_schedule(ZynferCuCtx *ctx, const char *sc
  * row scales, 768 KiB) is a file-scope device array that every GPU loading
  * the library holds until the process exits.
  * Limits: batch <= ZYNFER_CU_STATIC_MAX_ROWS, k <= ZYNFER_CU_STATIC_MAX_K,
- * k and m multiples of 128; otherwise ZYNFER_CU_INVALID.
+ * k and m multiples of 128, x 16-byte aligned; otherwise ZYNFER_CU_INVALID.
  * The first call on a device resolves the array's device address and sets
  * kernel attributes on that device; make it before any stream capture. All
  * calls share the array, so calls that overlap on the GPU (other streams,

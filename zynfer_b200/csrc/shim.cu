@@ -371,7 +371,7 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
     int path = c->path_policy;
     if (path == kPathAuto) path = (N <= kGemvMaxRows || (N <= 8 && M <= kGemvMaxRowsWideM)) ? kPathGemv : kPathTc;
     if (path == kPathGemv && N > 8) path = kPathTc;
-    if (path == kPathTc && (!tmA || N > c->tc_tpad || K > c->tc_kmax)) path = kPathSimt;
+    if (path == kPathTc && (!tmA || N > c->tc_tpad || K > c->tc_kmax || K > kPlanesMaxK)) path = kPathSimt;
     TimedEvent* te;
     tbegin(c, cls, &te);
     if (path == kPathGemv) {
@@ -395,12 +395,13 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
         L.tmB = b_map(c, wkind, K, nt);
         L.args = TcArgs{M, K, N, c->tc_tpad, wkind, epi, s, c->exps, y, a.ldy, resid, keys, c->tc_acc, c->tc_cnt,
                         c->derr};
-        int splits = tc_splits(M, N, K, wkind, c->caps.sm_count > 0 ? c->caps.sm_count : 148);
-        if (N > kAccT || (size_t)splits * kAccT * M * 8 > c->tc_acc_bytes || (M / 128) * ((N + nt - 1) / nt) > 8192)
-            splits = 1;
-        L.splits = splits;
+        L.splits = 1;
         L.sms = c->caps.sm_count > 0 ? c->caps.sm_count : 148;
-        if (L.tmB) launch_tc_gemm(L, c->stream);
+        const int S = tc_cluster_size(M, N, K, wkind, epi, L.sms);
+        if (L.tmB) {
+            if (S > 1) launch_tc_cluster(L, S, c->stream);
+            else launch_tc_gemm(L, c->stream);
+        }
         c->step_launches += 2;
     }
     tend(c, te);
@@ -1270,6 +1271,8 @@ int zynfer_cu_linear(ZynferCuCtx* c, int wkind, const void* w, const float* scal
     if (wkind != ZYNFER_CU_W_Q8 && wkind != ZYNFER_CU_W_BF16) return fail(c, ZYNFER_CU_INVALID, "unknown weight kind");
     if (wkind == ZYNFER_CU_W_Q8 && !scale) return fail(c, ZYNFER_CU_INVALID, "int8 weights need scales");
     if (k % 512) return fail(c, ZYNFER_CU_UNSUPPORTED, "k must be a multiple of 512");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 8)
+        return fail(c, ZYNFER_CU_INVALID, "x must be 16-byte and y 8-byte aligned");
     if (m % 128) return fail(c, ZYNFER_CU_UNSUPPORTED, "m must be a multiple of 128");
     if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
     cudaSetDevice(c->device);

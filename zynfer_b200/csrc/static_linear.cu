@@ -61,6 +61,7 @@ int setup_device(int dev, DeviceScratch** out) {
 extern "C" int zynfer_cu_linear_q8_static(const int8_t* w, const float* scale, const float* x, uint32_t batch,
                                           uint32_t m, uint32_t k, float* y, void* stream) {
     if (!w || !scale || !x || !y) return ZYNFER_CU_INVALID;
+    if (reinterpret_cast<uintptr_t>(x) % 16) return ZYNFER_CU_INVALID;  // rows are read as float4
     if (batch == 0 || batch > (uint32_t)kMaxRows || k == 0 || k > (uint32_t)kMaxK || k % 128 || m == 0 || m % 128)
         return ZYNFER_CU_INVALID;
     int dev = 0;

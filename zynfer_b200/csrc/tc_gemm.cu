@@ -418,74 +418,331 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
 }
 
 
+// ------------------------------------------------- cluster split-K kernel
+//
+// For linears with few (M, N) tiles (batched decode: M = 1024..6144 rows,
+// T <= 64 tokens), one tile per thread-block cluster of S CTAs along K: CTA
+// `rank` runs the same TMA -> tcgen05 pipeline over its K blocks
+// [rank nkb / S, (rank + 1) nkb / S) into its own TMEM accumulator, writes
+// the exact per-(token, row) values (int8: 64-bit integers; bf16: f64) to
+// its shared memory, and after a cluster barrier reduces rows
+// [r0(rank), r0(rank + 1)) of the tile by reading all S copies through
+// distributed shared memory (ld.shared::cluster) in rank order. The result
+// equals the single-CTA kernel's bit for bit. No global scratch, no atomics.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    __syncwarp();  // the .aligned barrier wants every warp converged
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void ld_cluster_s64x2(uint32_t addr, long long& v0, long long& v1) {
+    asm volatile("ld.shared::cluster.v2.s64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "r"(addr) : "memory");
+}
+constexpr int kMaxCluster = 8;  // portable cluster size
+
+template <int WK, int NT, int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                  const __grid_constant__ CUtensorMap tmB,
+                                                                  TcArgs a) {
+    constexpr int P = WK == kWQ8 ? 3 : 2;
+    constexpr int N = P * NT;
+    constexpr int A_BYTES = kBM * kKB;
+    constexpr int B_BYTES = N * kKB;
+    constexpr int STAGE = A_BYTES + B_BYTES;
+    constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
+    constexpr uint32_t TMEM_COLS = N <= 32 ? 32 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));
+    constexpr int KSTEP = 32;
+    static_assert(NT % 16 == 0 && N <= 256 && STAGES >= 2, "tile shape");
+    static_assert((size_t)NT * kBM * 8 <= (size_t)STAGES * STAGE, "partial tile must fit in the stages");
+    static_assert(EPI != kEpiArgmax, "the cluster kernel has no argmax epilogue");
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tmem_full = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+    long long* part = reinterpret_cast<long long*>(smem);  // [NT][kBM], after the last MMA
+
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    pdl_launch_dependents();
+    const int S = (int)cluster_size(), rank = (int)cluster_rank();
+    const int m_tiles = a.M / kBM;
+    const int tile = blockIdx.x / S;
+    const int mt = tile % m_tiles, nt = tile / m_tiles;
+    const int nkb = a.K * (WK == kWQ8 ? 1 : 2) / kKB;
+    const int kb0 = (int)((long)rank * nkb / S), kb1 = (int)((long)(rank + 1) * nkb / S);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tmem_full, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // weights first (they do not depend on the previous kernel), then the planes
+            const int npre = min(STAGES, kb1 - kb0);
+            for (int i = 0; i < npre; ++i) {
+                mbar_arrive_expect_tx(&full[i], STAGE);
+                tma_load_2d(smem + i * STAGE, &tmA, (kb0 + i) * (WK == kWQ8 ? kKB : kKB / 2), mt * kBM, &full[i]);
+            }
+            pdl_wait();
+            for (int i = 0; kb0 + i < kb1; ++i) {
+                const int kb = kb0 + i, s = i % STAGES, round = i / STAGES;
+                uint8_t* as = smem + s * STAGE;
+                uint8_t* bs = as + A_BYTES;
+                const int kx = kb * (WK == kWQ8 ? kKB : kKB / 2);
+                if (i >= npre) {
+                    if (!mbar_wait_bounded(&empty[s], (uint32_t)((round & 1) ^ 1), a.err)) break;
+                    mbar_arrive_expect_tx(&full[s], STAGE);
+                    tma_load_2d(as, &tmA, kx, mt * kBM, &full[s]);
+                }
+#pragma unroll
+                for (int p = 0; p < P; ++p) tma_load_2d(bs + p * NT * kKB, &tmB, kx, p * a.t_pad + nt * NT, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = make_idesc<WK>(N);
+            for (int i = 0; kb0 + i < kb1; ++i) {
+                const int s = i % STAGES, round = i / STAGES;
+                if (!mbar_wait_bounded(&full[s], (uint32_t)(round & 1), a.err)) break;
+                tc_fence_after();
+                const uint32_t as = smem_addr(smem + s * STAGE);
+                const uint32_t bs = as + A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < kKB / KSTEP; ++kk)
+                    mma_issue<WK>(tmem_base, sdesc_sw128(as + kk * KSTEP), sdesc_sw128(bs + kk * KSTEP), idesc,
+                                  (i > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&empty[s]);
+            }
+            mma_commit(tmem_full);  // also fires when no MMA was issued
+        }
+    } else {
+        // this CTA's exact values -> shared memory [t][row]
+        const int q = warp & 3, h = (warp - 2) >> 2;
+        const bool ok = mbar_wait_bounded(tmem_full, 0u, a.err);
+        tc_fence_after();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // stages were TMA / MMA operands
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16);
+        const int row = q * 32 + lane;
+        for (int t0 = 16 * h; t0 < NT; t0 += 32) {
+            uint32_t r[P][16];
+#pragma unroll
+            for (int p = 0; p < P; ++p) tmem_ld16(tbase + p * NT + t0, r[p]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+                long long v;
+                if constexpr (WK == kWQ8) {
+                    v = (long long)(int)r[0][jj] * 65536ll + (long long)(int)r[1][jj] * 256ll + (long long)(int)r[2][jj];
+                } else {
+                    v = __double_as_longlong((double)__uint_as_float(r[0][jj]) + (double)__uint_as_float(r[1][jj]));
+                }
+                part[(t0 + jj) * kBM + row] = ok ? v : 0ll;
+            }
+        }
+        tc_fence_before();
+    }
+    cluster_sync_all();  // every rank's values are in its shared memory
+
+    if (warp >= 2) {
+        pdl_wait();  // residual and row scales come from earlier kernels
+        const int e = threadIdx.x - 64;  // 0 .. 255
+        const int r0 = 2 * ((rank * (kBM / 2)) / S), r1 = 2 * (((rank + 1) * (kBM / 2)) / S);
+        const int pairs = (r1 - r0) / 2;
+        const int n0 = nt * NT, m0 = mt * kBM;
+        uint32_t rb[kMaxCluster];  // every rank's partial tile in the cluster's shared window
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxCluster; ++s2) rb[s2] = s2 < S ? map_rank(smem_addr(part), (uint32_t)s2) : 0u;
+        // thread = (token, row pair); all S copies of the pair are loaded before the rank-order sum
+        for (int idx = e; idx < pairs * NT; idx += 256) {
+            const int t = idx / pairs, row = r0 + 2 * (idx % pairs);
+            if (n0 + t >= a.T) continue;
+            const uint32_t off = (uint32_t)((t * kBM + row) * 8);
+            long long x0[kMaxCluster], x1[kMaxCluster];
+#pragma unroll
+            for (int s2 = 0; s2 < kMaxCluster; ++s2)
+                if (s2 < S) ld_cluster_s64x2(rb[s2] + off, x0[s2], x1[s2]);
+            long long vi[2] = {0, 0};
+            double vd[2] = {0.0, 0.0};
+#pragma unroll
+            for (int s2 = 0; s2 < kMaxCluster; ++s2) {
+                if (s2 >= S) break;
+                if constexpr (WK == kWQ8) {
+                    vi[0] += x0[s2];
+                    vi[1] += x1[s2];
+                } else {
+                    vd[0] += __longlong_as_double(x0[s2]);
+                    vd[1] += __longlong_as_double(x1[s2]);
+                }
+            }
+            float y[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                if constexpr (WK == kWQ8)
+                    y[u] = __fmul_rn(__fmul_rn(__ll2float_rn(vi[u]), __ldg(a.xscale + n0 + t)), __ldg(a.scale + m0 + row + u));
+                else
+                    y[u] = (float)vd[u];
+            }
+            const size_t o = (size_t)(n0 + t) * a.ldy;
+            if constexpr (EPI == kEpiSwiGLU) {
+                a.y[o + ((m0 + row) >> 1)] = __fmul_rn(silu(y[0]), y[1]);
+            } else if constexpr (EPI == kEpiResid) {
+                const float2 rs = *reinterpret_cast<const float2*>(a.resid + o + m0 + row);
+                *reinterpret_cast<float2*>(a.y + o + m0 + row) = make_float2(__fadd_rn(rs.x, y[0]), __fadd_rn(rs.y, y[1]));
+            } else {
+                *reinterpret_cast<float2*>(a.y + o + m0 + row) = make_float2(y[0], y[1]);
+            }
+        }
+    }
+    tc_fence_before();
+    cluster_sync_all();  // no rank leaves while another still reads its shared memory
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
 // --------------------------------------------------- activation planes
 
+// One CTA per activation row, every value loaded once into registers
+// (K <= kPrepMaxK): one block reduction gives sum(x^2) and max|w x| (the
+// RMSNorm scale is a positive constant and rounding keeps the order, so
+// max |(w x) inv| = max|w x| * inv exactly), then the planes are written from
+// the registers. RMSNorm as ops.zig:49-67: (w * x) * 1/sqrt(mean(x^2) + eps).
+constexpr int kPrepThreads = 256;
+constexpr int kPrepMaxK = kPlanesMaxK;
+constexpr int kPrepVec = kPrepMaxK / (4 * kPrepThreads);  // float4 per thread
 template <int WK>
-__global__ void __launch_bounds__(256) prep_planes_kernel(PlanesArgs a) {
+__global__ void __launch_bounds__(kPrepThreads) prep_planes_kernel(PlanesArgs a) {
     pdl_launch_dependents();
     pdl_wait();
+    __shared__ float red_ss[kPrepThreads / kWarp], red_mx[kPrepThreads / kWarp];
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     const int t = blockIdx.x;
-    const int K = a.K;
+    const int K = a.K;  // multiple of 128, <= kPrepMaxK
     const float* xr = a.x + (size_t)t * a.ldx;
-    __shared__ float red[8];
-    __shared__ float bcast;
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    float inv = 1.0f;
-    if (a.norm_w) {  // RMSNorm prologue (ops.zig:49-67)
-        float acc = 0.0f;
-        for (int k = threadIdx.x; k < K; k += 256) acc += xr[k] * xr[k];
-        acc = warp_sum(acc);
-        if (lane == 0) red[warp] = acc;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float tot = 0.0f;
-            for (int w = 0; w < 8; ++w) tot += red[w];
-            bcast = 1.0f / sqrtf(tot / (float)K + a.eps);
+    float4 v[kPrepVec], w[kPrepVec];
+    float ss = 0.0f, mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPrepVec; ++i) {
+        const int k = 4 * (threadIdx.x + i * kPrepThreads);
+        if (k < K) {
+            v[i] = *reinterpret_cast<const float4*>(xr + k);
+            w[i] = a.norm_w ? __ldg(reinterpret_cast<const float4*>(a.norm_w + k)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        } else {
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            w[i] = v[i];
         }
-        __syncthreads();
-        inv = bcast;
     }
-    auto val = [&](int k) -> float {
-        const float v = xr[k];
-        return a.norm_w ? __fmul_rn(__fmul_rn(a.norm_w[k], v), inv) : v;
-    };
+#pragma unroll
+    for (int i = 0; i < kPrepVec; ++i) {
+        ss += v[i].x * v[i].x;
+        ss += v[i].y * v[i].y;
+        ss += v[i].z * v[i].z;
+        ss += v[i].w * v[i].w;
+        const float4 p = a.norm_w ? make_float4(__fmul_rn(w[i].x, v[i].x), __fmul_rn(w[i].y, v[i].y),
+                                                __fmul_rn(w[i].z, v[i].z), __fmul_rn(w[i].w, v[i].w))
+                                  : v[i];
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
+    }
+    ss = warp_sum(ss);
+    mx = warp_max(mx);
+    if (lane == 0) {
+        red_ss[warp] = ss;
+        red_mx[warp] = mx;
+    }
+    __syncthreads();
+    ss = 0.0f;
+    mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPrepThreads / kWarp; ++i) {
+        ss += red_ss[i];
+        mx = fmaxf(mx, red_mx[i]);
+    }
+    float inv = 1.0f;
+    if (a.norm_w) {
+        inv = 1.0f / sqrtf(ss / (float)K + a.eps);
+        mx = __fmul_rn(mx, inv);
+    }
+    auto val = [&](float wv, float xv) -> float { return a.norm_w ? __fmul_rn(__fmul_rn(wv, xv), inv) : xv; };
+    const size_t plane = (size_t)a.t_pad * K;
     if constexpr (WK == kWQ8) {
-        float mx = 0.0f;
-        for (int k = threadIdx.x; k < K; k += 256) mx = fmaxf(mx, fabsf(val(k)));
-        mx = warp_max(mx);
-        __syncthreads();
-        if (lane == 0) red[warp] = mx;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float m = 0.0f;
-            for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w]);
-            bcast = m;
-        }
-        __syncthreads();
         int e = 0;
-        if (bcast > 0.0f) frexpf(bcast, &e);  // max|x| < 2^e
+        if (mx > 0.0f) frexpf(mx, &e);  // max|x| < 2^e
         if (threadIdx.x == 0) a.xscale[t] = ldexpf(1.0f, e - 22);  // exact power of two
         int8_t* p0 = reinterpret_cast<int8_t*>(a.planes) + (size_t)t * K;
-        const size_t plane = (size_t)a.t_pad * K;
-        for (int k = threadIdx.x; k < K; k += 256) {
-            const int v = __float2int_rn(ldexpf(val(k), 22 - e));  // |v| <= 2^22
-            const int d2 = (int)(int8_t)(v & 0xFF);
-            const int v1 = (v - d2) >> 8;
-            const int d1 = (int)(int8_t)(v1 & 0xFF);
-            const int d0 = (v1 - d1) >> 8;  // |d0| <= 64
-            p0[k] = (int8_t)d0;
-            p0[plane + k] = (int8_t)d1;
-            p0[2 * plane + k] = (int8_t)d2;
+#pragma unroll
+        for (int i = 0; i < kPrepVec; ++i) {
+            const int k = 4 * (threadIdx.x + i * kPrepThreads);
+            if (k >= K) break;
+            const float f[4] = {val(w[i].x, v[i].x), val(w[i].y, v[i].y), val(w[i].z, v[i].z), val(w[i].w, v[i].w)};
+            char4 d0, d1, d2;
+            int8_t* o0 = &d0.x;
+            int8_t* o1 = &d1.x;
+            int8_t* o2 = &d2.x;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int q = __float2int_rn(ldexpf(f[j], 22 - e));  // |q| <= 2^22
+                const int q2 = (int)(int8_t)(q & 0xFF);
+                const int q1v = (q - q2) >> 8;
+                const int q1 = (int)(int8_t)(q1v & 0xFF);
+                const int q0 = (q1v - q1) >> 8;  // |q0| <= 64
+                o0[j] = (int8_t)q0;
+                o1[j] = (int8_t)q1;
+                o2[j] = (int8_t)q2;
+            }
+            *reinterpret_cast<char4*>(p0 + k) = d0;
+            *reinterpret_cast<char4*>(p0 + plane + k) = d1;
+            *reinterpret_cast<char4*>(p0 + 2 * plane + k) = d2;
         }
     } else {
         uint16_t* p0 = reinterpret_cast<uint16_t*>(a.planes) + (size_t)t * K;
-        const size_t plane = (size_t)a.t_pad * K;
-        for (int k = threadIdx.x; k < K; k += 256) {
-            const float v = val(k);
-            const uint16_t hi = f32_to_bf16_rne(v);
-            const float hif = __uint_as_float((uint32_t)hi << 16);
-            p0[k] = hi;
-            p0[plane + k] = f32_to_bf16_rne(__fsub_rn(v, hif));
+#pragma unroll
+        for (int i = 0; i < kPrepVec; ++i) {
+            const int k = 4 * (threadIdx.x + i * kPrepThreads);
+            if (k >= K) break;
+            const float f[4] = {val(w[i].x, v[i].x), val(w[i].y, v[i].y), val(w[i].z, v[i].z), val(w[i].w, v[i].w)};
+            ushort4 hi, lo;
+            uint16_t* h = &hi.x;
+            uint16_t* l = &lo.x;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                h[j] = f32_to_bf16_rne(f[j]);
+                l[j] = f32_to_bf16_rne(__fsub_rn(f[j], __uint_as_float((uint32_t)h[j] << 16)));
+            }
+            *reinterpret_cast<ushort4*>(p0 + k) = hi;
+            *reinterpret_cast<ushort4*>(p0 + plane + k) = lo;
         }
     }
 }
@@ -496,6 +753,45 @@ constexpr size_t tile_smem() {
     constexpr int STAGE = kBM * kKB + P * NT * kKB;
     constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
     return (size_t)STAGES * STAGE + 1024 + (2 * STAGES + 4) * 8 + 16;
+}
+
+template <int WK, int NT, int EPI>
+void launch_cluster_tile(const TcLaunch& L, int S, cudaStream_t st) {
+    constexpr size_t smem = tile_smem<WK, NT>();
+    TcArgs args = L.args;
+    args.splits = 1;
+    const int tiles = (args.M / kBM) * ((args.T + NT - 1) / NT);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles * S);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, tc_cluster_kernel<WK, NT, EPI>, *L.tmA, *L.tmB, args);
+}
+
+template <int WK, int NT>
+void launch_cluster_epi(const TcLaunch& L, int S, cudaStream_t st) {
+    switch (L.args.epi) {
+        case kEpiResid: launch_cluster_tile<WK, NT, kEpiResid>(L, S, st); break;
+        case kEpiSwiGLU: launch_cluster_tile<WK, NT, kEpiSwiGLU>(L, S, st); break;
+        default: launch_cluster_tile<WK, NT, kEpiNone>(L, S, st); break;
+    }
+}
+
+template <int WK, int NT>
+void prepare_cluster_tile() {
+    configure_kernel((const void*)tc_cluster_kernel<WK, NT, kEpiNone>, tile_smem<WK, NT>());
+    configure_kernel((const void*)tc_cluster_kernel<WK, NT, kEpiResid>, tile_smem<WK, NT>());
+    configure_kernel((const void*)tc_cluster_kernel<WK, NT, kEpiSwiGLU>, tile_smem<WK, NT>());
 }
 
 template <int WK, int NT>
@@ -537,6 +833,8 @@ int tc_tile_tokens(int wkind, int T) {
 }
 
 void prepare_tc_kernels() {
+    prepare_cluster_tile<kWQ8, 16>(); prepare_cluster_tile<kWQ8, 32>(); prepare_cluster_tile<kWQ8, 64>();
+    prepare_cluster_tile<kWBF16, 16>(); prepare_cluster_tile<kWBF16, 32>(); prepare_cluster_tile<kWBF16, 64>();
     prepare_tile<kWQ8, 16>(); prepare_tile<kWQ8, 32>(); prepare_tile<kWQ8, 64>();
     prepare_tile<kWBF16, 16>(); prepare_tile<kWBF16, 32>(); prepare_tile<kWBF16, 64>(); prepare_tile<kWBF16, 128>();
     configure_kernel((const void*)prep_planes_kernel<kWQ8>, 0);
@@ -544,8 +842,8 @@ void prepare_tc_kernels() {
 }
 
 void launch_prep_planes(const PlanesArgs& a, cudaStream_t st) {
-    if (a.wkind == kWQ8) launch_pdl(prep_planes_kernel<kWQ8>, a.T, 256, 0, st, a);
-    else launch_pdl(prep_planes_kernel<kWBF16>, a.T, 256, 0, st, a);
+    if (a.wkind == kWQ8) launch_pdl(prep_planes_kernel<kWQ8>, a.T, kPrepThreads, 0, st, a);
+    else launch_pdl(prep_planes_kernel<kWBF16>, a.T, kPrepThreads, 0, st, a);
 }
 
 void launch_tc_gemm(const TcLaunch& L, cudaStream_t st) {
@@ -562,6 +860,35 @@ void launch_tc_gemm(const TcLaunch& L, cudaStream_t st) {
             case 32: launch_epi<kWBF16, 32>(L, st); break;
             case 64: launch_epi<kWBF16, 64>(L, st); break;
             default: launch_epi<kWBF16, 128>(L, st); break;
+        }
+    }
+}
+
+int tc_cluster_size(int M, int T, int K, int wkind, int epi, int sms) {
+    const int nt = tc_tile_tokens(wkind, T);
+    if (nt > 64 || epi == kEpiArgmax) return 1;
+    const int tiles = (M / kBM) * ((T + nt - 1) / nt);
+    if (2 * tiles > sms) return 1;  // enough tiles to fill the GPU without splitting K
+    const int nkb = K * (wkind == kWQ8 ? 1 : 2) / kKB;
+    // powers of two pack into the GPCs without leaving clusters for a second wave
+    int S = 1;
+    while (2 * S <= std::min({sms / tiles, kMaxCluster, nkb})) S *= 2;
+    return S;
+}
+
+void launch_tc_cluster(const TcLaunch& L, int S, cudaStream_t st) {
+    const int nt = tc_tile_tokens(L.args.wkind, L.args.T);
+    if (L.args.wkind == kWQ8) {
+        switch (nt) {
+            case 16: launch_cluster_epi<kWQ8, 16>(L, S, st); break;
+            case 32: launch_cluster_epi<kWQ8, 32>(L, S, st); break;
+            default: launch_cluster_epi<kWQ8, 64>(L, S, st); break;
+        }
+    } else {
+        switch (nt) {
+            case 16: launch_cluster_epi<kWBF16, 16>(L, S, st); break;
+            case 32: launch_cluster_epi<kWBF16, 32>(L, S, st); break;
+            default: launch_cluster_epi<kWBF16, 64>(L, S, st); break;
         }
     }
 }

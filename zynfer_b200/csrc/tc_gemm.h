@@ -22,6 +22,7 @@ struct PlanesArgs {
     float* xscale;  // int8 only: 2^(e - 22) per row
 };
 
+constexpr int kPlanesMaxK = 4096;  // activation rows the plane kernel holds in registers
 constexpr int kAccT = 64;  // split-K accumulator rows per plane (split-K only for T <= 64)
 
 struct TcArgs {
@@ -54,5 +55,9 @@ bool make_tmap_k_major(CUtensorMap* map, const void* base, int wkind, uint64_t k
                        uint32_t box_rows);
 void launch_prep_planes(const PlanesArgs& a, cudaStream_t st);
 void launch_tc_gemm(const TcLaunch& L, cudaStream_t st);
+// Cluster split-K variant for narrow problems: CTAs per cluster along K
+// (1 = use launch_tc_gemm), and its launcher (no argmax epilogue, T <= 64).
+int tc_cluster_size(int M, int T, int K, int wkind, int epi, int sms);
+void launch_tc_cluster(const TcLaunch& L, int S, cudaStream_t st);
 
 }  // namespace zc
