@@ -40,6 +40,11 @@ METRIC = "Qwen3-0.6B int8 decode tok/s"
 N_SEQS = 64
 SEED = 20250601
 KV_BYTES_PER_TOKEN_LAYER = 2 * 8 * 128 * 2  # K + V, 8 kv heads, d = 128, bf16
+# DRAM bytes (read + write) per algorithmic byte of attn_decode_kernel, from one
+# ncu capture of 32 sequences at context 2048 (profiles/attn_decode_b32_ctx2048.txt:
+# 275.4 MB for 269.3 MB); the traffic grows with the KV bytes, so a launch of this
+# workload moves about this ratio times its algorithmic bytes.
+ATTN_TRAFFIC_RATIO = 275.43 / 269.3
 
 
 def parse():
@@ -286,7 +291,10 @@ def run_ours(args):
                     "d2h_bytes_per_step": int(d2h_all), "steps": args.e2e_steps},
             "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel", "achieved": round(achieved_all, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(achieved_all / peak, 4), "traffic": None,
+                         "frac": round(achieved_all / peak, 4),
+                         "traffic": int(ATTN_TRAFFIC_RATIO * attn_bytes),
+                         "traffic_source": "ncu dram read+write of a 32-sequence, context-2048 launch, "
+                                           "scaled by KV bytes",
                          "bytes_per_launch": int(attn_bytes), "avg_launch_ms": round(attn_avg_ms, 5),
                          "launches_timed": n_attn,
                          "note": "CUDA events around each attention launch in an instrumented pass of "

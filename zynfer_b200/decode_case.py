@@ -15,6 +15,7 @@ from __future__ import annotations
 import argparse
 import dataclasses
 import json
+import time
 
 KV_BYTES_PER_TOKEN_HEAD = 2 * 128 * 2  # K and V rows, bf16
 
@@ -28,6 +29,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--path", default="auto", help="linear kernel family (auto, gemv, tcgen05, simt)")
+    ap.add_argument("--schedule", default="auto", help="decode schedule (auto, kernels, persistent)")
+    ap.add_argument("--window", default="decode", choices=["decode", "prefill"],
+                    help="what runs between cudaProfilerStart/Stop: the timed decode steps, or one more prefill")
+    ap.add_argument("--weights", default="q8", choices=["q8", "bf16"])
     args = ap.parse_args()
 
     import torch
@@ -39,11 +44,25 @@ def main():
     B = args.seqs
     total = args.warmup + 2 * args.steps + 2
     gpu = zc.Gpu(0)
-    model = zc.Model(gpu, arch, zc.W_Q8, max_batch=B, max_seqs=B, max_seq_len=args.ctx + total + 16,
+    wk = zc.W_Q8 if args.weights == "q8" else zc.W_BF16
+    model = zc.Model(gpu, arch, wk, max_batch=B, max_seqs=B, max_seq_len=args.ctx + total + 16,
                      max_prefill=args.ctx)
     model.fill_synthetic(args.seed, 0.02, 0.0)
     gpu.set_linear_path(args.path)
+    gpu.set_decode_schedule(args.schedule)
     first = [model.prefill(s, workload.prompt(s, args.ctx, args.seed), want_logits=False) for s in range(B)]
+    if args.window == "prefill":
+        gpu.sync()
+        torch.cuda.profiler.start()
+        t0 = time.perf_counter()
+        first[0] = model.prefill(0, workload.prompt(0, args.ctx, args.seed), want_logits=False)
+        gpu.sync()
+        prefill_ms = (time.perf_counter() - t0) * 1e3
+        torch.cuda.profiler.stop()
+        print(json.dumps({"prefill_tokens": args.ctx, "layers": args.layers, "weights": args.weights,
+                          "prefill_ms_wall": round(prefill_ms, 3)}), flush=True)
+        gpu.close()
+        return
     slots = list(range(B))
     out, _ = model.generate(slots, first, args.warmup)
     nxt = out[-1].tolist()
