@@ -159,16 +159,17 @@ ZYNFER_CU_API int zynfer_cu_block_forward(ZynferCuCtx *ctx, uint32_t layer, uint
  * x must be 16-byte aligned and y 8-byte aligned. */
 ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, const float *scale,
                      const float *x, uint32_t batch, uint32_t m, uint32_t k, float *y);
-/* Kernel family for linear layers: "auto" (CUDA-core GEMV for <= 4 rows,
- * tcgen05 tensor cores above), "gemv", "tcgen05", or "simt" (the CUDA-core
- * tiled GEMM, kept for comparisons). Applies to later calls of this context. */
+/* Kernel family for linear layers: "auto" (tcgen05 tensor cores for the model
+ * schedules; for zynfer_cu_linear CUDA-core GEMV up to 4 rows), "gemv",
+ * "tcgen05", or "simt" (the CUDA-core tiled GEMM, kept for comparisons).
+ * Applies to later calls of this context. */
 ZYNFER_CU_API int zynfer_cu_set_linear_path(ZynferCuCtx *ctx, const char *path);
 /* Decode schedule for zynfer_cu_decode_step / zynfer_cu_generate: "kernels"
  * (one kernel per op, captured in a CUDA graph per batch size), "persistent"
  * (the whole step as one cooperative persistent kernel with grid barriers;
  * int8 models of hidden 1024, intermediate 3072, 16 x 128 query dims, batch
- * <= 8; ZYNFER_CU_UNSUPPORTED otherwise), or "auto" (persistent for batch 1
- * where it applies, kernels otherwise). Both follow qwen_block.forward (qwen_block.zig:161-235) per layer
+ * <= 8; ZYNFER_CU_UNSUPPORTED otherwise), or "auto" (= "kernels", measured
+ * faster at every batch size). Both follow qwen_block.forward (qwen_block.zig:161-235) per layer
  * and qwen_forward's tied LM head + topK(1) (qwen_forward.zig:163-193). */
 ZYNFER_CU_API int zynfer_cu_set_decode_schedule(ZynferCuCtx *ctx, const char *schedule);
 /* Allocation-free int8 linear (no counterpart in the reference; an addition

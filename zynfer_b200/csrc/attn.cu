@@ -53,8 +53,10 @@ constexpr int kRing = 3;                                     // slots per warp
 constexpr int kMaxBatch = 1024;
 constexpr size_t kRingBytes = (size_t)kDecWarps * kRing * kSlotBytes;
 constexpr int kIdRing = 64;                                 // per-warp ring of block addresses (2 chunks of 32)
-constexpr size_t kDecodeSmem = kRingBytes + kDecWarps * kRing * sizeof(uint64_t) + (kMaxBatch + 1) * sizeof(int) +
-                               kDecWarps * kIdRing * sizeof(uint32_t);
+constexpr size_t kScratchOff = kRingBytes + kDecWarps * kRing * sizeof(uint64_t) + (kMaxBatch + 1) * sizeof(int) +
+                                kDecWarps * kIdRing * sizeof(uint32_t);  // per warp: q (2 x 128 f32), new K/V row
+constexpr size_t kWarpScratch = kG * kD * 4 + 2 * kD * 2;
+constexpr size_t kDecodeSmem = kScratchOff + kDecWarps * kWarpScratch;
 
 struct BlockCursor {
     int b, head, blk, nblk;
@@ -67,6 +69,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
     uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kRingBytes) + warp * kRing;
     int* pref = reinterpret_cast<int*>(smem_raw + kRingBytes + kDecWarps * kRing * sizeof(uint64_t));
     uint32_t* kidx = reinterpret_cast<uint32_t*>(pref + kMaxBatch + 1) + warp * kIdRing;
+    float* qb = reinterpret_cast<float*>(smem_raw + kScratchOff + warp * kWarpScratch);
+    uint16_t* kvnew = reinterpret_cast<uint16_t*>(qb + kG * kD);
     constexpr unsigned kAll = 0xFFFFFFFFu;
 
     pdl_launch_dependents();
@@ -165,21 +169,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
         bulk_g2s(dst + kBlockBytes, vp, kBlockBytes, &full[s]);
     };
 
-    // Fill the ring. Only the last block of a row receives this step's K/V
-    // (from the kernel before this one), so the fill stops there until
-    // griddepcontrol.wait has returned.
+    // Fill the ring. The cache holds every earlier token (this step's row is
+    // computed here and patched into the shared copy), so the copies start
+    // before griddepcontrol.wait; only the QKV output is the previous kernel's.
     BlockCursor cc;
     locate(lo, cc);
     fill_chunk(0);
     const int first = min(kRing, n);
-    int issued = 0;
-    while (issued < first && !(kidx[issued] & kLastBit)) {
-        if (lane == 0) issue(issued, issued);
-        ++issued;
-    }
+    if (lane == 0)
+        for (int j = 0; j < first; ++j) issue(j, j);
     pdl_wait();
-    for (; issued < first; ++issued)
-        if (lane == 0) issue(issued, issued);
 
     const int g = lane >> 2, t = lane & 3;
     const int mi = lane >> 3, ri = lane & 7;
@@ -190,32 +189,23 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
     uint32_t qf[8][2];
     float acc[16][4];
     float m_run = -INFINITY, l_run = 0.0f;
-    int kv_len = 0;
-    bool seg_start = true;
+    int kv_len = 0, pos = 0;
+    bool seg_start = true, has_last = false;
 
     for (int i = 0; i < n; ++i) {
         const int s = i % kRing;
         if (seg_start) {
-            // B operand of S: column g = (head g/2, term g%2), k = dims 16 ks + 2t (+1, +8, +9)
-            if (g < 4) {
-                const float* qp = a.q + ((size_t)cc.b * a.n_q + cc.head * kG + (g >> 1)) * kD;
-                const bool lo_part = g & 1;
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
-                    const float2 x0 = *reinterpret_cast<const float2*>(qp + 16 * ks + 2 * t);
-                    const float2 x1 = *reinterpret_cast<const float2*>(qp + 16 * ks + 2 * t + 8);
-                    qf[ks][0] = pack_terms(x0.x, x0.y, lo_part);
-                    qf[ks][1] = pack_terms(x1.x, x1.y, lo_part);
-                }
-            } else {
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks) qf[ks][0] = qf[ks][1] = 0u;
-            }
+            pos = a.positions[cc.b];
+            kv_len = min(max(pos + 1, 1), max_len);
+            const int f_last = a.n_kv * pref[cc.b] + cc.head * cc.nblk + cc.nblk - 1;
+            has_last = f_last < lo + n;  // this warp also holds the row's last block
+            const attn::QkvSource src{a.qkv, (a.n_q + 2 * a.n_kv) * kD, a.n_q * kD, a.n_kv, a.q_norm, a.k_norm,
+                                      a.rope, a.rope_max_pos, a.eps, a.err};
+            attn::share_setup(src, cc.b, cc.head, pos, has_last, qb, kvnew, qf);
 #pragma unroll
             for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
             m_run = -INFINITY;
             l_run = 0.0f;
-            kv_len = min(max(a.positions[cc.b] + 1, 1), max_len);
             seg_start = false;
         }
         const bool ok = __all_sync(kAll, mbar_wait_bounded(&full[s], (uint32_t)((i / kRing) & 1), a.err));
@@ -229,12 +219,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
         }
         unsigned char* kb = ring + s * kSlotBytes;
         const int nv = min(kKvBlock, kv_len - cc.blk * kKvBlock);  // valid tokens in this block
+        const bool last = cc.blk == cc.nblk - 1;
+        if (last) attn::patch_new_row(const_cast<uint16_t*>(block_k(i)), a.n_kv, kb, nv - 1, kvnew);
         if (nv < kKvBlock) {
             // rows past the end of the sequence: p = 0 there, but 0 * (stale NaN) is NaN
             uint4* vrow = reinterpret_cast<uint4*>(kb + kBlockBytes + nv * kD * 2);
             for (int x = lane; x < (kKvBlock - nv) * (kD * 2 / 16); x += kWarp) vrow[x] = make_uint4(0, 0, 0, 0);
-            __syncwarp();
         }
+        __syncwarp();
 
         // S = K . Qcols
         float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sd[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // even / odd k-steps
@@ -294,7 +286,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
             mma_bf16(acc[2 * np], pa0, 0u, pa2, 0u, b0, b1);
             mma_bf16(acc[2 * np + 1], pa0, 0u, pa2, 0u, b2, b3);
         }
-        if (nv < kKvBlock) fence_proxy_async_smem();  // generic writes above, bulk copy next
+        if (nv < kKvBlock || last) fence_proxy_async_smem();  // generic writes above, bulk copy next
         __syncwarp();
         {
             const int jn = i + kRing;  // next block for this slot
@@ -302,7 +294,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
             if (lane == 0 && jn < n) issue(jn, s);
         }
 
-        if (cc.blk == cc.nblk - 1 || i == n - 1) {
+        if (last || i == n - 1) {
             // ---- end of this warp's share of (row b, kv head)
             const int f0 = a.n_kv * pref[cc.b] + cc.head * cc.nblk;
             const int fw = f0 / per, lw = (f0 + cc.nblk - 1) / per;

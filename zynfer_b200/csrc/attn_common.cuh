@@ -58,6 +58,114 @@ __device__ __forceinline__ uint32_t pack_terms(float x0, float x1, bool lo_part)
     return cvt_bf16x2(x0 - __uint_as_float(h << 16), x1 - __uint_as_float(h & 0xFFFF0000u));
 }
 
+// Where the fused decode attention reads this step's q, k and v: the raw
+// fused-QKV linear output [B][qkv_rows] (q heads, then k heads, then v heads)
+// with the per-head RMSNorm weights and the RoPE table.
+struct QkvSource {
+    const float* qkv;
+    int qkv_rows, qd, n_kv;
+    const float* q_norm;
+    const float* k_norm;
+    const float2* rope;  // [rope_max_pos][64] (cos, sin)
+    int rope_max_pos;
+    float eps;
+    uint32_t* err;
+};
+
+// Set-up of a warp's share of (row b, kv head) at position pos (qkv_post's
+// math, qwen_block.zig:191-205): the two query heads, RMSNorm(q_norm) +
+// split-half RoPE, become the tensor-core B fragments qf; when the share
+// holds the row's last block (has_last), this step's key (RMSNorm(k_norm) +
+// RoPE) and value, rounded to bf16, go to kvnew[0..127] / kvnew[128..255].
+// Every load is issued before any is used. qb: 2 x 128 f32 of shared memory.
+__device__ __forceinline__ void share_setup(const QkvSource& src, int b, int head, int pos, bool has_last, float* qb,
+                                            uint16_t* kvnew, uint32_t (&qf)[8][2]) {
+    const int lane = threadIdx.x % kWarp;
+    const int g = lane >> 2, t = lane & 3;
+    const float* qsrc = src.qkv + (size_t)b * src.qkv_rows + (size_t)(head * kG) * kD;
+    const float* ksrc = src.qkv + (size_t)b * src.qkv_rows + src.qd + (size_t)head * kD;
+    const float* vsrc = ksrc + (size_t)src.n_kv * kD;
+    const bool rope_ok = pos >= 0 && pos < src.rope_max_pos;
+    const float2* cs = src.rope + (size_t)(rope_ok ? pos : 0) * (kD / 2);
+    float qv[kG][4], qn[4], kr[4], vr[4], kn[4];
+    float2 c2[2];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int hh = 0; hh < kG; ++hh) qv[hh][j] = __ldcg(qsrc + hh * kD + lane + 32 * j);
+        qn[j] = __ldg(src.q_norm + lane + 32 * j);
+        kr[j] = has_last ? __ldcg(ksrc + lane + 32 * j) : 0.0f;
+        vr[j] = has_last ? __ldcg(vsrc + lane + 32 * j) : 0.0f;
+        kn[j] = has_last ? __ldg(src.k_norm + lane + 32 * j) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) c2[j] = __ldg(cs + lane + 32 * j);
+    auto norm_rope = [&](float (&v)[4], const float (&w)[4]) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ss += v[j] * v[j];
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)kD + src.eps);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = __fmul_rn(__fmul_rn(w[j], v[j]), inv);
+        if (rope_ok) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float x0 = v[j], x1 = v[j + 2];
+                v[j] = __fsub_rn(__fmul_rn(x0, c2[j].x), __fmul_rn(x1, c2[j].y));
+                v[j + 2] = __fadd_rn(__fmul_rn(x0, c2[j].y), __fmul_rn(x1, c2[j].x));
+            }
+        }
+    };
+#pragma unroll
+    for (int hh = 0; hh < kG; ++hh) {
+        norm_rope(qv[hh], qn);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) qb[hh * kD + lane + 32 * j] = qv[hh][j];
+    }
+    if (has_last) {
+        norm_rope(kr, kn);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            kvnew[lane + 32 * j] = f32_to_bf16_rne(kr[j]);
+            kvnew[kD + lane + 32 * j] = f32_to_bf16_rne(vr[j]);
+        }
+    }
+    if (!rope_ok && lane == 0 && src.err) atomicOr(src.err, kErrBadIndex);
+    __syncwarp();
+    if (g < 4) {
+        const float* qp = qb + (g >> 1) * kD;
+        const bool lo_part = g & 1;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            qf[ks][0] = pack_terms(qp[16 * ks + 2 * t], qp[16 * ks + 2 * t + 1], lo_part);
+            qf[ks][1] = pack_terms(qp[16 * ks + 2 * t + 8], qp[16 * ks + 2 * t + 9], lo_part);
+        }
+    } else {
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) qf[ks][0] = qf[ks][1] = 0u;
+    }
+}
+
+// This step's K/V row (token r of its block) into the cache block (kg: K of
+// this head, V n_kv blocks later) and into the shared copy of the block.
+__device__ __forceinline__ void patch_new_row(uint16_t* kg, int n_kv, unsigned char* slot, int r,
+                                              const uint16_t* kvnew) {
+    const int lane = threadIdx.x % kWarp;
+    uint16_t* vg = kg + (size_t)n_kv * kBlockElems;
+    uint16_t* kl = reinterpret_cast<uint16_t*>(slot);
+    uint16_t* vl = reinterpret_cast<uint16_t*>(slot + kBlockBytes);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int e = kv_swizzle(r, lane + 32 * j);
+        const uint16_t kbits = kvnew[lane + 32 * j], vbits = kvnew[kD + lane + 32 * j];
+        kg[e] = kbits;
+        vg[e] = vbits;
+        kl[e] = kbits;
+        vl[e] = vbits;
+    }
+}
+
 // End of a warp's share (segment `seg` of `nseg`) of one (batch row b, kv
 // head). acc / l_run / m_run are the fragment-layout state of the block loop:
 // lanes (g < 4, t) hold O rows g = (head g/2, term g%2) at dims 8 nt + 2t

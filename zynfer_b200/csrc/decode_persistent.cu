@@ -488,71 +488,9 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PersistentArg
                     kv_len = min(max(pos + 1, 1), max_len);
                     const int f_last = a.n_kv * S.pref[cc.b] + cc.head * cc.nblk + cc.nblk - 1;
                     has_last = f_last < att_lo + att_n;  // this warp also holds the row's last block
-                    // every load of the segment set-up is issued before any is used
-                    const float* qsrc = a.qkv + (size_t)cc.b * qkv_rows + (size_t)(cc.head * kG) * kD;
-                    const float* ksrc = a.qkv + (size_t)cc.b * qkv_rows + qd + (size_t)cc.head * kD;
-                    const float* vsrc = ksrc + (size_t)a.n_kv * kD;
-                    const bool rope_ok = pos < a.rope_max_pos;
-                    const float2* cs = a.rope + (size_t)(rope_ok ? pos : 0) * (kD / 2);
-                    float qv[kG][4], qn[4], kr[4], vr[4], kn[4];
-                    float2 c2[2];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-#pragma unroll
-                        for (int hh = 0; hh < kG; ++hh) qv[hh][j] = __ldcg(qsrc + hh * kD + lane + 32 * j);
-                        qn[j] = __ldg(P.q_norm + lane + 32 * j);
-                        kr[j] = has_last ? __ldcg(ksrc + lane + 32 * j) : 0.0f;
-                        vr[j] = has_last ? __ldcg(vsrc + lane + 32 * j) : 0.0f;
-                        kn[j] = has_last ? __ldg(P.k_norm + lane + 32 * j) : 0.0f;
-                    }
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) c2[j] = __ldg(cs + lane + 32 * j);
-                    // RMSNorm (q_norm / k_norm) + split-half RoPE, as qkv_post_kernel
-                    auto norm_rope = [&](float (&v)[4], const float (&w)[4]) {
-                        float ss = 0.0f;
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) ss += v[j] * v[j];
-                        ss = warp_sum(ss);
-                        const float inv = 1.0f / sqrtf(ss / (float)kD + a.eps);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) v[j] = __fmul_rn(__fmul_rn(w[j], v[j]), inv);
-                        if (rope_ok) {
-#pragma unroll
-                            for (int j = 0; j < 2; ++j) {
-                                const float x0 = v[j], x1 = v[j + 2];
-                                v[j] = __fsub_rn(__fmul_rn(x0, c2[j].x), __fmul_rn(x1, c2[j].y));
-                                v[j + 2] = __fadd_rn(__fmul_rn(x0, c2[j].y), __fmul_rn(x1, c2[j].x));
-                            }
-                        }
-                    };
-#pragma unroll
-                    for (int hh = 0; hh < kG; ++hh) {
-                        norm_rope(qv[hh], qn);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) qb[hh * kD + lane + 32 * j] = qv[hh][j];
-                    }
-                    if (has_last) {
-                        norm_rope(kr, kn);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            kvnew[lane + 32 * j] = f32_to_bf16_rne(kr[j]);
-                            kvnew[kD + lane + 32 * j] = f32_to_bf16_rne(vr[j]);
-                        }
-                        if (!rope_ok && lane == 0 && a.err) atomicOr(a.err, kErrBadIndex);
-                    }
-                    __syncwarp();
-                    if (g < 4) {
-                        const float* qp = qb + (g >> 1) * kD;
-                        const bool lo_part = g & 1;
-#pragma unroll
-                        for (int ks = 0; ks < 8; ++ks) {
-                            qf[ks][0] = pack_terms(qp[16 * ks + 2 * t], qp[16 * ks + 2 * t + 1], lo_part);
-                            qf[ks][1] = pack_terms(qp[16 * ks + 2 * t + 8], qp[16 * ks + 2 * t + 9], lo_part);
-                        }
-                    } else {
-#pragma unroll
-                        for (int ks = 0; ks < 8; ++ks) qf[ks][0] = qf[ks][1] = 0u;
-                    }
+                    attn::QkvSource src{a.qkv, qkv_rows, qd, a.n_kv, P.q_norm, P.k_norm, a.rope, a.rope_max_pos,
+                                        a.eps, a.err};
+                    attn::share_setup(src, cc.b, cc.head, pos, has_last, qb, kvnew, qf);
 #pragma unroll
                     for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
                     m_run = -INFINITY;
@@ -571,24 +509,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PersistentArg
                 unsigned char* kb = ring + s * kSlotBytes;
                 const int nv = min(kKvBlock, kv_len - cc.blk * kKvBlock);
                 const bool last = cc.blk == cc.nblk - 1;
-                if (last) {
-                    // this step's token (computed at the segment start): into the cache
-                    // and into this shared copy of its block
-                    const int r = nv - 1;
-                    uint16_t* kg = block_k(i);
-                    uint16_t* vg = kg + (size_t)a.n_kv * kBlockElems;
-                    uint16_t* kl = reinterpret_cast<uint16_t*>(kb);
-                    uint16_t* vl = reinterpret_cast<uint16_t*>(kb + kBlockBytes);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int e = kv_swizzle(r, lane + 32 * j);
-                        const uint16_t kbits = kvnew[lane + 32 * j], vbits = kvnew[kD + lane + 32 * j];
-                        kg[e] = kbits;
-                        vg[e] = vbits;
-                        kl[e] = kbits;
-                        vl[e] = vbits;
-                    }
-                }
+                if (last) attn::patch_new_row(block_k(i), a.n_kv, kb, nv - 1, kvnew);
                 if (nv < kKvBlock) {
                     uint4* vrow = reinterpret_cast<uint4*>(kb + kBlockBytes + nv * kD * 2);
                     for (int x = lane; x < (kKvBlock - nv) * (kD * 2 / 16); x += kWarp) vrow[x] = make_uint4(0, 0, 0, 0);

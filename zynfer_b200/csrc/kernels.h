@@ -113,8 +113,15 @@ void launch_gemm_simt(const LinearArgs& a, cudaStream_t st);
 constexpr int kMinBlocksPerWarp = 4;
 inline int decode_max_segs(int max_blocks) { return max_blocks / kMinBlocksPerWarp + 2; }
 struct AttnDecodeArgs {
-    const float* q;             // [B][n_q][d]
-    const uint16_t* kv_layer;   // [blocks][2][n_kv][16][d], rows chunk-swizzled (kv_swizzle)
+    // this step's q, k, v: the raw fused-QKV output [B][(n_q + 2 n_kv) d]; the
+    // kernel applies the per-head RMSNorm + RoPE and appends K/V to the cache
+    const float* qkv;
+    const float* q_norm;        // [d]
+    const float* k_norm;        // [d]
+    const float2* rope;         // [rope_max_pos][d / 2] (cos, sin)
+    int rope_max_pos;
+    float eps;
+    uint16_t* kv_layer;         // [blocks][2][n_kv][16][d], rows chunk-swizzled (kv_swizzle)
     const int* block_table;     // [seqs][max_blocks]
     int max_blocks;
     int n_pool_blocks;

@@ -34,8 +34,7 @@ enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3 };
 // kernel per step for small int8 batches; auto picks the persistent kernel
 // whenever it applies.
 enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2 };
-constexpr int kGemvMaxRows = 4;  // auto policy: GEMV up to this many rows, tcgen05 above ...
-constexpr int kGemvMaxRowsWideM = 16384;  // ... and up to 8 rows for matrices of at most this many outputs
+constexpr int kGemvMaxRows = 4;  // op-level auto policy: GEMV up to this many rows, tcgen05 above
 
 struct LayerDev {
     void* wqkv = nullptr;
@@ -369,7 +368,7 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
     a.y = y; a.ldy = epi == kEpiSwiGLU ? M / 2 : M; a.epi = epi; a.resid = resid; a.norm_w = norm_w;
     a.eps = c->d.eps > 0.0f ? c->d.eps : 1e-6f; a.argmax_keys = keys;
     int path = c->path_policy;
-    if (path == kPathAuto) path = (N <= kGemvMaxRows || (N <= 8 && M <= kGemvMaxRowsWideM)) ? kPathGemv : kPathTc;
+    if (path == kPathAuto) path = kPathTc;  // measured faster than the GEMVs from batch 1 up
     if (path == kPathGemv && N > 8) path = kPathTc;
     if (path == kPathTc && (!tmA || N > c->tc_tpad || K > c->tc_kmax || K > kPlanesMaxK)) path = kPathSimt;
     TimedEvent* te;
@@ -387,17 +386,17 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
         launch_gemm_simt(a, c->stream);
         c->step_launches += 1;
     } else {
-        PlanesArgs pa{x, K, N, K, c->tc_tpad, wkind, norm_w, a.eps, c->planes, c->exps};
-        launch_prep_planes(pa, c->stream);
         const int nt = tc_tile_tokens(wkind, N);
         TcLaunch L;
         L.tmA = tmA;
-        L.tmB = b_map(c, wkind, K, nt);
         L.args = TcArgs{M, K, N, c->tc_tpad, wkind, epi, s, c->exps, y, a.ldy, resid, keys, c->tc_acc, c->tc_cnt,
                         c->derr};
         L.splits = 1;
         L.sms = c->caps.sm_count > 0 ? c->caps.sm_count : 148;
         const int S = tc_cluster_size(M, N, K, wkind, epi, L.sms);
+        PlanesArgs pa{x, K, N, K, c->tc_tpad, wkind, norm_w, a.eps, c->planes, c->exps};
+        launch_prep_planes(pa, c->stream);
+        L.tmB = b_map(c, wkind, K, nt);
         if (L.tmB) {
             if (S > 1) launch_tc_cluster(L, S, c->stream);
             else launch_tc_gemm(L, c->stream);
@@ -408,13 +407,12 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
 }
 
 // One decode step for the rows already staged in dtok/dseq/dpos.
-// "auto" takes the persistent kernel at batch 1 only: its linear phases run
-// on CUDA cores, which fall behind the graph of GEMV kernels from batch 2 up.
-constexpr int kPersistentAutoMaxBatch = 1;
+// "auto" takes the kernel graph: with the tcgen05 linears it measured faster
+// than the persistent kernel (whose linear phases run on CUDA cores) at every
+// batch size, batch 1 included.
 bool use_persistent(const ZynferCuCtx* c, int B) {
     if (!c->persistent_ok || B > kPersistentMaxBatch) return false;
-    if (c->schedule == kSchedKernels) return false;
-    return c->schedule == kSchedPersistent || B <= kPersistentAutoMaxBatch;
+    return c->schedule == kSchedPersistent;
 }
 
 void enqueue_decode_persistent(ZynferCuCtx* c, int B, bool want_logits) {
@@ -476,20 +474,11 @@ void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
         const LayerDev& Ld = c->L[l];
         linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, &Ld.tm_qkv, c->qkv_rows, H, c->dx, B, c->dqkv, kEpiNone,
                nullptr, Ld.input_ln, nullptr);
-        QkvArgs qa{};
-        qa.qkv = c->dqkv; qa.T = B; qa.n_q = m.n_q; qa.n_kv = m.n_kv; qa.d = m.head_dim;
-        qa.q_norm = Ld.q_norm; qa.k_norm = Ld.k_norm; qa.eps = m.eps;
-        qa.rope = c->rope; qa.rope_max_pos = m.max_seq_len;
-        qa.row_pos = c->dpos; qa.row_seq = c->dseq;
-        qa.kv_layer = c->kv + l * c->kv_layer_elems; qa.block_table = c->table_dev;
-        qa.max_blocks = c->max_blocks; qa.n_pool_blocks = c->n_blocks;
-        qa.q_out = c->dq; qa.q_heads_major = 0; qa.err = c->derr;
-        tbegin(c, ZYNFER_CU_K_OTHER, &te);
-        launch_qkv_post(qa, c->stream);
-        tend(c, te);
-        c->step_launches += 1;
+        // per-head RMSNorm + RoPE and the K/V append run inside the attention kernel
         AttnDecodeArgs aa{};
-        aa.q = c->dq; aa.kv_layer = qa.kv_layer; aa.block_table = c->table_dev;
+        aa.qkv = c->dqkv; aa.q_norm = Ld.q_norm; aa.k_norm = Ld.k_norm; aa.rope = c->rope;
+        aa.rope_max_pos = (int)m.max_seq_len; aa.eps = m.eps;
+        aa.kv_layer = c->kv + l * c->kv_layer_elems; aa.block_table = c->table_dev;
         aa.max_blocks = c->max_blocks; aa.n_pool_blocks = c->n_blocks;
         aa.seq_of = c->dseq; aa.positions = c->dpos; aa.B = B; aa.n_q = m.n_q; aa.n_kv = m.n_kv;
         aa.d = m.head_dim; aa.max_segs = decode_max_segs(c->max_blocks); aa.partial = c->dpart;
@@ -1235,17 +1224,12 @@ int zynfer_cu_block_forward(ZynferCuCtx* c, uint32_t layer, uint32_t seq, const 
             ZC_CHECK(c, cudaMemcpyAsync(c->dio, c->hio, 12, cudaMemcpyHostToDevice, c->stream), "stage");
             ZC_CHECK(c, cudaMemcpyAsync(c->dx, x + (size_t)i * H, (size_t)H * 4, cudaMemcpyHostToDevice, c->stream), "x");
             linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, &Ld.tm_qkv, c->qkv_rows, H, c->dx, 1, c->dqkv, kEpiNone, nullptr, Ld.input_ln, nullptr);
-            QkvArgs qa{};
-            qa.qkv = c->dqkv; qa.T = 1; qa.n_q = m.n_q; qa.n_kv = m.n_kv; qa.d = m.head_dim;
-            qa.q_norm = Ld.q_norm; qa.k_norm = Ld.k_norm; qa.eps = m.eps; qa.rope = c->rope;
-            qa.rope_max_pos = m.max_seq_len; qa.row_pos = c->dpos; qa.row_seq = c->dseq;
-            qa.kv_layer = c->kv + layer * c->kv_layer_elems; qa.block_table = c->table_dev;
-            qa.max_blocks = c->max_blocks; qa.n_pool_blocks = c->n_blocks; qa.q_out = c->dq; qa.err = c->derr;
-            launch_qkv_post(qa, c->stream);
             AttnDecodeArgs aa{};
-            aa.q = c->dq; aa.kv_layer = qa.kv_layer; aa.block_table = c->table_dev; aa.max_blocks = c->max_blocks;
-            aa.n_pool_blocks = c->n_blocks; aa.seq_of = c->dseq; aa.positions = c->dpos; aa.B = 1;
-            aa.n_q = m.n_q; aa.n_kv = m.n_kv; aa.d = m.head_dim;
+            aa.qkv = c->dqkv; aa.q_norm = Ld.q_norm; aa.k_norm = Ld.k_norm; aa.rope = c->rope;
+            aa.rope_max_pos = (int)m.max_seq_len; aa.eps = m.eps;
+            aa.kv_layer = c->kv + layer * c->kv_layer_elems; aa.block_table = c->table_dev;
+            aa.max_blocks = c->max_blocks; aa.n_pool_blocks = c->n_blocks; aa.seq_of = c->dseq; aa.positions = c->dpos;
+            aa.B = 1; aa.n_q = m.n_q; aa.n_kv = m.n_kv; aa.d = m.head_dim;
             aa.max_segs = decode_max_segs(c->max_blocks); aa.partial = c->dpart;
             aa.counters = c->dcnt; aa.out = c->dattn; aa.err = c->derr;
             launch_attn_decode(aa, c->stream);
