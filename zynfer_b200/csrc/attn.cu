@@ -308,137 +308,203 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
 
 // ------------------------------------------------------------ prefill
 //
-// CTA per (64-query tile, query head), 256 threads, f32 throughout:
-// S = Q K^T (thread: 4 queries x 4 keys), online softmax (4 threads per
-// query row), O += P V (thread: 4 queries x 8 dims). Keys after the query or
-// past T are masked (kv_len == q_len == T, ops.zig:322).
+// Causal GQA prefill attention on the tensor cores (mma.sync m16n8k16, bf16
+// in, f32 accumulate), flash-attention style. CTA = (64-query tile, kv
+// head): warps 0-3 take rows 16w.. of query head 2 kvh, warps 4-7 of head
+// 2 kvh + 1, so both heads share each staged K/V tile. Every f32 operand is
+// split into two bf16 terms (x = hi + lo to 2^-18 relative) and each product
+// is taken as hi*hi + hi*lo + lo*hi (three MMAs), so S and P V carry f32-grade
+// accuracy; the K/V tiles are staged as hi and lo bf16 copies (64 keys x 128
+// dims, rows chunk-swizzled for conflict-free ldmatrix). Keys after the query
+// or past T are masked (kv_len == q_len == T, ops.zig:322).
 constexpr int PQ = 64, PK = 64, PTHREADS = 256;
+constexpr int kTileElems = PK * kD;                     // one bf16 copy of a K or V tile
+constexpr size_t kPrefillSmem = (size_t)4 * kTileElems * 2;  // K hi, K lo, V hi, V lo
 
-__global__ void __launch_bounds__(PTHREADS) attn_prefill_kernel(AttnPrefillArgs a) {
-    extern __shared__ __align__(16) float sm[];
-    float* Qs = sm;                       // [128][PQ]  (d-major)
-    float* Ks = Qs + kD * PQ;             // [128][PK]  (d-major)
-    float* Vs = Ks + kD * PK;             // [PK][128]
-    float* Ps = Vs + PK * kD;             // [PK][PQ]   (key-major)
-    float* rowc = Ps + PK * PQ;           // [PQ] correction factors
-    float* rowl = rowc + PQ;              // [PQ] final sums
+// element (row, dim) of a staged 64 x 128 bf16 tile, 16-byte chunks XOR-swizzled by row
+__device__ __forceinline__ int tile_swz(int r, int e) { return r * kD + ((((e >> 3) ^ (r & 7)) << 3) | (e & 7)); }
+
+__global__ void __launch_bounds__(PTHREADS, 1) attn_prefill_kernel(AttnPrefillArgs a) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    uint16_t* khi = reinterpret_cast<uint16_t*>(smem_raw);
+    uint16_t* klo = khi + kTileElems;
+    uint16_t* vhi = klo + kTileElems;
+    uint16_t* vlo = vhi + kTileElems;
+    constexpr unsigned kAll = 0xFFFFFFFFu;
 
     pdl_launch_dependents();
     pdl_wait();
-    const int qt = blockIdx.x, h = blockIdx.y;
-    const int kvh = h / (a.n_q / a.n_kv);
-    const int q0 = qt * PQ;
-    const int tid = threadIdx.x;
+    const int qt = gridDim.x - 1 - blockIdx.x, kvh = blockIdx.y;  // longest (causal) tiles first
     const int T = a.T;
+    const int q0 = qt * PQ;
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    const int h = kvh * kG + (warp >> 2);       // query head of this warp
+    const int r0 = q0 + (warp & 3) * 16;         // first query row of this warp
+    const int g = lane >> 2, t = lane & 3;
+    const int mi = lane >> 3, ri = lane & 7;
     const float scale = 1.0f / sqrtf((float)kD);
 
-    for (int i = tid; i < PQ * kD; i += PTHREADS) {
-        const int r = i / kD, d = i % kD;
-        Qs[d * PQ + r] = (q0 + r < T) ? a.q[((size_t)h * T + q0 + r) * kD + d] : 0.0f;
+    // Q fragments (A operand, 16 rows x 16 dims per k-step), hi and lo terms
+    uint32_t qa[8][4], qb[8][4];
+    {
+        const float* qh = a.q + (size_t)h * T * kD;
+        const int ra = min(r0 + g, T - 1), rb = min(r0 + g + 8, T - 1);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            const int d0 = 16 * ks + 2 * t;
+            const float2 x0 = *reinterpret_cast<const float2*>(qh + (size_t)ra * kD + d0);
+            const float2 x1 = *reinterpret_cast<const float2*>(qh + (size_t)rb * kD + d0);
+            const float2 x2 = *reinterpret_cast<const float2*>(qh + (size_t)ra * kD + d0 + 8);
+            const float2 x3 = *reinterpret_cast<const float2*>(qh + (size_t)rb * kD + d0 + 8);
+            qa[ks][0] = attn::pack_terms(x0.x, x0.y, false);
+            qa[ks][1] = attn::pack_terms(x1.x, x1.y, false);
+            qa[ks][2] = attn::pack_terms(x2.x, x2.y, false);
+            qa[ks][3] = attn::pack_terms(x3.x, x3.y, false);
+            qb[ks][0] = attn::pack_terms(x0.x, x0.y, true);
+            qb[ks][1] = attn::pack_terms(x1.x, x1.y, true);
+            qb[ks][2] = attn::pack_terms(x2.x, x2.y, true);
+            qb[ks][3] = attn::pack_terms(x3.x, x3.y, true);
+        }
     }
-    // S-phase mapping
-    const int sx = tid % 16, sy = tid / 16;  // keys sx*4.., queries sy*4..
-    // O-phase mapping
-    const int ox = tid % 16, oy = tid / 16;  // dims ox*8.., queries oy*4..
-    // softmax mapping: row = tid / 4, part = tid % 4 (16 keys each)
-    const int srow = tid / 4, spart = tid % 4;
-    float m_run = -INFINITY, l_run = 0.0f;
-    float o[4][8];
+    float o[16][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) o[i][c] = 0.0f;
+    for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // rows g and g + 8
 
     const int last_key = min(q0 + PQ, T);  // keys [0, last_key)
+    const float* kg = a.k + (size_t)kvh * T * kD;
+    const float* vg = a.v + (size_t)kvh * T * kD;
     for (int k0 = 0; k0 < last_key; k0 += PK) {
-        __syncthreads();
-        for (int i = tid; i < PK * kD; i += PTHREADS) {
-            const int r = i / kD, d = i % kD;
-            const bool in = k0 + r < T;
-            const size_t off = ((size_t)kvh * T + k0 + r) * kD + d;
-            Ks[d * PK + r] = in ? a.k[off] : 0.0f;
-            Vs[r * kD + d] = in ? a.v[off] : 0.0f;
-        }
-        __syncthreads();
-        float s[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) s[i][c] = 0.0f;
-#pragma unroll 8
-        for (int d = 0; d < kD; ++d) {
-            const float4 qv = *reinterpret_cast<const float4*>(Qs + d * PQ + sy * 4);
-            const float4 kv = *reinterpret_cast<const float4*>(Ks + d * PK + sx * 4);
-            const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
-            const float ka[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) s[i][c] = fmaf(qa[i], ka[c], s[i][c]);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int qi = q0 + sy * 4 + i, kj = k0 + sx * 4 + c;
-                Ps[(sx * 4 + c) * PQ + sy * 4 + i] = (kj <= qi && kj < T) ? s[i][c] * scale : -INFINITY;
+        __syncthreads();  // previous tile fully consumed
+        // stage K and V (f32 -> bf16 hi / lo), keys past T as zeros
+        for (int i = threadIdx.x; i < PK * kD / 4; i += PTHREADS) {
+            const int r = i / (kD / 4), e = 4 * (i % (kD / 4));
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (k0 + r < T) {
+                kv = *reinterpret_cast<const float4*>(kg + (size_t)(k0 + r) * kD + e);
+                vv = *reinterpret_cast<const float4*>(vg + (size_t)(k0 + r) * kD + e);
             }
-        __syncthreads();
-        // online softmax over this tile's 64 keys for row srow
-        float mx = -INFINITY;
-        for (int c = 0; c < 16; ++c) mx = fmaxf(mx, Ps[(spart * 16 + c) * PQ + srow]);
-        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
-        const float m_new = fmaxf(m_run, mx);
-        const float corr = m_new == -INFINITY ? 1.0f : expf(m_run - m_new);
-        float sum = 0.0f;
-        for (int c = 0; c < 16; ++c) {
-            float* pp = Ps + (spart * 16 + c) * PQ + srow;
-            const float pv = *pp == -INFINITY ? 0.0f : expf(*pp - m_new);
-            *pp = pv;
-            sum += pv;
+            const int off = tile_swz(r, e);
+            *reinterpret_cast<uint2*>(khi + off) = make_uint2(attn::pack_terms(kv.x, kv.y, false), attn::pack_terms(kv.z, kv.w, false));
+            *reinterpret_cast<uint2*>(klo + off) = make_uint2(attn::pack_terms(kv.x, kv.y, true), attn::pack_terms(kv.z, kv.w, true));
+            *reinterpret_cast<uint2*>(vhi + off) = make_uint2(attn::pack_terms(vv.x, vv.y, false), attn::pack_terms(vv.z, vv.w, false));
+            *reinterpret_cast<uint2*>(vlo + off) = make_uint2(attn::pack_terms(vv.x, vv.y, true), attn::pack_terms(vv.z, vv.w, true));
         }
-        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
-        l_run = l_run * corr + sum;
-        m_run = m_new;
-        if (spart == 0) rowc[srow] = corr;
         __syncthreads();
+        if (k0 > r0 + 15) continue;  // every key of this tile is after every query of this warp
+
+        // S = Q K^T over 64 keys: 8 n-tiles of 8 keys; ldmatrix.x4 yields two n-tiles
+        float sacc[8][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float c = rowc[oy * 4 + i];
+        for (int j = 0; j < 8; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
+        const uint32_t khi_s = smem_addr(khi), klo_s = smem_addr(klo);
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc) o[i][cc] *= c;
+        for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+            for (int jp = 0; jp < 4; ++jp) {
+                // matrices: (keys 16jp + 0..7, dims 16ks..+7), (same keys, +8), (keys +8, dims), (keys +8, +8)
+                const int key = 16 * jp + ri + ((mi >> 1) << 3);
+                const int ch = 2 * ks + (mi & 1);
+                const uint32_t off = (uint32_t)(key * kD * 2 + ((ch ^ (key & 7)) << 4));
+                uint32_t h0, h1, h2, h3, l0b, l1b, l2b, l3b;
+                attn::ldsm_x4(khi_s + off, h0, h1, h2, h3);
+                attn::ldsm_x4(klo_s + off, l0b, l1b, l2b, l3b);
+                // n-tile 2jp: (h0, h1), n-tile 2jp + 1: (h2, h3)
+                attn::mma_bf16(sacc[2 * jp], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], h0, h1);
+                attn::mma_bf16(sacc[2 * jp], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], l0b, l1b);
+                attn::mma_bf16(sacc[2 * jp], qb[ks][0], qb[ks][1], qb[ks][2], qb[ks][3], h0, h1);
+                attn::mma_bf16(sacc[2 * jp + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], h2, h3);
+                attn::mma_bf16(sacc[2 * jp + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], l2b, l3b);
+                attn::mma_bf16(sacc[2 * jp + 1], qb[ks][0], qb[ks][1], qb[ks][2], qb[ks][3], h2, h3);
+            }
         }
-        const int kmax = min(PK, last_key - k0);
-        for (int kk = 0; kk < kmax; ++kk) {
-            const float4 pv = *reinterpret_cast<const float4*>(Ps + kk * PQ + oy * 4);
-            const float4 v0 = *reinterpret_cast<const float4*>(Vs + kk * kD + ox * 8);
-            const float4 v1 = *reinterpret_cast<const float4*>(Vs + kk * kD + ox * 8 + 4);
-            const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
-            const float va[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        // scale, causal mask, online softmax (rows g and g + 8 of the warp's 16)
+        const int qa_row = r0 + g, qb_row = r0 + g + 8;
+        float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+        for (int j = 0; j < 8; ++j) {
+            const int key = k0 + 8 * j + 2 * t;
+            sacc[j][0] = (key <= qa_row && key < T) ? sacc[j][0] * scale : -INFINITY;
+            sacc[j][1] = (key + 1 <= qa_row && key + 1 < T) ? sacc[j][1] * scale : -INFINITY;
+            sacc[j][2] = (key <= qb_row && key < T) ? sacc[j][2] * scale : -INFINITY;
+            sacc[j][3] = (key + 1 <= qb_row && key + 1 < T) ? sacc[j][3] * scale : -INFINITY;
+            mx0 = fmaxf(mx0, fmaxf(sacc[j][0], sacc[j][1]));
+            mx1 = fmaxf(mx1, fmaxf(sacc[j][2], sacc[j][3]));
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(kAll, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(kAll, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(kAll, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(kAll, mx1, 2));
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        // a row with no visible key yet keeps max -inf; its terms stay 0
+        const float c0 = n0 == -INFINITY ? 1.0f : expf(m0 - n0);
+        const float c1 = n1 == -INFINITY ? 1.0f : expf(m1 - n1);
+        m0 = n0;
+        m1 = n1;
+        l0 *= c0;
+        l1 *= c1;
 #pragma unroll
-                for (int cc = 0; cc < 8; ++cc) o[i][cc] = fmaf(pa[i], va[cc], o[i][cc]);
+        for (int nt = 0; nt < 16; ++nt) {
+            o[nt][0] *= c0;
+            o[nt][1] *= c0;
+            o[nt][2] *= c1;
+            o[nt][3] *= c1;
+        }
+        uint32_t pa[4][4], pb[4][4];  // P as the A operand of 4 k-steps of 16 keys, hi and lo
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float p0 = n0 == -INFINITY ? 0.0f : expf(sacc[j][0] - n0);
+            const float p1 = n0 == -INFINITY ? 0.0f : expf(sacc[j][1] - n0);
+            const float p2 = n1 == -INFINITY ? 0.0f : expf(sacc[j][2] - n1);
+            const float p3 = n1 == -INFINITY ? 0.0f : expf(sacc[j][3] - n1);
+            l0 += p0 + p1;
+            l1 += p2 + p3;
+            // n-tile j = keys 8j..: k-step j / 2, registers (0, 1) for even j, (2, 3) for odd j
+            const int kk = j >> 1, hi2 = (j & 1) * 2;
+            pa[kk][hi2 + 0] = attn::pack_terms(p0, p1, false);
+            pa[kk][hi2 + 1] = attn::pack_terms(p2, p3, false);
+            pb[kk][hi2 + 0] = attn::pack_terms(p0, p1, true);
+            pb[kk][hi2 + 1] = attn::pack_terms(p2, p3, true);
+        }
+        // O += P V: 4 k-steps of 16 keys x 16 n-tiles of 8 dims (ldmatrix.trans: two n-tiles each)
+        const uint32_t vhi_s = smem_addr(vhi), vlo_s = smem_addr(vlo);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+            for (int np = 0; np < 8; ++np) {
+                const int key = 16 * kk + ri + ((mi & 1) << 3);
+                const int ch = 2 * np + (mi >> 1);
+                const uint32_t off = (uint32_t)(key * kD * 2 + ((ch ^ (key & 7)) << 4));
+                uint32_t h0, h1, h2, h3, l0b, l1b, l2b, l3b;
+                attn::ldsm_x4_trans(vhi_s + off, h0, h1, h2, h3);
+                attn::ldsm_x4_trans(vlo_s + off, l0b, l1b, l2b, l3b);
+                attn::mma_bf16(o[2 * np], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], h0, h1);
+                attn::mma_bf16(o[2 * np], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], l0b, l1b);
+                attn::mma_bf16(o[2 * np], pb[kk][0], pb[kk][1], pb[kk][2], pb[kk][3], h0, h1);
+                attn::mma_bf16(o[2 * np + 1], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], h2, h3);
+                attn::mma_bf16(o[2 * np + 1], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], l2b, l3b);
+                attn::mma_bf16(o[2 * np + 1], pb[kk][0], pb[kk][1], pb[kk][2], pb[kk][3], h2, h3);
+            }
         }
     }
-    if (spart == 0) rowl[srow] = l_run;
-    __syncthreads();
+    // normalise and store rows g, g + 8: out [T][n_q][d]
+    l0 += __shfl_xor_sync(kAll, l0, 1);
+    l0 += __shfl_xor_sync(kAll, l0, 2);
+    l1 += __shfl_xor_sync(kAll, l1, 1);
+    l1 += __shfl_xor_sync(kAll, l1, 2);
+    const float i0 = l0 > 0.0f ? 1.0f / l0 : 0.0f, i1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
+    const int ra = r0 + g, rb = r0 + g + 8;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int qi = q0 + oy * 4 + i;
-        if (qi >= T) continue;
-        const float inv = 1.0f / rowl[oy * 4 + i];
-        float* op = a.out + ((size_t)qi * a.n_q + h) * kD + ox * 8;
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) op[cc] = o[i][cc] * inv;
+    for (int nt = 0; nt < 16; ++nt) {
+        const int d = 8 * nt + 2 * t;
+        if (ra < T)
+            *reinterpret_cast<float2*>(a.out + ((size_t)ra * a.n_q + h) * kD + d) = make_float2(o[nt][0] * i0, o[nt][1] * i0);
+        if (rb < T)
+            *reinterpret_cast<float2*>(a.out + ((size_t)rb * a.n_q + h) * kD + d) = make_float2(o[nt][2] * i1, o[nt][3] * i1);
     }
 }
 
 }  // namespace
-
-constexpr size_t kPrefillSmem = ((size_t)kD * PQ + kD * PK + PK * kD + PK * PQ + 2 * PQ) * sizeof(float);
 
 void prepare_attn_kernels() {
     configure_kernel((const void*)attn_decode_kernel, kDecodeSmem);
@@ -450,7 +516,7 @@ void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st) {
 }
 
 void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st) {
-    dim3 grid((a.T + PQ - 1) / PQ, a.n_q);
+    dim3 grid((a.T + PQ - 1) / PQ, a.n_kv);
     launch_pdl(attn_prefill_kernel, grid, PTHREADS, kPrefillSmem, st, a);
 }
 
