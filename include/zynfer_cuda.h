@@ -159,8 +159,9 @@ ZYNFER_CU_API int zynfer_cu_block_forward(ZynferCuCtx *ctx, uint32_t layer, uint
  * x must be 16-byte aligned and y 8-byte aligned. */
 ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, const float *scale,
                      const float *x, uint32_t batch, uint32_t m, uint32_t k, float *y);
-/* Kernel family for linear layers: "auto" (tcgen05 tensor cores for the model
- * schedules; for zynfer_cu_linear CUDA-core GEMV up to 4 rows), "gemv",
+/* Kernel family for linear layers: "auto" (model schedules: CUDA-core GEMV for
+ * one activation row except the LM head, tcgen05 tensor cores otherwise;
+ * zynfer_cu_linear: GEMV up to 4 rows), "gemv",
  * "tcgen05", or "simt" (the CUDA-core tiled GEMM, kept for comparisons).
  * Applies to later calls of this context. */
 ZYNFER_CU_API int zynfer_cu_set_linear_path(ZynferCuCtx *ctx, const char *path);

@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
                 if (a.err) atomicOr(a.err, kErrBadIndex);
                 id = 0;  // keep the pipeline whole; the error word reports the launch
             }
-            kidx[j % kIdRing] = ((uint32_t)id * 2u * (uint32_t)a.n_kv + (uint32_t)x.head) |
+            kidx[j % kIdRing] = (((uint32_t)x.head * (uint32_t)a.n_pool_blocks + (uint32_t)id) * 2u) |
                                 (x.blk == x.nblk - 1 ? kLastBit : 0u);
         }
         __syncwarp();
@@ -162,11 +162,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
     };
     auto issue = [&](int j, int s) {  // lane 0: block j of the range into slot s
         const uint16_t* kp = block_k(j);
-        const uint16_t* vp = kp + (size_t)a.n_kv * kBlockElems;
         unsigned char* dst = ring + s * kSlotBytes;
         mbar_arrive_expect_tx(&full[s], kSlotBytes);
-        bulk_g2s(dst, kp, kBlockBytes, &full[s]);
-        bulk_g2s(dst + kBlockBytes, vp, kBlockBytes, &full[s]);
+        bulk_g2s(dst, kp, kSlotBytes, &full[s]);  // K then V of the block: one contiguous 8 KB
     };
 
     // Fill the ring. The cache holds every earlier token (this step's row is
@@ -220,7 +218,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
         unsigned char* kb = ring + s * kSlotBytes;
         const int nv = min(kKvBlock, kv_len - cc.blk * kKvBlock);  // valid tokens in this block
         const bool last = cc.blk == cc.nblk - 1;
-        if (last) attn::patch_new_row(const_cast<uint16_t*>(block_k(i)), a.n_kv, kb, nv - 1, kvnew);
+        if (last) attn::patch_new_row(const_cast<uint16_t*>(block_k(i)), kb, nv - 1, kvnew);
         if (nv < kKvBlock) {
             // rows past the end of the sequence: p = 0 there, but 0 * (stale NaN) is NaN
             uint4* vrow = reinterpret_cast<uint4*>(kb + kBlockBytes + nv * kD * 2);

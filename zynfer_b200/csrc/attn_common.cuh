@@ -148,11 +148,10 @@ __device__ __forceinline__ void share_setup(const QkvSource& src, int b, int hea
 }
 
 // This step's K/V row (token r of its block) into the cache block (kg: K of
-// this head, V n_kv blocks later) and into the shared copy of the block.
-__device__ __forceinline__ void patch_new_row(uint16_t* kg, int n_kv, unsigned char* slot, int r,
-                                              const uint16_t* kvnew) {
+// this head, its V right after) and into the shared copy of the block.
+__device__ __forceinline__ void patch_new_row(uint16_t* kg, unsigned char* slot, int r, const uint16_t* kvnew) {
     const int lane = threadIdx.x % kWarp;
-    uint16_t* vg = kg + (size_t)n_kv * kBlockElems;
+    uint16_t* vg = kg + kBlockElems;
     uint16_t* kl = reinterpret_cast<uint16_t*>(slot);
     uint16_t* vl = reinterpret_cast<uint16_t*>(slot + kBlockBytes);
 #pragma unroll

@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PersistentArg
                 if (a.err) atomicOr(a.err, kErrBadIndex);
                 id = 0;
             }
-            kidx[j % kIdRing] = ((uint32_t)id * 2u * (uint32_t)a.n_kv + (uint32_t)x.head) |
+            kidx[j % kIdRing] = (((uint32_t)x.head * (uint32_t)a.n_pool_blocks + (uint32_t)id) * 2u) |
                                 (x.blk == x.nblk - 1 ? kLastBit : 0u);
         }
         __syncwarp();
@@ -426,8 +426,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PersistentArg
             if (lane == 0)  // this layer's KV blocks toward L2 (the new rows are patched in shared memory)
                 for (int j = 0; j < min(att_n, kWarp); ++j) {
                     const uint16_t* kp = kv_layer + (size_t)(kidx[j % kIdRing] & ~kLastBit) * kBlockElems;
-                    prefetch_l2_bulk(kp, kBlockBytes);
-                    prefetch_l2_bulk(kp + (size_t)a.n_kv * kBlockElems, kBlockBytes);
+                    prefetch_l2_bulk(kp, kSlotBytes);
                 }
             stage_rows<NB>(S, xs, B, H, P.input_ln, a.eps, [&](int b, int k) -> float {
                 if (x_in_f) return __ldcg(x_in_f + (size_t)b * H + k);
@@ -458,8 +457,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PersistentArg
                 const uint16_t* kp = block_k(j);
                 unsigned char* dst = ring + s * kSlotBytes;
                 mbar_arrive_expect_tx(&full[s], kSlotBytes);
-                bulk_g2s(dst, kp, kBlockBytes, &full[s]);
-                bulk_g2s(dst + kBlockBytes, kp + (size_t)a.n_kv * kBlockElems, kBlockBytes, &full[s]);
+                bulk_g2s(dst, kp, kSlotBytes, &full[s]);  // K then V of the block: one contiguous 8 KB
             };
             fence_proxy_async_smem();  // the ring held staged activations (generic writes) until the barrier
             const int first = min(kRing, att_n);
@@ -509,7 +507,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(PersistentArg
                 unsigned char* kb = ring + s * kSlotBytes;
                 const int nv = min(kKvBlock, kv_len - cc.blk * kKvBlock);
                 const bool last = cc.blk == cc.nblk - 1;
-                if (last) attn::patch_new_row(block_k(i), a.n_kv, kb, nv - 1, kvnew);
+                if (last) attn::patch_new_row(block_k(i), kb, nv - 1, kvnew);
                 if (nv < kKvBlock) {
                     uint4* vrow = reinterpret_cast<uint4*>(kb + kBlockBytes + nv * kD * 2);
                     for (int x = lane; x < (kKvBlock - nv) * (kD * 2 / 16); x += kWarp) vrow[x] = make_uint4(0, 0, 0, 0);

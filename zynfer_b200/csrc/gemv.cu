@@ -38,6 +38,7 @@ __device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf
 
 template <int WK, int NB, int R, int EPI>
 __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
+    static_assert(EPI != kEpiSwiGLU || R % 2 == 0, "SwiGLU needs (gate, up) row pairs in one unit");
     extern __shared__ float xs[];  // [NB][K] swizzled
     __shared__ float red[kWarps];
     __shared__ unsigned long long best_s[kWarps][NB];
@@ -192,7 +193,9 @@ void launch_nb(const LinearArgs& a, cudaStream_t st) {
     };
     switch (a.epi) {
         case kEpiResid: pick(gemv_kernel<WK, NB, R, kEpiResid>); break;
-        case kEpiSwiGLU: pick(gemv_kernel<WK, NB, R, kEpiSwiGLU>); break;
+        case kEpiSwiGLU:
+            if constexpr (R % 2 == 0) pick(gemv_kernel<WK, NB, R, kEpiSwiGLU>);
+            break;
         case kEpiArgmax: pick(gemv_kernel<WK, NB, R, kEpiArgmax>); break;
         default: pick(gemv_kernel<WK, NB, R, kEpiNone>); break;
     }
@@ -200,7 +203,10 @@ void launch_nb(const LinearArgs& a, cudaStream_t st) {
 
 template <int WK>
 void launch_wk(const LinearArgs& a, cudaStream_t st) {
-    if (a.N <= 1) launch_nb<WK, 1, 4>(a, st);
+    // one activation row: one weight row per warp (most CTAs, shortest chain),
+    // two for SwiGLU, whose (gate, up) rows must meet in one warp
+    if (a.N <= 1 && a.epi == kEpiSwiGLU) launch_nb<WK, 1, 2>(a, st);
+    else if (a.N <= 1) launch_nb<WK, 1, 1>(a, st);
     else if (a.N <= 2) launch_nb<WK, 2, 4>(a, st);
     else if (a.N <= 4) launch_nb<WK, 4, 2>(a, st);
     else launch_nb<WK, 8, 2>(a, st);
@@ -211,15 +217,15 @@ void prepare_nb() {
     constexpr size_t smem = (size_t)8 * 3072 * 4;  // 8 rows of the widest K (3072)
     configure_kernel((const void*)gemv_kernel<WK, NB, R, kEpiNone>, smem);
     configure_kernel((const void*)gemv_kernel<WK, NB, R, kEpiResid>, smem);
-    configure_kernel((const void*)gemv_kernel<WK, NB, R, kEpiSwiGLU>, smem);
+    if constexpr (R % 2 == 0) configure_kernel((const void*)gemv_kernel<WK, NB, R, kEpiSwiGLU>, smem);
     configure_kernel((const void*)gemv_kernel<WK, NB, R, kEpiArgmax>, smem);
 }
 
 }  // namespace
 
 void prepare_gemv_kernels() {
-    prepare_nb<kWQ8, 1, 4>(); prepare_nb<kWQ8, 2, 4>(); prepare_nb<kWQ8, 4, 2>(); prepare_nb<kWQ8, 8, 2>();
-    prepare_nb<kWBF16, 1, 4>(); prepare_nb<kWBF16, 2, 4>(); prepare_nb<kWBF16, 4, 2>(); prepare_nb<kWBF16, 8, 2>();
+    prepare_nb<kWQ8, 1, 1>(); prepare_nb<kWQ8, 1, 2>(); prepare_nb<kWQ8, 2, 4>(); prepare_nb<kWQ8, 4, 2>(); prepare_nb<kWQ8, 8, 2>();
+    prepare_nb<kWBF16, 1, 1>(); prepare_nb<kWBF16, 1, 2>(); prepare_nb<kWBF16, 2, 4>(); prepare_nb<kWBF16, 4, 2>(); prepare_nb<kWBF16, 8, 2>();
 }
 
 void launch_gemv(const LinearArgs& a, cudaStream_t st) {

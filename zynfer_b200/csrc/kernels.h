@@ -77,7 +77,7 @@ struct QkvArgs {
     const int* row_seq;
     int seq0;
     // paged bf16 cache
-    uint16_t* kv_layer;         // this layer's pool base: [blocks][2][n_kv][16][d], kv_swizzle rows
+    uint16_t* kv_layer;         // this layer's pool base: [n_kv][blocks][K, V][16][d], kv_swizzle rows
     const int* block_table;     // [seqs][max_blocks]
     int max_blocks;
     int n_pool_blocks;
@@ -121,7 +121,7 @@ struct AttnDecodeArgs {
     const float2* rope;         // [rope_max_pos][d / 2] (cos, sin)
     int rope_max_pos;
     float eps;
-    uint16_t* kv_layer;         // [blocks][2][n_kv][16][d], rows chunk-swizzled (kv_swizzle)
+    uint16_t* kv_layer;         // [n_kv][blocks][K, V][16][d], rows chunk-swizzled (kv_swizzle)
     const int* block_table;     // [seqs][max_blocks]
     int max_blocks;
     int n_pool_blocks;

@@ -135,7 +135,7 @@ __global__ void qkv_post_kernel(QkvArgs a) {
     if (blk < 0 || blk >= a.n_pool_blocks) {
         if (lane == 0 && a.err) atomicOr(a.err, kErrBadIndex);
     } else {
-        uint16_t* dst = a.kv_layer + (((size_t)blk * 2 + which) * a.n_kv + kvh) * kKvBlock * d;
+        uint16_t* dst = a.kv_layer + (((size_t)kvh * a.n_pool_blocks + blk) * 2 + which) * kKvBlock * d;
 #pragma unroll
         for (int j = 0; j < 4; ++j) dst[kv_swizzle(pos % kKvBlock, lane + 32 * j)] = f32_to_bf16_rne(v[j]);
     }

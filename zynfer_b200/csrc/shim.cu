@@ -35,6 +35,7 @@ enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3 };
 // whenever it applies.
 enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2 };
 constexpr int kGemvMaxRows = 4;  // op-level auto policy: GEMV up to this many rows, tcgen05 above
+constexpr int kGemvMaxM = 16384;  // model auto policy: largest matrix (output rows) for the batch-1 GEMV
 
 struct LayerDev {
     void* wqkv = nullptr;
@@ -368,7 +369,9 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
     a.y = y; a.ldy = epi == kEpiSwiGLU ? M / 2 : M; a.epi = epi; a.resid = resid; a.norm_w = norm_w;
     a.eps = c->d.eps > 0.0f ? c->d.eps : 1e-6f; a.argmax_keys = keys;
     int path = c->path_policy;
-    if (path == kPathAuto) path = kPathTc;  // measured faster than the GEMVs from batch 1 up
+    // auto: one activation row -> GEMV (no plane kernel, one launch) except the
+    // vocabulary-sized LM head; more rows -> tcgen05 (measured faster from 2 up)
+    if (path == kPathAuto) path = (N == 1 && M <= kGemvMaxM) ? kPathGemv : kPathTc;
     if (path == kPathGemv && N > 8) path = kPathTc;
     if (path == kPathTc && (!tmA || N > c->tc_tpad || K > c->tc_kmax || K > kPlanesMaxK)) path = kPathSimt;
     TimedEvent* te;
@@ -1056,7 +1059,7 @@ int zynfer_cu_kv_read(ZynferCuCtx* c, uint32_t seq, uint32_t layer, int which_v,
     for (uint32_t p0 = 0; p0 < len; p0 += kKvBlock) {
         const int b = c->seq_blocks[seq][p0 / kKvBlock];
         for (int h = 0; h < nkv; ++h) {
-            const uint16_t* src = c->kv + layer * c->kv_layer_elems + (((size_t)b * 2 + (which_v ? 1 : 0)) * nkv + h) * kKvBlock * d;
+            const uint16_t* src = c->kv + layer * c->kv_layer_elems + (((size_t)h * c->n_blocks + b) * 2 + (which_v ? 1 : 0)) * kKvBlock * d;
             ZC_CHECK(c, cudaMemcpy(blk.data(), src, blk.size() * 2, cudaMemcpyDeviceToHost), "kv read");
             for (uint32_t i = 0; i < (uint32_t)kKvBlock && p0 + i < len; ++i)
                 for (int e = 0; e < d; ++e) {
