@@ -127,3 +127,31 @@ def test_schedule_names_and_shape_limits(gpu, wide):
         g2.set_decode_schedule("persistent")
     g2.set_decode_schedule("kernels")
     g2.close()
+
+
+def test_phase_trace_covers_every_phase(wide):
+    """With timing on, the persistent step records (start, end) of every phase
+    as globaltimer ns: 4 + 10 L entries, each phase starting after the previous
+    one ended, and the per-class totals of kernel_time add up to the step."""
+    gpu = wide.gpu
+    ids = O.synth_tokens(20, SEED, 31, WIDE["vocab"])
+    wide.prefill(11, ids, want_logits=False)
+    gpu.set_timing(True)
+    try:
+        wide.decode_step([11], [5])
+        t = gpu.phase_trace().astype(np.int64)
+        n_att, ms_att = gpu.kernel_time(zc.K_ATTN)
+        n_lin, ms_lin = gpu.kernel_time(zc.K_LINEAR)
+        n_head, ms_head = gpu.kernel_time(zc.K_LMHEAD)
+    finally:
+        gpu.set_timing(False)
+    L = WIDE["layers"]
+    assert t.size == 4 + 10 * L
+    phases = 5 * L + 1
+    starts, ends = t[1:2 * phases:2], t[2:2 * phases + 1:2]
+    assert (ends >= starts).all()
+    assert (starts[1:] >= ends[:-1]).all()
+    assert t[3 + 2 * (phases - 1)] >= ends[-1]
+    assert (n_att, n_lin, n_head) == (L, 4 * L, 1)
+    total_ms = (t[3 + 2 * (phases - 1)] - t[1]) / 1e6
+    assert abs((ms_att + ms_lin + ms_head) - total_ms) < 1e-3
