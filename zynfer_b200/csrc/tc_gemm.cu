@@ -395,13 +395,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 }
                 if (!split_k) release_acc();
                 if constexpr (EPI == kEpiArgmax) {
-                    epi_bar();
-                    const int e = threadIdx.x - 64;  // 0 .. 255
-                    for (int t = e; t < NT; t += 256) {
-                        if (n0 + t < a.T && best_s[t]) atomicMax(a.argmax_keys + n0 + t, best_s[t]);
-                        best_s[t] = 0ull;
+                    // Keep the per-token best over every M tile this CTA takes and
+                    // publish it once per N tile: one global atomic per token and
+                    // CTA instead of one per tile (the vocabulary has ~1200 tiles).
+                    const int un = u + (int)gridDim.x;
+                    const bool flush = un >= units || (un / m_tiles) % n_tiles != nt;
+                    if (flush) {
+                        epi_bar();
+                        const int e = threadIdx.x - 64;  // 0 .. 255
+                        for (int t = e; t < NT; t += 256) {
+                            if (n0 + t < a.T && best_s[t]) atomicMax(a.argmax_keys + n0 + t, best_s[t]);
+                            best_s[t] = 0ull;
+                        }
+                        epi_bar();
                     }
-                    epi_bar();
                 }
                 if (split_k && threadIdx.x == 64) a.counters[(size_t)nt * m_tiles + mt] = 0u;
             }
