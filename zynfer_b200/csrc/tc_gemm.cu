@@ -465,58 +465,76 @@ constexpr int kMaxCluster = 8;  // portable cluster size
 // ranks' exact values (part: [NT][kBM] in every rank's shared memory) in rank
 // order, then scale and store with the epilogue. Epilogue threads 64..319.
 // Row scales 2^(e - 22) of the int8 digit planes come from xsc (shared
-// memory) when given, else from a.xscale.
-template <int WK, int NT, int EPI>
-__device__ __forceinline__ void cluster_reduce_store(const TcArgs& a, long long* part, int rank, int S, int mt,
+// memory) when given, else from a.xscale. Each thread takes U (token, row
+// pair) items at a time and issues all their remote loads before any sum.
+template <int WK, int NT, int EPI, int SMAX, int U>
+__device__ __forceinline__ void cluster_reduce_items(const TcArgs& a, long long* part, int rank, int S, int mt,
                                                      int nt, const float* xsc) {
     const int e = threadIdx.x - 64;  // 0 .. 255
     const int r0 = 2 * ((rank * (kBM / 2)) / S), r1 = 2 * (((rank + 1) * (kBM / 2)) / S);
     const int pairs = (r1 - r0) / 2;
     const int n0 = nt * NT, m0 = mt * kBM;
-    uint32_t rb[kMaxCluster];  // every rank's partial tile in the cluster's shared window
+    uint32_t rb[SMAX];  // every rank's partial tile in the cluster's shared window
 #pragma unroll
-    for (int s2 = 0; s2 < kMaxCluster; ++s2) rb[s2] = s2 < S ? map_rank(smem_addr(part), (uint32_t)s2) : 0u;
-    // thread = (token, row pair); all S copies of the pair are loaded before the rank-order sum
-    for (int idx = e; idx < pairs * NT; idx += 256) {
-        const int t = idx / pairs, row = r0 + 2 * (idx % pairs);
-        if (n0 + t >= a.T) continue;
-        const uint32_t off = (uint32_t)((t * kBM + row) * 8);
-        long long x0[kMaxCluster], x1[kMaxCluster];
+    for (int s2 = 0; s2 < SMAX; ++s2) rb[s2] = s2 < S ? map_rank(smem_addr(part), (uint32_t)s2) : 0u;
+    const int items = pairs * NT;
+    for (int base = e; base < items; base += 256 * U) {
+        long long x0[U][SMAX], x1[U][SMAX];
 #pragma unroll
-        for (int s2 = 0; s2 < kMaxCluster; ++s2)
-            if (s2 < S) ld_cluster_s64x2(rb[s2] + off, x0[s2], x1[s2]);
-        long long vi[2] = {0, 0};
-        double vd[2] = {0.0, 0.0};
+        for (int u = 0; u < U; ++u) {
+            const int idx = min(base + 256 * u, items - 1);
+            const int t = idx / pairs, row = r0 + 2 * (idx % pairs);
+            const uint32_t off = (uint32_t)((t * kBM + row) * 8);
 #pragma unroll
-        for (int s2 = 0; s2 < kMaxCluster; ++s2) {
-            if (s2 >= S) break;
+            for (int s2 = 0; s2 < SMAX; ++s2)
+                if (s2 < S) ld_cluster_s64x2(rb[s2] + off, x0[u][s2], x1[u][s2]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int idx = base + 256 * u;
+            if (idx >= items) break;
+            const int t = idx / pairs, row = r0 + 2 * (idx % pairs);
+            if (n0 + t >= a.T) continue;
+            long long vi[2] = {0, 0};
+            double vd[2] = {0.0, 0.0};
+#pragma unroll
+            for (int s2 = 0; s2 < SMAX; ++s2) {
+                if (s2 >= S) break;
+                if constexpr (WK == kWQ8) {
+                    vi[0] += x0[u][s2];
+                    vi[1] += x1[u][s2];
+                } else {
+                    vd[0] += __longlong_as_double(x0[u][s2]);
+                    vd[1] += __longlong_as_double(x1[u][s2]);
+                }
+            }
+            float y[2];
             if constexpr (WK == kWQ8) {
-                vi[0] += x0[s2];
-                vi[1] += x1[s2];
+                const float xs = xsc ? xsc[t] : __ldg(a.xscale + n0 + t);
+#pragma unroll
+                for (int v = 0; v < 2; ++v) y[v] = __fmul_rn(__fmul_rn(__ll2float_rn(vi[v]), xs), __ldg(a.scale + m0 + row + v));
             } else {
-                vd[0] += __longlong_as_double(x0[s2]);
-                vd[1] += __longlong_as_double(x1[s2]);
+#pragma unroll
+                for (int v = 0; v < 2; ++v) y[v] = (float)vd[v];
+            }
+            const size_t o = (size_t)(n0 + t) * a.ldy;
+            if constexpr (EPI == kEpiSwiGLU) {
+                a.y[o + ((m0 + row) >> 1)] = __fmul_rn(silu(y[0]), y[1]);
+            } else if constexpr (EPI == kEpiResid) {
+                const float2 rs = *reinterpret_cast<const float2*>(a.resid + o + m0 + row);
+                *reinterpret_cast<float2*>(a.y + o + m0 + row) = make_float2(__fadd_rn(rs.x, y[0]), __fadd_rn(rs.y, y[1]));
+            } else {
+                *reinterpret_cast<float2*>(a.y + o + m0 + row) = make_float2(y[0], y[1]);
             }
         }
-        float y[2];
-        if constexpr (WK == kWQ8) {
-            const float xs = xsc ? xsc[t] : __ldg(a.xscale + n0 + t);
-#pragma unroll
-            for (int u = 0; u < 2; ++u) y[u] = __fmul_rn(__fmul_rn(__ll2float_rn(vi[u]), xs), __ldg(a.scale + m0 + row + u));
-        } else {
-#pragma unroll
-            for (int u = 0; u < 2; ++u) y[u] = (float)vd[u];
-        }
-        const size_t o = (size_t)(n0 + t) * a.ldy;
-        if constexpr (EPI == kEpiSwiGLU) {
-            a.y[o + ((m0 + row) >> 1)] = __fmul_rn(silu(y[0]), y[1]);
-        } else if constexpr (EPI == kEpiResid) {
-            const float2 rs = *reinterpret_cast<const float2*>(a.resid + o + m0 + row);
-            *reinterpret_cast<float2*>(a.y + o + m0 + row) = make_float2(__fadd_rn(rs.x, y[0]), __fadd_rn(rs.y, y[1]));
-        } else {
-            *reinterpret_cast<float2*>(a.y + o + m0 + row) = make_float2(y[0], y[1]);
-        }
     }
+}
+template <int WK, int NT, int EPI>
+__device__ __forceinline__ void cluster_reduce_store(const TcArgs& a, long long* part, int rank, int S, int mt,
+                                                     int nt, const float* xsc) {
+    if (S <= 2) cluster_reduce_items<WK, NT, EPI, 2, 8>(a, part, rank, S, mt, nt, xsc);
+    else if (S <= 4) cluster_reduce_items<WK, NT, EPI, 4, 4>(a, part, rank, S, mt, nt, xsc);
+    else cluster_reduce_items<WK, NT, EPI, kMaxCluster, 2>(a, part, rank, S, mt, nt, xsc);
 }
 
 template <int WK, int NT, int EPI>
