@@ -121,14 +121,11 @@ struct ZynferCuCtx {
     uint32_t* hids = nullptr;  // pinned [max_batch]
 
     CUtensorMap tm_embed;
-    // tcgen05 linear scratch: activation planes, per-row exponents, split-K
-    // accumulator and tile counters, plus B-operand descriptors per (kind, K, NT)
+    // tcgen05 linear scratch: activation planes and per-row exponents, plus
+    // B-operand descriptors per (kind, K, NT)
     uint8_t* planes = nullptr;
     float* exps = nullptr;  // per-row 2^(e-22) of the int8 digit planes
-    void* tc_acc = nullptr;
-    unsigned* tc_cnt = nullptr;
     int tc_tpad = 0, tc_kmax = 0;
-    size_t tc_acc_bytes = 0;
     std::map<uint64_t, CUtensorMap> bmaps;
     std::map<std::pair<const void*, uint64_t>, CUtensorMap> amaps;  // op-level weights
     float* simt_xn = nullptr;  // normalised rows for the CUDA-core GEMM path
@@ -323,27 +320,15 @@ void tend(ZynferCuCtx* c, TimedEvent* te) {
 // Grow the tcgen05 scratch to hold `t` activation rows of up to `kmax` columns.
 int ensure_tc_scratch(ZynferCuCtx* c, int t, int kmax, int mmax) {
     const int tpad = ((t + 127) / 128) * 128;
-    // split-K partials: [split][kAccT rows][M] 8-byte values. K is split only
-    // when there are fewer (M, N) tiles than SMs, so splits * M stays below
-    // ~2 * 148 * 128; 32768 covers it (linear() falls back to one split otherwise).
     (void)mmax;
-    const size_t acc_bytes = (size_t)kAccT * 8 * 32768;
-    if (tpad <= c->tc_tpad && kmax <= c->tc_kmax && acc_bytes <= c->tc_acc_bytes) return ZYNFER_CU_OK;
+    if (tpad <= c->tc_tpad && kmax <= c->tc_kmax) return ZYNFER_CU_OK;
     int rc;
     const int nt = std::max(tpad, c->tc_tpad), nk = std::max(kmax, c->tc_kmax);
-    const size_t na = std::max(acc_bytes, c->tc_acc_bytes);
     // superseded buffers stay in c->allocs until destroy (scratch only grows)
     if ((rc = dalloc(c, &c->planes, (size_t)4 * nt * nk))) return rc;  // 3 int8 or 2 bf16 planes
     if ((rc = dalloc(c, &c->exps, (size_t)nt))) return rc;
-    char* acc;
-    if ((rc = dalloc(c, &acc, na))) return rc;
-    c->tc_acc = acc;
-    if ((rc = dalloc(c, &c->tc_cnt, 8192))) return rc;
-    cudaMemset(c->tc_acc, 0, na);
-    cudaMemset(c->tc_cnt, 0, 8192 * 4);
     c->tc_tpad = nt;
     c->tc_kmax = nk;
-    c->tc_acc_bytes = na;
     c->bmaps.clear();
     return ZYNFER_CU_OK;
 }
@@ -392,9 +377,7 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
         const int nt = tc_tile_tokens(wkind, N);
         TcLaunch L;
         L.tmA = tmA;
-        L.args = TcArgs{M, K, N, c->tc_tpad, wkind, epi, s, c->exps, y, a.ldy, resid, keys, c->tc_acc, c->tc_cnt,
-                        c->derr};
-        L.splits = 1;
+        L.args = TcArgs{M, K, N, c->tc_tpad, wkind, epi, s, c->exps, y, a.ldy, resid, keys, c->derr};
         L.sms = c->caps.sm_count > 0 ? c->caps.sm_count : 148;
         const int S = tc_cluster_size(M, N, K, wkind, epi, L.sms);
         PlanesArgs pa{x, K, N, K, c->tc_tpad, wkind, norm_w, a.eps, c->planes, c->exps};

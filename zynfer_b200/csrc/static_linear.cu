@@ -83,8 +83,7 @@ extern "C" int zynfer_cu_linear_q8_static(const int8_t* w, const float* scale, c
     L.tmA = &tmA;
     L.tmB = &tmB;
     L.args = zc::TcArgs{(int)m, (int)k, (int)batch, kPadRows, zc::kWQ8, zc::kEpiNone, scale, d->xscale, y, (int)m,
-                        nullptr, nullptr, nullptr, nullptr, nullptr};
-    L.splits = 1;  // no split-K: no accumulator or tile counters are needed
+                        nullptr, nullptr, nullptr};
     L.sms = d->sms;
     zc::launch_prep_planes(pa, st);
     zc::launch_tc_gemm(L, st);

@@ -20,16 +20,15 @@
 // the weights are exact bf16, so the product is f32-accumulate grade.
 //
 // Persistent and warp-specialised (320 threads, one CTA per SM walking the
-// (M tile, N tile, K split) units): warp 0 issues TMA loads, warp 1 owns TMEM
+// (M tile, N tile) units): warp 0 issues TMA loads, warp 1 owns TMEM
 // and issues MMAs (one elected lane), warps 2..9 drain TMEM (two warps per
 // 32-lane quarter, alternate 16-token chunks) and run the epilogue. TMEM holds
 // two accumulators so the epilogue of one unit overlaps the loads and MMAs of
 // the next. Shared-memory stages are recycled through mbarriers (full: TMA
 // transaction bytes; empty: tcgen05.commit). No multicast anywhere. Every wait
 // is bounded and reports through the device error word. When there are too
-// few (M, N) tiles to fill the GPU, K is split: each unit stores its exact
-// 64-bit partial values with plain stores and the last unit of a tile to
-// finish sums them in split order (deterministic) before the epilogue.
+// few (M, N) tiles to fill the GPU, tc_cluster_kernel (below) splits K over a
+// thread-block cluster instead.
 #include <cuda.h>
 
 #include <algorithm>
@@ -140,14 +139,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     uint64_t* tmem_empty = tmem_full + 2;   // [2]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
     __shared__ unsigned long long best_s[NT];
-    __shared__ int last_flag;
 
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     pdl_launch_dependents();
     const int m_tiles = a.M / kBM;
     const int n_tiles = (a.T + NT - 1) / NT;
-    const int splits = a.splits;
-    const int units = m_tiles * n_tiles * splits;
+    const int units = m_tiles * n_tiles;
     const int nkb = a.K * (WK == kWQ8 ? 1 : 2) / kKB;
 
     if (threadIdx.x == 0) {
@@ -175,15 +172,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    // unit u -> (m_tile, n_tile, split); consecutive CTAs stream consecutive weight tiles
-    auto unit_coords = [&](int u, int& mt, int& nt, int& sp) {
+    // unit u -> (m_tile, n_tile); consecutive CTAs stream consecutive weight tiles
+    auto unit_coords = [&](int u, int& mt, int& nt) {
         mt = u % m_tiles;
         nt = (u / m_tiles) % n_tiles;
-        sp = u / (m_tiles * n_tiles);
-    };
-    auto kb_range = [&](int sp, int& kb0, int& kb1) {
-        kb0 = (int)((long)sp * nkb / splits);
-        kb1 = (int)((long)(sp + 1) * nkb / splits);
     };
 
     if (warp == 0) {
@@ -196,9 +188,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             {
                 int u = blockIdx.x;
                 if (u < units) {
-                    int mt, nt, sp, kb0, kb1;
-                    unit_coords(u, mt, nt, sp);
-                    kb_range(sp, kb0, kb1);
+                    int mt, nt;
+                    unit_coords(u, mt, nt);
+                    const int kb0 = 0, kb1 = nkb;
                     for (int kb = kb0; kb < kb1 && npre < STAGES; ++kb, ++npre) {
                         mbar_arrive_expect_tx(&full[npre], STAGE);
                         tma_load_2d(smem + npre * STAGE, &tmA, kb * (WK == kWQ8 ? kKB : kKB / 2), mt * kBM,
@@ -210,9 +202,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             int i = 0;
             bool alive = true;
             for (int u = blockIdx.x; u < units && alive; u += gridDim.x) {
-                int mt, nt, sp, kb0, kb1;
-                unit_coords(u, mt, nt, sp);
-                kb_range(sp, kb0, kb1);
+                int mt, nt;
+                unit_coords(u, mt, nt);
+                const int kb0 = 0, kb1 = nkb;
                 for (int kb = kb0; kb < kb1; ++kb, ++i) {
                     const int s = i % STAGES, round = i / STAGES;
                     uint8_t* as = smem + s * STAGE;
@@ -239,9 +231,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             int i = 0, j = 0;
             bool alive = true;
             for (int u = blockIdx.x; u < units && alive; u += gridDim.x, ++j) {
-                int mt, nt, sp, kb0, kb1;
-                unit_coords(u, mt, nt, sp);
-                kb_range(sp, kb0, kb1);
+                int mt, nt;
+                unit_coords(u, mt, nt);
+                const int kb0 = 0, kb1 = nkb;
                 const int acc = j & 1;
                 if (!mbar_wait_bounded(&tmem_empty[acc], (uint32_t)(((j >> 1) & 1) ^ 1), a.err)) break;
                 tc_fence_after();
@@ -273,8 +265,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         const int h = (warp - 2) >> 2;   // which half of the 16-token chunks
         int j = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
-            int mt, nt, sp;
-            unit_coords(u, mt, nt, sp);
+            int mt, nt;
+            unit_coords(u, mt, nt);
             const int m0 = mt * kBM, n0 = nt * NT;
             const int acc = j & 1;
             const int row = m0 + q * 32 + lane;
@@ -282,7 +274,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             tc_fence_after();
             const uint32_t tbase = tmem_base + acc * ACC_COLS + ((uint32_t)(q * 32) << 16);
             const float sc = (a.scale && row < a.M) ? a.scale[row] : 1.0f;
-            const bool split_k = splits > 1;
             // Per (token, row) value of this unit's K range, exact: int8 digits
             // recombined in 64-bit integers; bf16 hi + lo planes summed in f64.
             auto tile_values = [&](int t0, long long (&v)[16]) {
@@ -306,52 +297,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tmem_empty[acc]);
             };
-            bool do_final = !split_k;
-            long long* part = reinterpret_cast<long long*>(a.acc);
-            if (split_k) {
-                // store this unit's values (plain coalesced stores); the last unit
-                // of the tile to finish sums the splits in split order
+            {
                 for (int t0 = 16 * h; t0 < NT; t0 += 32) {
                     long long v[16];
                     tile_values(t0, v);
-                    if (ok && row < a.M) {
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int t = n0 + t0 + jj;
-                            if (t < a.T) part[((size_t)sp * kAccT + t) * a.M + row] = v[jj];
-                        }
-                    }
-                }
-                release_acc();
-                __threadfence();
-                epi_bar();
-                if (threadIdx.x == 64) {
-                    const unsigned prev = atomicAdd(a.counters + (size_t)nt * m_tiles + mt, 1u);
-                    last_flag = prev == (unsigned)(splits - 1);
-                }
-                epi_bar();
-                do_final = last_flag != 0;
-                if (do_final) __threadfence();
-            }
-            if (do_final) {
-                for (int t0 = 16 * h; t0 < NT; t0 += 32) {
-                    long long v[16];
-                    if (!split_k) {
-                        tile_values(t0, v);
-                    } else {
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int t = min(n0 + t0 + jj, a.T - 1);
-                            long long si = 0;
-                            double sd = 0.0;
-                            for (int s = 0; s < splits; ++s) {
-                                const long long e = __ldcg(part + ((size_t)s * kAccT + t) * a.M + row);
-                                if constexpr (WK == kWQ8) si += e;
-                                else sd += __longlong_as_double(e);
-                            }
-                            v[jj] = WK == kWQ8 ? si : __double_as_longlong(sd);
-                        }
-                    }
                     // every load of the chunk is issued before any store (the
                     // output may alias the residual, which blocks reordering)
                     float y[16], rs[16];
@@ -393,7 +342,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                         }
                     }
                 }
-                if (!split_k) release_acc();
+                release_acc();
                 if constexpr (EPI == kEpiArgmax) {
                     // Keep the per-token best over every M tile this CTA takes and
                     // publish it once per N tile: one global atomic per token and
@@ -410,7 +359,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                         epi_bar();
                     }
                 }
-                if (split_k && threadIdx.x == 64) a.counters[(size_t)nt * m_tiles + mt] = 0u;
             }
         }
     }
@@ -795,8 +743,7 @@ constexpr size_t tile_smem() {
 template <int WK, int NT, int EPI>
 void launch_cluster_tile(const TcLaunch& L, int S, cudaStream_t st) {
     constexpr size_t smem = tile_smem<WK, NT>();
-    TcArgs args = L.args;
-    args.splits = 1;
+    const TcArgs& args = L.args;
     const int tiles = (args.M / kBM) * ((args.T + NT - 1) / NT);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(tiles * S);
@@ -844,9 +791,8 @@ void launch_tile(const TcLaunch& L, cudaStream_t st) {
     constexpr size_t smem = tile_smem<WK, NT>();
     auto kern = tc_gemm_kernel<WK, NT, EPI>;
     // persistent: one CTA per SM (at most one per work unit) walks the units
-    TcArgs args = L.args;
-    args.splits = L.splits;
-    const int units = (args.M / kBM) * ((args.T + NT - 1) / NT) * L.splits;
+    const TcArgs& args = L.args;
+    const int units = (args.M / kBM) * ((args.T + NT - 1) / NT);
     const int grid = std::min(units, L.sms > 0 ? L.sms : 148);
     launch_pdl(kern, grid, kTcThreads, smem, st, *L.tmA, *L.tmB, args);
 }
@@ -963,18 +909,6 @@ bool make_tmap_k_major(CUtensorMap* map, const void* base, int wkind, uint64_t k
                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
-}
-
-int tc_splits(int M, int T, int K, int wkind, int sms) {
-    const int nt = tc_tile_tokens(wkind, T);
-    const int tiles = (M / kBM) * ((T + nt - 1) / nt);
-    const int nkb = K * (wkind == kWQ8 ? 1 : 2) / kKB;
-    // The last unit of a tile re-reads splits x NT partial values per row on
-    // its critical path, so split only narrow tiles, and only a few ways.
-    if (nt > 16) return 1;
-    int s = (sms + tiles - 1) / tiles;
-    s = std::min(s, std::max(1, nkb / 2));  // at least two K blocks per split
-    return std::max(1, std::min(s, 4));
 }
 
 }  // namespace zc

@@ -23,7 +23,6 @@ struct PlanesArgs {
 };
 
 constexpr int kPlanesMaxK = 4096;  // activation rows the plane kernel holds in registers
-constexpr int kAccT = 64;  // split-K accumulator rows per plane (split-K only for T <= 64)
 
 struct TcArgs {
     int M, K, T, t_pad;
@@ -35,22 +34,17 @@ struct TcArgs {
     int ldy;
     const float* resid;
     unsigned long long* argmax_keys;
-    void* acc;               // split-K accumulator [P][kAccT][M] (zero between uses)
-    unsigned int* counters;  // split-K tile counters (zero between uses)
     uint32_t* err;
-    int splits;              // K splits per (M, N) tile (set by the launcher)
 };
 
 struct TcLaunch {
     const CUtensorMap* tmA;  // weights [M][K], box 128 B x 128 rows
     const CUtensorMap* tmB;  // planes [P * t_pad][K], box 128 B x NT rows
     TcArgs args;
-    int splits;
     int sms;  // persistent grid size
 };
 
 int tc_tile_tokens(int wkind, int T);  // NT: tokens per N tile
-int tc_splits(int M, int T, int K, int wkind, int sms);
 bool make_tmap_k_major(CUtensorMap* map, const void* base, int wkind, uint64_t k_elems, uint64_t rows,
                        uint32_t box_rows);
 void launch_prep_planes(const PlanesArgs& a, cudaStream_t st);
