@@ -307,15 +307,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
 // ------------------------------------------------------------ prefill
 //
 // Causal GQA prefill attention on the tensor cores (mma.sync m16n8k16, bf16
-// in, f32 accumulate), flash-attention style. CTA = (64-query tile, kv
-// head): warps 0-3 take rows 16w.. of query head 2 kvh, warps 4-7 of head
+// in, f32 accumulate), flash-attention style. CTA = (32-query tile, kv
+// head): warps 0-1 take rows 16w.. of query head 2 kvh, warps 2-3 of head
 // 2 kvh + 1, so both heads share each staged K/V tile. Every f32 operand is
 // split into two bf16 terms (x = hi + lo to 2^-18 relative) and each product
 // is taken as hi*hi + hi*lo + lo*hi (three MMAs), so S and P V carry f32-grade
 // accuracy; the K/V tiles are staged as hi and lo bf16 copies (64 keys x 128
 // dims, rows chunk-swizzled for conflict-free ldmatrix). Keys after the query
 // or past T are masked (kv_len == q_len == T, ops.zig:322).
-constexpr int PQ = 64, PK = 64, PTHREADS = 256;
+constexpr int PQ = 32, PK = 64, PTHREADS = 128;
 constexpr int kTileElems = PK * kD;                     // one bf16 copy of a K or V tile
 constexpr size_t kPrefillSmem = (size_t)4 * kTileElems * 2;  // K hi, K lo, V hi, V lo
 
@@ -336,8 +336,8 @@ __global__ void __launch_bounds__(PTHREADS, 1) attn_prefill_kernel(AttnPrefillAr
     const int T = a.T;
     const int q0 = qt * PQ;
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-    const int h = kvh * kG + (warp >> 2);       // query head of this warp
-    const int r0 = q0 + (warp & 3) * 16;         // first query row of this warp
+    const int h = kvh * kG + (warp >> 1);       // query head of this warp
+    const int r0 = q0 + (warp & 1) * 16;         // first query row of this warp
     const int g = lane >> 2, t = lane & 3;
     const int mi = lane >> 3, ri = lane & 7;
     const float scale = 1.0f / sqrtf((float)kD);
