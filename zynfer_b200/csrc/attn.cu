@@ -53,10 +53,17 @@ constexpr int kRing = 3;                                     // slots per warp
 constexpr int kMaxBatch = 1024;
 constexpr size_t kRingBytes = (size_t)kDecWarps * kRing * kSlotBytes;
 constexpr int kIdRing = 64;                                 // per-warp ring of block addresses (2 chunks of 32)
-constexpr size_t kScratchOff = kRingBytes + kDecWarps * kRing * sizeof(uint64_t) + (kMaxBatch + 1) * sizeof(int) +
-                                kDecWarps * kIdRing * sizeof(uint32_t);  // per warp: q (2 x 128 f32), new K/V row
+constexpr size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+constexpr size_t kScratchOff = align16(kRingBytes + kDecWarps * kRing * sizeof(uint64_t) + (kMaxBatch + 1) * sizeof(int) +
+                                       kDecWarps * kIdRing * sizeof(uint32_t));  // per warp: q (2 x 128 f32), new K/V row
 constexpr size_t kWarpScratch = kG * kD * 4 + 2 * kD * 2;
-constexpr size_t kDecodeSmem = kScratchOff + kDecWarps * kWarpScratch;
+constexpr size_t kRecOff = kScratchOff + kDecWarps * kWarpScratch;  // [2][kDecWarps] share records
+constexpr size_t kGidOff = kRecOff + (size_t)2 * kDecWarps * attn::kPartStride * 4;  // [2][kDecWarps] int
+constexpr size_t kDecodeSmem = kGidOff + 2 * kDecWarps * sizeof(int);
+static_assert(kDecodeSmem <= 232448, "decode attention shared memory");
+static_assert(kScratchOff % 16 == 0 && kWarpScratch % 16 == 0 && kRecOff % 16 == 0 &&
+                  (attn::kPartStride * 4) % 16 == 0,
+              "records are written and read as float2 / float4");
 
 struct BlockCursor {
     int b, head, blk, nblk;
@@ -70,6 +77,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
     int* pref = reinterpret_cast<int*>(smem_raw + kRingBytes + kDecWarps * kRing * sizeof(uint64_t));
     uint32_t* kidx = reinterpret_cast<uint32_t*>(pref + kMaxBatch + 1) + warp * kIdRing;
     float* qb = reinterpret_cast<float*>(smem_raw + kScratchOff + warp * kWarpScratch);
+    float* recs = reinterpret_cast<float*>(smem_raw + kRecOff);  // record (warp, k) at (k * kDecWarps + warp)
+    int (*rec_gid)[kDecWarps] = reinterpret_cast<int (*)[kDecWarps]>(smem_raw + kGidOff);  // (row, kv head) of each record
     uint16_t* kvnew = reinterpret_cast<uint16_t*>(qb + kG * kD);
     constexpr unsigned kAll = 0xFFFFFFFFu;
 
@@ -109,10 +118,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
     const int total = pref[B] * a.n_kv;
     const int nwarps = gridDim.x * kDecWarps;
     const int per = max((total + nwarps - 1) / nwarps, kMinBlocksPerWarp);
-    const int w = warp * gridDim.x + blockIdx.x;  // active warps spread over all SMs
+    // CTA-major shares: the warps of a CTA hold consecutive shares, so the
+    // pieces of a (row, kv head) mostly meet in one CTA and merge in shared
+    // memory; only CTA-level records go through global memory.
+    const int w = blockIdx.x * kDecWarps + warp;
+    const int c_lo = blockIdx.x * kDecWarps * per;
+    if (c_lo >= total) return;  // the whole CTA is idle
+    const int c_hi = min(total, c_lo + kDecWarps * per);
     const int lo = w * per;
-    const int n = min(total, lo + per) - lo;
-    if (n <= 0) return;
+    const int n = max(0, min(total, lo + per) - lo);
+    if (lane < 2) rec_gid[lane][warp] = -1;
 
     auto locate = [&](int f, BlockCursor& c) {
         int l = 0, h = B - 1;
@@ -208,12 +223,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
         }
         const bool ok = __all_sync(kAll, mbar_wait_bounded(&full[s], (uint32_t)((i / kRing) & 1), a.err));
         if (!ok) {
-            // let every copy still in flight land before the warp leaves
+            // let every copy still in flight land before the warp stops (the
+            // error word reports the launch; the CTA merge below still runs)
             if (lane == 0)
                 for (int j = i; j < min(n, i + kRing); ++j)
                     mbar_wait_bounded(&full[j % kRing], (uint32_t)((j / kRing) & 1), nullptr);
             __syncwarp();
-            return;
+            break;
         }
         unsigned char* kb = ring + s * kSlotBytes;
         const int nv = min(kKvBlock, kv_len - cc.blk * kKvBlock);  // valid tokens in this block
@@ -293,14 +309,85 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
         }
 
         if (last || i == n - 1) {
-            // ---- end of this warp's share of (row b, kv head)
+            // ---- end of this warp's piece of (row b, kv head): the whole row
+            // goes straight to the output, a piece to this warp's record 0 (the
+            // row began before this share) or 1 (it goes on past it)
             const int f0 = a.n_kv * pref[cc.b] + cc.head * cc.nblk;
-            const int fw = f0 / per, lw = (f0 + cc.nblk - 1) / per;
-            attn::flush_share(acc, l_run, m_run, cc.b, cc.head, lw - fw + 1, w - fw, a.max_segs, a.n_q, a.n_kv,
-                              a.partial, a.counters, a.out, a.err);
+            float Lh, Mh;
+            attn::share_reduce(acc, l_run, m_run, Lh, Mh);
+            if (f0 >= lo && f0 + cc.nblk <= lo + n) {
+                attn::share_store_out(acc, Lh, a.out, cc.b, cc.head, a.n_q);
+            } else {
+                const int k = f0 < lo ? 0 : 1;
+                attn::share_store_record(acc, Lh, Mh, recs + (size_t)(k * kDecWarps + warp) * attn::kPartStride);
+                if (lane == 0) rec_gid[k][warp] = cc.b * a.n_kv + cc.head;
+            }
             seg_start = true;
         }
         advance(cc);
+    }
+
+    // ---- CTA merge: every (row, kv head) that meets this CTA's range in more
+    // than one warp, or leaves it, is merged from the warps' records (warp
+    // order); a row that ends in this CTA is stored, otherwise the CTA's
+    // record goes to global memory and the last CTA to arrive merges them.
+    __syncthreads();
+    {
+        BlockCursor gc;
+        locate(c_lo, gc);
+        int g0 = a.n_kv * pref[gc.b] + gc.head * gc.nblk;
+        for (int gi = 0; g0 < c_hi; ++gi) {
+            const int g1 = g0 + gc.nblk, gb = gc.b, gh = gc.head;
+            if (gi % kDecWarps == warp) {
+                const int wa = max(0, (g0 - c_lo) / per), wb = min(kDecWarps - 1, (g1 - 1 - c_lo) / per);
+                const int lo_a = c_lo + wa * per;
+                const bool whole = wa == wb && g0 >= lo_a && g1 <= lo_a + per;  // already stored by its warp
+                if (!whole) {
+                    // records of warps wa..wb, in order; shared memory, so read them directly
+                    float M[attn::kG] = {-INFINITY, -INFINITY};
+                    for (int wi = wa; wi <= wb; ++wi) {
+                        const int k = (wi == wa && g0 >= c_lo + wi * per) ? 1 : 0;
+                        const float* r = recs + (size_t)(k * kDecWarps + wi) * attn::kPartStride;
+                        M[0] = fmaxf(M[0], r[0]);
+                        M[1] = fmaxf(M[1], r[attn::kPartHead]);
+                    }
+                    float L[attn::kG] = {0.0f, 0.0f};
+                    float4 A0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), A1 = A0;
+                    for (int wi = wa; wi <= wb; ++wi) {
+                        const int k = (wi == wa && g0 >= c_lo + wi * per) ? 1 : 0;
+                        const float* r = recs + (size_t)(k * kDecWarps + wi) * attn::kPartStride;
+                        if (rec_gid[k][wi] != gb * a.n_kv + gh) continue;  // a warp that stopped early
+                        const float c0 = r[0] == -INFINITY ? 0.0f : expf(r[0] - M[0]);
+                        const float c1 = r[attn::kPartHead] == -INFINITY ? 0.0f : expf(r[attn::kPartHead] - M[1]);
+                        L[0] += r[1] * c0;
+                        L[1] += r[attn::kPartHead + 1] * c1;
+                        const float4 u0 = *reinterpret_cast<const float4*>(r + 4 + 4 * lane);
+                        const float4 u1 = *reinterpret_cast<const float4*>(r + attn::kPartHead + 4 + 4 * lane);
+                        A0.x += u0.x * c0; A0.y += u0.y * c0; A0.z += u0.z * c0; A0.w += u0.w * c0;
+                        A1.x += u1.x * c1; A1.y += u1.y * c1; A1.z += u1.z * c1; A1.w += u1.w * c1;
+                    }
+                    if (g0 >= c_lo && g1 <= c_hi) {
+                        attn::merged_store_out(L, A0, A1, a.out, gb, gh, a.n_q);
+                    } else {
+                        const int span = kDecWarps * per;
+                        const int fc = g0 / span, nseg = (g1 - 1) / span - fc + 1, seg = (int)blockIdx.x - fc;
+                        if (seg < a.max_segs && nseg <= a.max_segs) {
+                            float* base = a.partial + ((size_t)gb * a.n_kv + gh) * a.max_segs * attn::kPartStride;
+                            attn::merged_store_record(M, L, A0, A1, base + (size_t)seg * attn::kPartStride);
+                            attn::publish_and_merge(gb, gh, nseg, a.n_q, a.n_kv, base, a.counters, a.out);
+                        } else if (lane == 0 && a.err) {
+                            atomicOr(a.err, kErrBadIndex);
+                        }
+                    }
+                }
+            }
+            g0 = g1;
+            if (++gc.head == a.n_kv) {
+                gc.head = 0;
+                ++gc.b;
+            }
+            gc.nblk = gc.b < B ? pref[gc.b + 1] - pref[gc.b] : 1;
+        }
     }
 }
 

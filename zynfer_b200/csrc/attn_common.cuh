@@ -165,100 +165,107 @@ __device__ __forceinline__ void patch_new_row(uint16_t* kg, unsigned char* slot,
     }
 }
 
-// End of a warp's share (segment `seg` of `nseg`) of one (batch row b, kv
-// head). acc / l_run / m_run are the fragment-layout state of the block loop:
-// lanes (g < 4, t) hold O rows g = (head g/2, term g%2) at dims 8 nt + 2t
-// (+1); lanes with t < 2 hold query head t's running max and partial sums.
-// A share that is the whole row stores o = acc / l directly; otherwise it
-// stores its partial and the last share to finish (atomic counter) merges
-// all of them in segment order:
-//   m = max m_s,  l = sum l_s e^(m_s - m),  o = sum acc_s e^(m_s - m) / l.
-__device__ __forceinline__ void flush_share(float (&acc)[16][4], float l_run, float m_run, int b, int head,
-                                            int nseg, int seg, int max_segs, int n_q, int n_kv, float* partial,
-                                            unsigned* counters, float* out, uint32_t* err) {
+// ---- end of a warp's share: the fragment-layout state of the block loop
+// (lanes (g < 4, t) hold O rows g = (head g/2, term g%2) at dims 8 nt + 2t
+// (+1); lanes with t < 2 hold query head t's running max and partial sums)
+// folded into a record [head][m, l, -, -, acc[128]] or a normalised output.
+
+// Sum l over the warp, combine the hi and lo rows of acc in place; returns
+// this lane's head (hsel) total l and max m.
+__device__ __forceinline__ void share_reduce(float (&acc)[16][4], float l_run, float m_run, float& Lh, float& Mh) {
     constexpr unsigned kAll = 0xFFFFFFFFu;
     const int lane = threadIdx.x % kWarp;
-    const int g = lane >> 2, t = lane & 3, hsel = (lane >> 3) & 1;
+    const int hsel = (lane >> 3) & 1;
     float L = l_run;
     L += __shfl_xor_sync(kAll, L, 4);
     L += __shfl_xor_sync(kAll, L, 8);
     L += __shfl_xor_sync(kAll, L, 16);
-    const float Lh = __shfl_sync(kAll, L, hsel);
-    const float Mh = __shfl_sync(kAll, m_run, hsel);
+    Lh = __shfl_sync(kAll, L, hsel);
+    Mh = __shfl_sync(kAll, m_run, hsel);
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {  // rows hi + lo of the same head
+    for (int nt = 0; nt < 16; ++nt) {
         acc[nt][0] += __shfl_xor_sync(kAll, acc[nt][0], 4);
         acc[nt][1] += __shfl_xor_sync(kAll, acc[nt][1], 4);
     }
-    const bool writer = lane < 16 && (g & 1) == 0;  // lanes 0-3: head 0, 8-11: head 1
-    if (nseg == 1) {
-        if (writer) {
-            float* op = out + ((size_t)b * n_q + head * kG + hsel) * kD + 2 * t;
-            const float inv = 1.0f / Lh;
+}
+__device__ __forceinline__ bool share_writer() {
+    const int lane = threadIdx.x % kWarp;
+    return lane < 16 && ((lane >> 2) & 1) == 0;  // lanes 0-3: head 0, 8-11: head 1
+}
+// o = acc / l of both query heads of (b, kv head) into out [B][n_q][d]
+__device__ __forceinline__ void share_store_out(const float (&acc)[16][4], float Lh, float* out, int b, int head,
+                                                int n_q) {
+    const int lane = threadIdx.x % kWarp;
+    const int t = lane & 3, hsel = (lane >> 3) & 1;
+    if (!share_writer()) return;
+    float* op = out + ((size_t)b * n_q + head * kG + hsel) * kD + 2 * t;
+    const float inv = 1.0f / Lh;
 #pragma unroll
-            for (int nt = 0; nt < 16; ++nt)
-                *reinterpret_cast<float2*>(op + nt * 8) = make_float2(acc[nt][0] * inv, acc[nt][1] * inv);
-        }
-        return;
+    for (int nt = 0; nt < 16; ++nt)
+        *reinterpret_cast<float2*>(op + nt * 8) = make_float2(acc[nt][0] * inv, acc[nt][1] * inv);
+}
+// the partial (m, l, acc) of both heads into a record (global or shared)
+__device__ __forceinline__ void share_store_record(const float (&acc)[16][4], float Lh, float Mh, float* rec) {
+    const int lane = threadIdx.x % kWarp;
+    const int t = lane & 3, hsel = (lane >> 3) & 1;
+    if (!share_writer()) return;
+    float* pg = rec + hsel * kPartHead;
+    if (t == 0) {
+        pg[0] = Mh;
+        pg[1] = Lh;
     }
-    if (seg >= max_segs || nseg > max_segs) {
-        if (lane == 0 && err) atomicOr(err, kErrBadIndex);
-        return;
-    }
-    float* base = partial + ((size_t)b * n_kv + head) * max_segs * kPartStride;
-    float* pg = base + (size_t)seg * kPartStride + hsel * kPartHead;
-    if (writer) {
-        if (t == 0) {
-            pg[0] = Mh;
-            pg[1] = Lh;
-        }
 #pragma unroll
-        for (int nt = 0; nt < 16; ++nt)
-            *reinterpret_cast<float2*>(pg + 4 + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
-    }
-    __threadfence();
-    __syncwarp();
-    unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(counters + (size_t)b * n_kv + head, 1u);
-    prev = __shfl_sync(kAll, prev, 0);
-    if (prev != (unsigned)(nseg - 1)) return;
-    __threadfence();
-    // Merge. Segment statistics one segment per lane; then every lane owns
-    // dims 4 lane .. 4 lane + 3 of both query heads and sums the segments
-    // with eight of them in flight at a time.
+    for (int nt = 0; nt < 16; ++nt)
+        *reinterpret_cast<float2*>(pg + 4 + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
+}
+
+// Merge `count` records (base + j * kPartStride, j in order) in the
+// log-sum-exp sense: m = max m_j, l = sum l_j e^(m_j - m), acc = sum acc_j
+// e^(m_j - m). Lane owns dims 4 lane .. 4 lane + 3 of both heads (A0, A1);
+// M and L of both heads are returned in every lane. kGlobal: records written
+// by other CTAs (read through L2), else shared memory.
+template <bool kGlobal, int kBatch>
+__device__ __forceinline__ void merge_records(const float* base, int count, float (&M)[kG], float (&L)[kG],
+                                              float4& A0, float4& A1) {
+    constexpr unsigned kAll = 0xFFFFFFFFu;
+    const int lane = threadIdx.x % kWarp;
+    auto ld = [](const float* p) { return kGlobal ? __ldcg(p) : *p; };
+    auto ld4 = [](const float* p) {
+        return kGlobal ? __ldcg(reinterpret_cast<const float4*>(p)) : *reinterpret_cast<const float4*>(p);
+    };
     float M0 = -INFINITY, M1 = -INFINITY;
-    for (int s = lane; s < nseg; s += kWarp) {
-        M0 = fmaxf(M0, __ldcg(base + (size_t)s * kPartStride));
-        M1 = fmaxf(M1, __ldcg(base + (size_t)s * kPartStride + kPartHead));
+    for (int s = lane; s < count; s += kWarp) {
+        M0 = fmaxf(M0, ld(base + (size_t)s * kPartStride));
+        M1 = fmaxf(M1, ld(base + (size_t)s * kPartStride + kPartHead));
     }
     M0 = warp_max(M0);
     M1 = warp_max(M1);
     float L0 = 0.0f, L1 = 0.0f;
-    float4 A0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), A1 = A0;
-    for (int s0 = 0; s0 < nseg; s0 += kWarp) {
+    A0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    A1 = A0;
+    for (int s0 = 0; s0 < count; s0 += kWarp) {
         float c0 = 0.0f, c1 = 0.0f;
-        if (s0 + lane < nseg) {
+        if (s0 + lane < count) {
             const float* ps = base + (size_t)(s0 + lane) * kPartStride;
-            const float m0 = __ldcg(ps), l0 = __ldcg(ps + 1);
-            const float m1 = __ldcg(ps + kPartHead), l1 = __ldcg(ps + kPartHead + 1);
+            const float m0 = ld(ps), l0 = ld(ps + 1);
+            const float m1 = ld(ps + kPartHead), l1 = ld(ps + kPartHead + 1);
             c0 = m0 == -INFINITY ? 0.0f : expf(m0 - M0);
             c1 = m1 == -INFINITY ? 0.0f : expf(m1 - M1);
             L0 += l0 * c0;
             L1 += l1 * c1;
         }
-        const int cnt = min(kWarp, nseg - s0);
+        const int cnt = min(kWarp, count - s0);
         const float* pa = base + (size_t)s0 * kPartStride + 4 + 4 * lane;
-        for (int j0 = 0; j0 < cnt; j0 += 8) {
-            // eight segments' accumulators in flight before any is used
-            float4 u0[8], u1[8];
+        for (int j0 = 0; j0 < cnt; j0 += kBatch) {
+            float4 u0[kBatch], u1[kBatch];  // kBatch records in flight before any is used
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < kBatch; ++j) {
                 const int jj = min(j0 + j, cnt - 1);
-                u0[j] = __ldcg(reinterpret_cast<const float4*>(pa + (size_t)jj * kPartStride));
-                u1[j] = __ldcg(reinterpret_cast<const float4*>(pa + (size_t)jj * kPartStride + kPartHead));
+                u0[j] = ld4(pa + (size_t)jj * kPartStride);
+                u1[j] = ld4(pa + (size_t)jj * kPartStride + kPartHead);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < kBatch; ++j) {
                 const bool live = j0 + j < cnt;
                 const float cj0 = __shfl_sync(kAll, c0, (j0 + j) & (kWarp - 1));
                 const float cj1 = __shfl_sync(kAll, c1, (j0 + j) & (kWarp - 1));
@@ -269,13 +276,74 @@ __device__ __forceinline__ void flush_share(float (&acc)[16][4], float l_run, fl
             }
         }
     }
-    L0 = warp_sum(L0);
-    L1 = warp_sum(L1);
-    const float i0 = 1.0f / L0, i1 = 1.0f / L1;
+    M[0] = M0;
+    M[1] = M1;
+    L[0] = warp_sum(L0);
+    L[1] = warp_sum(L1);
+}
+// A merged result (lane layout of merge_records) as output or as a record.
+__device__ __forceinline__ void merged_store_out(const float (&L)[kG], const float4& A0, const float4& A1,
+                                                 float* out, int b, int head, int n_q) {
+    const int lane = threadIdx.x % kWarp;
+    const float i0 = 1.0f / L[0], i1 = 1.0f / L[1];
     float* op = out + ((size_t)b * n_q + head * kG) * kD + 4 * lane;
     *reinterpret_cast<float4*>(op) = make_float4(A0.x * i0, A0.y * i0, A0.z * i0, A0.w * i0);
     *reinterpret_cast<float4*>(op + kD) = make_float4(A1.x * i1, A1.y * i1, A1.z * i1, A1.w * i1);
+}
+__device__ __forceinline__ void merged_store_record(const float (&M)[kG], const float (&L)[kG], const float4& A0,
+                                                    const float4& A1, float* rec) {
+    const int lane = threadIdx.x % kWarp;
+    if (lane == 0) {
+        rec[0] = M[0];
+        rec[1] = L[0];
+        rec[kPartHead] = M[1];
+        rec[kPartHead + 1] = L[1];
+    }
+    *reinterpret_cast<float4*>(rec + 4 + 4 * lane) = A0;
+    *reinterpret_cast<float4*>(rec + kPartHead + 4 + 4 * lane) = A1;
+}
+
+// Segment `seg` of `nseg` of (batch row b, kv head) is published in record
+// `rec` (global); the last segment to arrive (atomic counter, no spin)
+// merges all of them in segment order and stores the output.
+template <int kBatch = 8>
+__device__ __forceinline__ void publish_and_merge(int b, int head, int nseg, int n_q, int n_kv, const float* base,
+                                                  unsigned* counters, float* out) {
+    constexpr unsigned kAll = 0xFFFFFFFFu;
+    const int lane = threadIdx.x % kWarp;
+    __threadfence();
+    __syncwarp();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(counters + (size_t)b * n_kv + head, 1u);
+    prev = __shfl_sync(kAll, prev, 0);
+    if (prev != (unsigned)(nseg - 1)) return;
+    __threadfence();
+    float M[kG], L[kG];
+    float4 A0, A1;
+    merge_records<true, kBatch>(base, nseg, M, L, A0, A1);
+    merged_store_out(L, A0, A1, out, b, head, n_q);
     if (lane == 0) counters[(size_t)b * n_kv + head] = 0u;
+}
+
+// A warp's share as a whole: when it is the whole row (nseg == 1) the output
+// directly, else its record in segment `seg` and the merge by the last one.
+template <int kBatch = 8>
+__device__ __forceinline__ void flush_share(float (&acc)[16][4], float l_run, float m_run, int b, int head,
+                                            int nseg, int seg, int max_segs, int n_q, int n_kv, float* partial,
+                                            unsigned* counters, float* out, uint32_t* err) {
+    float Lh, Mh;
+    share_reduce(acc, l_run, m_run, Lh, Mh);
+    if (nseg == 1) {
+        share_store_out(acc, Lh, out, b, head, n_q);
+        return;
+    }
+    if (seg >= max_segs || nseg > max_segs) {
+        if ((threadIdx.x % kWarp) == 0 && err) atomicOr(err, kErrBadIndex);
+        return;
+    }
+    const float* base = partial + ((size_t)b * n_kv + head) * max_segs * kPartStride;
+    share_store_record(acc, Lh, Mh, const_cast<float*>(base) + (size_t)seg * kPartStride);
+    publish_and_merge<kBatch>(b, head, nseg, n_q, n_kv, base, counters, out);
 }
 
 }  // namespace attn
