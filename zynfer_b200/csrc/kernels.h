@@ -110,7 +110,7 @@ void launch_gemm_simt(const LinearArgs& a, cudaStream_t st);
 // attn.cu
 // Decode attention splits each (row, kv head) into at most
 // decode_max_segs(max_blocks) warp shares of >= kMinBlocksPerWarp blocks.
-constexpr int kMinBlocksPerWarp = 4;
+constexpr int kMinBlocksPerWarp = 2;
 inline int decode_max_segs(int max_blocks) { return max_blocks / kMinBlocksPerWarp + 2; }
 struct AttnDecodeArgs {
     // this step's q, k, v: the raw fused-QKV output [B][(n_q + 2 n_kv) d]; the
