@@ -108,8 +108,9 @@ void launch_gemv(const LinearArgs& a, cudaStream_t st);
 void launch_gemm_simt(const LinearArgs& a, cudaStream_t st);
 
 // attn.cu
-// Decode attention splits each (row, kv head) into at most
-// decode_max_segs(max_blocks) warp shares of >= kMinBlocksPerWarp blocks.
+// Decode attention splits each (row, kv head) into warp shares of >=
+// kMinBlocksPerWarp blocks; at most decode_max_segs(max_blocks) records of
+// one (row, kv head) reach global memory.
 constexpr int kMinBlocksPerWarp = 2;
 inline int decode_max_segs(int max_blocks) { return max_blocks / kMinBlocksPerWarp + 2; }
 struct AttnDecodeArgs {

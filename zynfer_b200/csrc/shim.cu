@@ -30,9 +30,8 @@ namespace {
 // Which kernel runs a linear layer: the CUDA-core GEMV (few rows), the
 // tensor-core tcgen05 path, or the CUDA-core tiled GEMM (kept for A/B checks).
 enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3 };
-// Decode schedule: separate kernels per op (graph-captured), or one persistent
-// kernel per step for small int8 batches; auto picks the persistent kernel
-// whenever it applies.
+// Decode schedule: separate kernels per op (graph-captured; what auto takes),
+// or one persistent kernel per step for small int8 batches (on request).
 enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2 };
 constexpr int kGemvMaxRows = 4;  // op-level auto policy: GEMV up to this many rows, tcgen05 above
 constexpr int kGemvMaxM = 16384;  // model auto policy: largest matrix (output rows) for the batch-1 GEMV
