@@ -1,7 +1,10 @@
-"""The persistent decode schedule (one cooperative kernel per step) against the
-oracle and against the multi-kernel schedule (B200 only).
+"""The single-kernel decode schedules against the oracle and against the
+multi-kernel schedule (B200 only): "persistent" (one cooperative kernel per
+step with grid barriers) and "flow" (one cooperative dataflow kernel per step:
+weights and KV blocks streamed into shared memory ahead of the layer chain,
+tagged activations instead of grid barriers). Every test runs for both.
 
-The persistent kernel is built for Qwen3-0.6B widths (hidden 1024,
+Both kernels are built for Qwen3-0.6B widths (hidden 1024,
 intermediate 3072, 16 x 128 query dims, 8 kv heads), so these tests use those
 widths with 2 layers and a 8192-token vocabulary, which keeps the oracle fast.
 Tolerances: BF16_KV (both sides keep a bf16 KV cache).
@@ -21,18 +24,23 @@ WIDE = dict(vocab=8192, hidden=1024, inter=3072, layers=2, n_q=16, n_kv=8, head_
 SEED, WSTD, NSTD = 5, 0.02, 0.1
 
 
+@pytest.fixture(scope="module", params=["persistent", "flow"])
+def sched(request):
+    return request.param
+
+
 @pytest.fixture(scope="module")
-def gpu():
+def gpu(sched):  # one context (and model) per schedule
     g = zc.Gpu(0)
     yield g
     g.close()
 
 
 @pytest.fixture(scope="module")
-def wide(gpu):
-    m = zc.Model(gpu, zc.Arch(**WIDE), zc.W_Q8, max_batch=8, max_seqs=12, max_seq_len=1024)
+def wide(gpu, sched):
+    m = zc.Model(gpu, zc.Arch(**WIDE), zc.W_Q8, max_batch=8, max_seqs=13, max_seq_len=1536)
     m.fill_synthetic(SEED, WSTD, NSTD)
-    gpu.set_decode_schedule("persistent")
+    gpu.set_decode_schedule(sched)
     return m
 
 
@@ -41,7 +49,7 @@ def oracle_wide():
     return O.Model(O.Arch(**WIDE), O.W_Q8, kv_bf16=True, seed=SEED, w_std=WSTD, norm_std=NSTD, threads=8)
 
 
-def test_single_sequence_teacher_forced(wide, oracle_wide):  # qwen_block.zig:161-235 per layer, t = 1
+def test_single_sequence_teacher_forced(wide, oracle_wide, sched):  # qwen_block.zig:161-235 per layer, t = 1
     ids = O.synth_tokens(27, SEED, 3, WIDE["vocab"])
     wide.prefill(0, ids, want_logits=False)
     s = oracle_wide.session(128)
@@ -49,7 +57,7 @@ def test_single_sequence_teacher_forced(wide, oracle_wide):  # qwen_block.zig:16
     feed = O.synth_tokens(9, SEED, 4, WIDE["vocab"])  # crosses the 32-token block boundary
     for i, tok in enumerate(feed):
         am, logits = wide.decode_step([0], [tok], want_logits=True)
-        assert wide.gpu.last_path == "decode:persistent"
+        assert wide.gpu.last_path == f"decode:{sched}"
         ref = s.forward([tok])
         check_logits(ref, logits[0], f"step {i}")
         assert int(am[0]) == int(np.argmax(logits[0]))
@@ -90,7 +98,25 @@ def test_batched_rows_match_oracle(wide, oracle_wide, batch):
             check_logits(sessions[r].forward([toks[r]]), logits[r], f"B={batch} row {r} step {step}")
 
 
-def test_generate_equals_stepwise(wide):
+def test_long_context_rows_match_oracle(wide, oracle_wide):
+    """Contexts of ~1000 and ~600 tokens: every (row, kv head) spans many CTAs'
+    block ranges, so the cross-CTA merge of partial softmax states runs."""
+    seqs, lens = [12, 11], [1000, 600]
+    sessions = []
+    for sq, n in zip(seqs, lens):
+        ids = O.synth_tokens(n, SEED + sq, 8, WIDE["vocab"])
+        wide.prefill(sq, ids, want_logits=False)
+        ses = oracle_wide.session(1100)
+        ses.forward(ids, want_logits=False)
+        sessions.append(ses)
+    for step in range(3):
+        toks = O.synth_tokens(2, 300 + step, 3, WIDE["vocab"])
+        am, logits = wide.decode_step(seqs, toks, want_logits=True)
+        for r in range(2):
+            check_logits(sessions[r].forward([toks[r]]), logits[r], f"long row {r} step {step}")
+
+
+def test_generate_equals_stepwise(wide, sched):
     ids = O.synth_tokens(40, SEED, 21, WIDE["vocab"])
     wide.prefill(10, ids, want_logits=False)
     stepwise, tok = [], 17
@@ -99,21 +125,21 @@ def test_generate_equals_stepwise(wide):
         stepwise.append(tok)
     wide.prefill(10, ids, want_logits=False)
     out, ms = wide.generate([10], [17], 12)
-    assert wide.gpu.last_path == "generate:persistent"
+    assert wide.gpu.last_path == f"generate:{sched}"
     assert out[:, 0].tolist() == stepwise
     assert ms > 0.0
 
 
-def test_persistent_and_kernel_schedules_agree(wide):
+def test_single_kernel_and_kernel_schedules_agree(wide, sched):
     ids = O.synth_tokens(50, SEED, 23, WIDE["vocab"])
     feed = O.synth_tokens(6, SEED, 24, WIDE["vocab"])
     runs = {}
-    for sched in ("persistent", "kernels"):
-        wide.gpu.set_decode_schedule(sched)
+    for name in (sched, "kernels"):
+        wide.gpu.set_decode_schedule(name)
         wide.prefill(11, ids, want_logits=False)
-        runs[sched] = [wide.decode_step([11], [t], want_logits=True)[1][0] for t in feed]
-    wide.gpu.set_decode_schedule("persistent")
-    for i, (a, b) in enumerate(zip(runs["persistent"], runs["kernels"])):
+        runs[name] = [wide.decode_step([11], [t], want_logits=True)[1][0] for t in feed]
+    wide.gpu.set_decode_schedule(sched)
+    for i, (a, b) in enumerate(zip(runs[sched], runs["kernels"])):
         check_logits(b, a, f"schedules step {i}", BF16_KV)
 
 
@@ -125,12 +151,14 @@ def test_schedule_names_and_shape_limits(gpu, wide):
     zc.Model(g2, zc.Arch(**small), zc.W_Q8, max_batch=1, max_seqs=1, max_seq_len=64)
     with pytest.raises(zc.Unsupported):
         g2.set_decode_schedule("persistent")
+    with pytest.raises(zc.Unsupported):
+        g2.set_decode_schedule("flow")
     g2.set_decode_schedule("kernels")
     g2.close()
 
 
 def test_phase_trace_covers_every_phase(wide):
-    """With timing on, the persistent step records (start, end) of every phase
+    """With timing on, the single-kernel step records (start, end) of every phase
     as globaltimer ns: 4 + 10 L entries, each phase starting after the previous
     one ended, and the per-class totals of kernel_time add up to the step."""
     gpu = wide.gpu

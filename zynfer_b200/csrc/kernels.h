@@ -173,10 +173,23 @@ struct PersistentArgs {
     uint32_t* err;
     uint64_t* trace;                // nullable [4 + 10 L] globaltimer ns: start, then per phase (start, end) as
                                     // seen by CTA 0 (phases QKV, ATT, O, GU, D per layer, then HEAD), then finish
+    // dataflow kernel only: tagged activations (f32 value | 32-bit tag << 32)
+    uint64_t *llx, *llx1;           // [kPersistentMaxBatch][H]
+    uint64_t *llqkv, *llattn, *llh; // [..][qkv rows], [..][n_q d], [..][I]
+    uint64_t* llrec;                // flow_record_words(ctas): cross-CTA attention records
+    uint32_t tag;                   // this step's tag base: a multiple of 64, fresh per launch; layer l uses tag + l + 1
 };
 inline int persistent_trace_len(int layers) { return 4 + 10 * layers; }
 bool persistent_supported(int device);
 cudaError_t launch_decode_persistent(const PersistentArgs& a, cudaStream_t st);
+// decode_flow.cu: the same step as a dataflow kernel (weights and KV blocks
+// streamed into a shared-memory ring by a producer warp, tagged activations
+// instead of grid barriers); up to 62 layers.
+constexpr int kFlowMaxLayers = 62;
+void prepare_flow_kernels();
+bool flow_supported(int device);
+size_t flow_record_words(int ctas);
+cudaError_t launch_decode_flow(const PersistentArgs& a, cudaStream_t st);
 struct AttnPrefillArgs {
     const float* q;   // [n_q][T][d]
     const float* k;   // [n_kv][T][d]

@@ -32,7 +32,7 @@ namespace {
 enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3 };
 // Decode schedule: separate kernels per op (graph-captured; what auto takes),
 // or one persistent kernel per step for small int8 batches (on request).
-enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2 };
+enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2, kSchedFlow = 3 };
 constexpr int kGemvMaxRows = 4;  // op-level auto policy: GEMV up to this many rows, tcgen05 above
 constexpr int kGemvMaxM = 16384;  // model auto policy: largest matrix (output rows) for the batch-1 GEMV
 
@@ -134,6 +134,10 @@ struct ZynferCuCtx {
     bool persistent_ok = false;          // model shape and device allow the persistent decode kernel
     PersistentLayer* dlayers = nullptr;  // [layers] weight pointers for it
     unsigned* psync = nullptr;           // [3] its grid-barrier / finish / abort words
+    bool flow_ok = false;                // ... and the dataflow decode kernel
+    uint64_t* ll = nullptr;              // its tagged activation buffers and attention records
+    size_t ll_words = 0;
+    uint32_t flow_step = 0;              // launches so far: tag base = 64 (1 + step % 2^25)
     uint64_t* ptrace = nullptr;          // its phase timestamps when timing is on
     std::vector<uint64_t> ptrace_host;
 
@@ -396,8 +400,9 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
 // than the persistent kernel (whose linear phases run on CUDA cores) at every
 // batch size, batch 1 included.
 bool use_persistent(const ZynferCuCtx* c, int B) {
-    if (!c->persistent_ok || B > kPersistentMaxBatch) return false;
-    return c->schedule == kSchedPersistent;
+    if (B > kPersistentMaxBatch) return false;
+    if (c->schedule == kSchedFlow) return c->flow_ok;
+    return c->persistent_ok && c->schedule == kSchedPersistent;
 }
 
 void enqueue_decode_persistent(ZynferCuCtx* c, int B, bool want_logits) {
@@ -419,7 +424,20 @@ void enqueue_decode_persistent(ZynferCuCtx* c, int B, bool want_logits) {
     const int tl = persistent_trace_len((int)m.layers);
     if (c->timing && !c->ptrace && dalloc(c, &c->ptrace, (size_t)tl) != ZYNFER_CU_OK) c->ptrace = nullptr;
     a.trace = c->timing ? c->ptrace : nullptr;
-    launch_decode_persistent(a, c->stream);
+    if (c->schedule == kSchedFlow) {
+        const size_t act = (size_t)kPersistentMaxBatch;
+        a.llx = c->ll;
+        a.llx1 = a.llx + act * m.hidden;
+        a.llqkv = a.llx1 + act * m.hidden;
+        a.llattn = a.llqkv + act * c->qkv_rows;
+        a.llh = a.llattn + act * c->qd;
+        a.llrec = a.llh + act * m.inter;
+        // tags are unique per (launch, layer): 64 (1 + step) + layer + 1
+        a.tag = 64u * (1u + (c->flow_step++ % (1u << 25)));
+        launch_decode_flow(a, c->stream);
+    } else {
+        launch_decode_persistent(a, c->stream);
+    }
     c->step_launches = 1;
     if (a.trace) {
         // phase p lasts from its start to the next phase's start (its grid barrier included)
@@ -853,6 +871,15 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
         if ((rc = dalloc(c, &c->psync, 3)) != ZYNFER_CU_OK) return rc;
         cudaMemset(c->psync, 0, 3 * sizeof(unsigned));
     }
+    // dataflow decode kernel: tagged activations [8][H] x2, [8][qkv], [8][qd],
+    // [8][I] and the cross-CTA attention records (zero tags are never valid)
+    c->flow_ok = c->persistent_ok && m.layers <= (uint32_t)kFlowMaxLayers && m.n_kv == 8 && flow_supported(c->device);
+    if (c->flow_ok) {
+        const int sms = c->caps.sm_count > 0 ? c->caps.sm_count : device_sm_count();
+        c->ll_words = (size_t)kPersistentMaxBatch * (2 * H + c->qkv_rows + c->qd + I) + flow_record_words(sms);
+        if ((rc = dalloc(c, &c->ll, c->ll_words)) != ZYNFER_CU_OK) return rc;
+        cudaMemset(c->ll, 0, c->ll_words * 8);
+    }
     if ((rc = halloc(c, &c->herr, 1)) != ZYNFER_CU_OK) return rc;
     if ((rc = halloc(c, &c->hio, 3 * B)) != ZYNFER_CU_OK) return rc;
     if ((rc = halloc(c, &c->hids, B)) != ZYNFER_CU_OK) return rc;
@@ -1113,7 +1140,8 @@ int zynfer_cu_decode_step(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* 
     cudaEventRecord(c->ev0, c->stream);
     if (eager) {
         enqueue_decode(c, (int)batch, logits != nullptr);
-        c->path = persistent ? "decode:persistent" : (batch <= 8 ? "decode:gemv:eager" : "decode:gemm:eager");
+        c->path = persistent ? (c->schedule == kSchedFlow ? "decode:flow" : "decode:persistent")
+                             : (batch <= 8 ? "decode:gemv:eager" : "decode:gemm:eager");
     } else {
         cudaGraphExec_t g;
         if ((rc = get_graph(c, (int)batch, &g))) return rc;
@@ -1174,7 +1202,7 @@ int zynfer_cu_generate(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* fir
     c->last_step_ns = (uint64_t)(ms * 1e6 / steps);
     ZC_CHECK(c, cudaMemcpy(out_ids, c->dhist, (size_t)steps * batch * 4, cudaMemcpyDeviceToHost), "history");
     for (uint32_t i = 0; i < batch; ++i) c->seq_len[seqs[i]] += steps;
-    c->path = persistent ? std::string("generate:persistent")
+    c->path = persistent ? std::string(c->schedule == kSchedFlow ? "generate:flow" : "generate:persistent")
                          : std::string(batch <= 8 ? "generate:gemv" : "generate:gemm") + (c->timing ? ":eager" : ":graph");
     return ZYNFER_CU_OK;
 }
@@ -1290,6 +1318,12 @@ int zynfer_cu_set_decode_schedule(ZynferCuCtx* c, const char* schedule) {
             return fail(c, ZYNFER_CU_UNSUPPORTED, "the persistent decode kernel needs int8 weights, hidden 1024, "
                                                   "intermediate 3072, 2048 query dims and cooperative launch");
         c->schedule = kSchedPersistent;
+    } else if (!strcmp(schedule, "flow")) {
+        if (c->ready && !c->flow_ok)
+            return fail(c, ZYNFER_CU_UNSUPPORTED, "the dataflow decode kernel needs int8 weights, hidden 1024, "
+                                                  "intermediate 3072, 16 x 128 query and 8 x 128 kv dims, at most "
+                                                  "62 layers, 100+ SMs and cooperative launch");
+        c->schedule = kSchedFlow;
     } else {
         return fail(c, ZYNFER_CU_INVALID, std::string("unknown decode schedule ") + schedule);
     }
