@@ -95,7 +95,9 @@ struct Lay {
     static constexpr size_t pref = best + (size_t)kCW * NB * 8;              // [NB + 1] i32
     static constexpr size_t iend = up(pref + (size_t)(NB + 1) * 4, 16);      // [kNF] u32 (producer)
     static constexpr size_t flag = iend + (size_t)kNF * 4;                   // abort flag (i32)
-    static constexpr size_t bars = up(flag + 16, 16);                        // [2][kNF] u64: full, empty
+    static constexpr size_t shr = flag + 16;                                 // Shares (this CTA's row ranges)
+    static constexpr size_t cur = up(shr + 64, 16);                          // [kCW] u32 x2: consumer ring cursors
+    static constexpr size_t bars = up(cur + (size_t)kCW * 8, 16);            // [2][kNF] u64: full, empty
     static constexpr size_t ring = up(bars + (size_t)2 * kNF * 8, 1024);
     static constexpr uint32_t ring_bytes = (uint32_t)((kSmemMax - ring) / 1024 * 1024);
     static constexpr size_t total = ring + ring_bytes;
@@ -156,6 +158,21 @@ __device__ __forceinline__ bool mbar_wait_ctl(uint64_t* bar, uint32_t parity, co
     return true;
 }
 
+// mbarrier wait that suspends the thread for up to `ns` nanoseconds per try
+// (it resumes as soon as the phase completes), so a waiting producer warp
+// takes no issue slots from the consumer warps of its SM sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Consumer-group barrier (named barrier 1, the 256 consumer threads) that
 // also ANDs a flag over them.
 __device__ __forceinline__ bool cbar_and(bool ok) {
@@ -197,8 +214,8 @@ __device__ __forceinline__ uint32_t u4get(const uint4& v, int q) {
 // CTA c's share [lo, hi) of n items, in multiples of `align`.
 __device__ __forceinline__ void cta_share(int n, int align, int& lo, int& hi) {
     const int units = n / align;
-    lo = (int)((long long)blockIdx.x * units / gridDim.x) * align;
-    hi = (int)((long long)(blockIdx.x + 1) * units / gridDim.x) * align;
+    lo = (int)((unsigned)blockIdx.x * (unsigned)units / gridDim.x) * align;
+    hi = (int)((unsigned)(blockIdx.x + 1) * (unsigned)units / gridDim.x) * align;
 }
 
 struct Shares {
@@ -225,11 +242,11 @@ __device__ __forceinline__ void locate(const int* pref, int B, int f, int& b, in
     blk = r % nblk;
 }
 // First flattened attention block of CTA c's range [att_lo(c), att_lo(c + 1)).
-__device__ __forceinline__ int att_lo(int c, int T) { return (int)((long long)c * T / gridDim.x); }
+__device__ __forceinline__ int att_lo(int c, int T) { return (int)((unsigned)c * (unsigned)T / gridDim.x); }
 // CTA whose attention range holds flattened block f (ranges may be empty
 // when there are fewer blocks than CTAs).
 __device__ __forceinline__ int cta_of(int f, int T) {
-    return (int)(((long long)(f + 1) * gridDim.x - 1) / T);
+    return (int)(((unsigned)(f + 1) * gridDim.x - 1u) / (unsigned)T);
 }
 
 __device__ __forceinline__ void trace_mark(const PersistentArgs& a, int slot) {
@@ -240,107 +257,160 @@ __device__ __forceinline__ void trace_mark(const PersistentArgs& a, int slot) {
     }
 }
 
+// ------------------------------------------------------------ shared views
+
+__device__ __forceinline__ unsigned char* smem_base() {
+    extern __shared__ __align__(1024) unsigned char flow_smem_raw[];
+    return flow_smem_raw;
+}
+template <int NB, class T>
+__device__ __forceinline__ T* at(size_t off) {
+    return reinterpret_cast<T*>(smem_base() + off);
+}
+template <int NB>
+__device__ __forceinline__ Ctl ctl_of(const PersistentArgs& a) {
+    return Ctl{a.sync + 2, a.err, at<NB, int>(Lay<NB>::flag)};
+}
+template <int NB>
+__device__ __forceinline__ uint64_t* full_bar(int s) { return at<NB, uint64_t>(Lay<NB>::bars) + s; }
+template <int NB>
+__device__ __forceinline__ uint64_t* empty_bar(int s) { return at<NB, uint64_t>(Lay<NB>::bars) + kNF + s; }
+
 // ------------------------------------------------------------ producer
 
+// The producer warp's ring state; lane 0 does the waiting.
+struct Prod {
+    uint32_t n, head, oldest, tail;
+    int ok;
+};
+// Room for an item of `bytes` (placement size) at the ring position the
+// consumers compute too: waits, suspended, for the oldest items to be freed.
 template <int NB>
-__device__ __forceinline__ void producer(const PersistentArgs& a, const Shares& sh, const int* pref, unsigned char* ring,
-                         uint64_t* full, uint64_t* empty, uint32_t* iend, const Ctl& ctl) {
-    using LY = Lay<NB>;
-    constexpr uint32_t RB = LY::ring_bytes;
-    constexpr int A = LY::att_item;
+__device__ __noinline__ uint32_t prod_reserve(Prod& p, uint32_t bytes, Ctl ctl) {
+    constexpr uint32_t RB = Lay<NB>::ring_bytes;
+    uint32_t* iend = at<NB, uint32_t>(Lay<NB>::iend);
     const int lane = threadIdx.x % kWarp;
-    uint32_t n = 0, head = 0, oldest = 0, tail = 0;
-    int ok = 1;
-
-    // Room for an item of `bytes` (placement size) at the ring position the
-    // consumers will compute too; lane 0 waits for freed items.
-    auto reserve = [&](uint32_t bytes, uint32_t& off) -> bool {
-        const uint32_t start = ring_take<RB>(head, bytes);
-        if (lane == 0) {
-            while (ok && oldest < n && (head - tail > RB || n - oldest >= (uint32_t)kNF)) {
-                const int s = (int)(oldest % kNF);
-                if (!mbar_wait_ctl(&empty[s], (oldest / kNF) & 1u, ctl)) {
-                    ok = 0;
-                    break;
-                }
-                tail = iend[s];
-                ++oldest;
+    const uint32_t start = ring_take<RB>(p.head, bytes);
+    if (lane == 0) {
+#pragma unroll 1
+        while (p.ok && p.oldest < p.n && (p.head - p.tail > RB || p.n - p.oldest >= (uint32_t)kNF)) {
+            const int s = (int)(p.oldest % kNF);
+            uint32_t spins = 0;
+            bool done;
+#pragma unroll 1
+            while (!(done = mbar_try_wait_sleep(empty_bar<NB>(s), (p.oldest / kNF) & 1u, 20000u)))
+                if (!keep_waiting(spins, ctl)) break;
+            if (!done) {
+                p.ok = 0;
+                break;
             }
-            if (ok) iend[n % kNF] = head;
+            p.tail = iend[s];
+            ++p.oldest;
         }
-        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-        off = start % RB;
-        return ok != 0;
-    };
-    auto linear_item = [&](const int8_t* src, uint32_t bytes) {
-        if (!bytes || !ok) return;
-        uint32_t off;
-        if (!reserve(item_bytes(bytes), off)) return;
-        const int s = (int)(n % kNF);
-        if (lane == 0) {
-            mbar_arrive_expect_tx(&full[s], bytes);
-            for (uint32_t o = 0; o < bytes; o += 32768u)
-                bulk_g2s(ring + off + o, src + o, min(32768u, bytes - o), &full[s]);
+        if (p.ok) iend[p.n % kNF] = p.head;
+    }
+    p.ok = __shfl_sync(0xFFFFFFFFu, p.ok, 0);
+    return start % RB;
+}
+template <int NB>
+__device__ __noinline__ void prod_linear(Prod& p, const int8_t* src, uint32_t bytes, Ctl ctl) {
+    if (!bytes || !p.ok) return;
+    const uint32_t off = prod_reserve<NB>(p, item_bytes(bytes), ctl);
+    if (!p.ok) return;
+    unsigned char* ring = at<NB, unsigned char>(Lay<NB>::ring);
+    uint64_t* bar = full_bar<NB>((int)(p.n % kNF));
+    if (threadIdx.x % kWarp == 0) {
+        mbar_arrive_expect_tx(bar, bytes);
+#pragma unroll 1
+        for (uint32_t o = 0; o < bytes; o += 32768u) bulk_g2s(ring + off + o, src + o, min(32768u, bytes - o), bar);
+    }
+    __syncwarp();
+    ++p.n;
+}
+template <int NB>
+__device__ __noinline__ void prod_att(Prod& p, const PersistentArgs& a, const uint16_t* kv_layer, int b, int hd,
+                                      int blk0, int nb, Ctl ctl) {
+    if (!p.ok) return;
+    const uint32_t off = prod_reserve<NB>(p, item_bytes((uint32_t)nb * kSlotBytes), ctl);
+    if (!p.ok) return;
+    unsigned char* ring = at<NB, unsigned char>(Lay<NB>::ring);
+    uint64_t* bar = full_bar<NB>((int)(p.n % kNF));
+    const int lane = threadIdx.x % kWarp;
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)nb * kSlotBytes);
+    __syncwarp();
+    if (lane < nb) {
+        int id = a.block_table[(size_t)a.seq_of[b] * a.max_blocks + blk0 + lane];
+        if (id < 0 || id >= a.n_pool_blocks) {
+            if (a.err) atomicOr(a.err, kErrBadIndex);
+            id = 0;
         }
-        __syncwarp();
-        ++n;
-    };
-    auto att_item = [&](const uint16_t* kv_layer, int b, int head_, int blk0, int nb) {
-        if (!ok) return;
-        uint32_t off;
-        if (!reserve(item_bytes((uint32_t)nb * kSlotBytes), off)) return;
-        const int s = (int)(n % kNF);
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)nb * kSlotBytes);
-        __syncwarp();
-        if (lane < nb) {
-            int id = a.block_table[(size_t)a.seq_of[b] * a.max_blocks + blk0 + lane];
-            if (id < 0 || id >= a.n_pool_blocks) {
-                if (a.err) atomicOr(a.err, kErrBadIndex);
-                id = 0;
-            }
-            const uint16_t* src = kv_layer + ((size_t)head_ * a.n_pool_blocks + id) * 2 * kBlockElems;
-            bulk_g2s(ring + off + lane * kSlotBytes, src, kSlotBytes, &full[s]);
-        }
-        __syncwarp();
-        ++n;
-    };
+        const uint16_t* src = kv_layer + ((size_t)hd * a.n_pool_blocks + id) * 2 * kBlockElems;
+        bulk_g2s(ring + off + lane * kSlotBytes, src, kSlotBytes, bar);
+    }
+    __syncwarp();
+    ++p.n;
+}
 
-    for (int l = 0; l < a.L && ok; ++l) {
+// The producer warp: this CTA's slices of every phase, in phase order.
+template <int NB>
+__device__ __noinline__ void producer(const PersistentArgs& a) {
+    constexpr int A = Lay<NB>::att_item;
+    const Shares sh = *at<NB, Shares>(Lay<NB>::shr);
+    const int* pref = at<NB, int>(Lay<NB>::pref);
+    const Ctl ctl = ctl_of<NB>(a);
+    Prod p{0u, 0u, 0u, 0u, 1};
+#pragma unroll 1
+    for (int l = 0; l < a.L && p.ok; ++l) {
         const PersistentLayer& P = a.layers[l];
         const uint16_t* kv_layer = a.kv + (size_t)l * a.kv_layer_elems;
-        linear_item(P.wqkv + (size_t)sh.q_lo * kH, (uint32_t)(sh.q_hi - sh.q_lo) * kH);
+        prod_linear<NB>(p, P.wqkv + (size_t)sh.q_lo * kH, (uint32_t)(sh.q_hi - sh.q_lo) * kH, ctl);
+#pragma unroll 1
         for (int f = sh.a_lo; f < sh.a_hi;) {
             int b, hd, blk, nblk;
             locate(pref, a.B, f, b, hd, blk, nblk);
             const int e = min(sh.a_hi, f - blk + nblk);
-            for (int i = 0; i < e - f; i += A) att_item(kv_layer, b, hd, blk + i, min(A, e - f - i));
+#pragma unroll 1
+            for (int i = 0; i < e - f; i += A) prod_att<NB>(p, a, kv_layer, b, hd, blk + i, min(A, e - f - i), ctl);
             f = e;
         }
-        linear_item(P.wo + (size_t)sh.h_lo * kQD, (uint32_t)(sh.h_hi - sh.h_lo) * kQD);
-        linear_item(P.wgu + (size_t)2 * sh.p_lo * kH, (uint32_t)(2 * (sh.p_hi - sh.p_lo)) * kH);
-        linear_item(P.wd + (size_t)sh.h_lo * kI, (uint32_t)(sh.h_hi - sh.h_lo) * kI);
+        prod_linear<NB>(p, P.wo + (size_t)sh.h_lo * kQD, (uint32_t)(sh.h_hi - sh.h_lo) * kQD, ctl);
+        prod_linear<NB>(p, P.wgu + (size_t)2 * sh.p_lo * kH, (uint32_t)(2 * (sh.p_hi - sh.p_lo)) * kH, ctl);
+        prod_linear<NB>(p, P.wd + (size_t)sh.h_lo * kI, (uint32_t)(sh.h_hi - sh.h_lo) * kI, ctl);
     }
-    for (int r = sh.v_lo; r < sh.v_hi && ok; r += kHeadRows)
-        linear_item(a.embed + (size_t)r * kH, (uint32_t)min(kHeadRows, sh.v_hi - r) * kH);
+#pragma unroll 1
+    for (int r = sh.v_lo; r < sh.v_hi && p.ok; r += kHeadRows)
+        prod_linear<NB>(p, a.embed + (size_t)r * kH, (uint32_t)min(kHeadRows, sh.v_hi - r) * kH, ctl);
 
     // Before leaving, wait (bounded) until every copy it issued has landed,
     // so that none is in flight into this CTA's shared memory if the
     // consumers stop early.
-    if (lane == 0)
-        for (uint32_t i = oldest; i < n; ++i) mbar_wait_bounded(&full[i % kNF], (i / kNF) & 1u, nullptr, 1u << 20);
+    if (threadIdx.x % kWarp == 0) {
+#pragma unroll 1
+        for (uint32_t i = p.oldest; i < p.n; ++i)
+            mbar_wait_bounded(full_bar<NB>((int)(i % kNF)), (i / kNF) & 1u, nullptr, 1u << 20);
+    }
 }
 
 // ------------------------------------------------------------ consumer helpers
 
 // Stage the rows [B][K] of a tagged vector into xs (swizzled rows of K),
-// multiplied by the norm weights nw (when given; thread t's pairs are k = 2 t
-// + 512 j), summing squares of the raw values per row and copying rows
-// [r_lo, r_hi) of the raw values into res.
+// multiplied by the norm weights nw_g when given (thread t's pairs are k =
+// 2 t + 512 j), copying rows [r_lo, r_hi) of the raw values into res, and
+// publishing each warp's per-row sums of squares of the raw values in
+// red[warp][b]. Not inlined: its polling loop runs in registers of its own.
 template <int NB, int K>
-__device__ __forceinline__ bool stage_ll(const uint64_t* src, int B, uint32_t tag, float* xs, const float2* nw,
-                                         float (&ss)[NB], float* res, int r_lo, int r_hi, const Ctl& c) {
+__device__ __noinline__ bool stage_ll(const uint64_t* src, int B, uint32_t tag, float* xs, const float* nw_g,
+                                      float* red, float* res, int r_lo, int r_hi, Ctl c) {
     constexpr int J = K / 512, N = NB * J;
     const int t = threadIdx.x;
+    float2 nw[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+        nw[j] = nw_g ? __ldg(reinterpret_cast<const float2*>(nw_g) + t + 256 * j) : make_float2(1.0f, 1.0f);
+    float ss[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) ss[b] = 0.0f;
+    bool ok = true;
     // Pairs are polled eight at a time; every pair of a group that is not
     // ready yet is re-read together, so a group completes one round trip
     // after its last pair lands.
@@ -357,18 +427,23 @@ __device__ __forceinline__ bool stage_ll(const uint64_t* src, int B, uint32_t ta
             }
         }
         uint32_t spins = 0;
-        while (true) {
+#pragma unroll 1
+        while (ok) {
 #pragma unroll
             for (int u = 0; u < 8; ++u)
                 if (((pending >> u) & 1u) && ll_ok(w[u][0], tag) && ll_ok(w[u][1], tag)) pending &= ~(1u << u);
             if (!pending) break;
-            if (!keep_waiting(spins, c)) return false;
+            if (!keep_waiting(spins, c)) {
+                ok = false;
+                break;
+            }
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const int i = i0 + u, b = i / J, j = i % J;
                 if ((pending >> u) & 1u) ll_ld2(src + (size_t)b * K + 2 * t + 512 * j, w[u][0], w[u][1]);
             }
         }
+        if (!ok) break;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             const int i = i0 + u, b = i / J, j = i % J;
@@ -381,27 +456,41 @@ __device__ __forceinline__ bool stage_ll(const uint64_t* src, int B, uint32_t ta
                 if (k >= r_lo && k < r_hi) res[b * kMaxResRows + k - r_lo] = v0;
                 if (k + 1 >= r_lo && k + 1 < r_hi) res[b * kMaxResRows + k + 1 - r_lo] = v1;
             }
-            xs[b * K + swz(k)] = nw ? __fmul_rn(nw[j].x, v0) : v0;
-            xs[b * K + swz(k + 1)] = nw ? __fmul_rn(nw[j].y, v1) : v1;
+            xs[b * K + swz(k)] = nw_g ? __fmul_rn(nw[j].x, v0) : v0;
+            xs[b * K + swz(k + 1)] = nw_g ? __fmul_rn(nw[j].y, v1) : v1;
         }
     }
-    return true;
+    if (red) {
+        const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float sw = warp_sum(ss[b]);
+            if (lane == 0) red[warp * NB + b] = sw;
+        }
+    }
+    return ok;
 }
 
 // Layer 0's input: embedding rows dequantised (embeddingGather ops.zig:397-411
 // on the int8 table: f32(q) * scale), staged like stage_ll.
 template <int NB>
-__device__ __forceinline__ void stage_embed(const PersistentArgs& a, float* xs, const float2* nw, float (&ss)[NB],
-                                            float* res, int r_lo, int r_hi) {
+__device__ __noinline__ void stage_embed(const uint32_t* tok, int B, int V, const int8_t* embed, const float* sembed,
+                                         uint32_t* err, float* xs, const float* nw_g, float* red, float* res, int r_lo,
+                                         int r_hi) {
     const int t = threadIdx.x;
+    float2 nw[kH / 512];
+#pragma unroll
+    for (int j = 0; j < kH / 512; ++j) nw[j] = __ldg(reinterpret_cast<const float2*>(nw_g) + t + 256 * j);
+    float ss[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-        if (b >= a.B) break;
-        const uint32_t id = a.tok[b];
-        const bool valid = id < (uint32_t)a.V;
-        if (!valid && t == 0 && blockIdx.x == 0 && a.err) atomicOr(a.err, kErrBadIndex);
-        const float sc = valid ? __ldg(a.sembed + id) : 0.0f;
-        const int8_t* row = a.embed + (size_t)(valid ? id : 0) * kH;
+        ss[b] = 0.0f;
+        if (b >= B) continue;
+        const uint32_t id = tok[b];
+        const bool valid = id < (uint32_t)V;
+        if (!valid && t == 0 && blockIdx.x == 0 && err) atomicOr(err, kErrBadIndex);
+        const float sc = valid ? __ldg(sembed + id) : 0.0f;
+        const int8_t* row = embed + (size_t)(valid ? id : 0) * kH;
 #pragma unroll
         for (int j = 0; j < kH / 512; ++j) {
             const int k = 2 * t + 512 * j;
@@ -416,19 +505,16 @@ __device__ __forceinline__ void stage_embed(const PersistentArgs& a, float* xs, 
             xs[b * kH + swz(k + 1)] = __fmul_rn(nw[j].y, v1);
         }
     }
-}
-
-// Per-row sums of squares -> 1 / sqrt(mean + eps) in every consumer thread
-// (after the barrier that follows the staging). red: [kCW][NB].
-template <int NB>
-__device__ __forceinline__ void publish_ss(float (&ss)[NB], float* red) {
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-        const float s = warp_sum(ss[b]);
-        if (lane == 0) red[warp * NB + b] = s;
+        const float sw = warp_sum(ss[b]);
+        if (lane == 0) red[warp * NB + b] = sw;
     }
 }
+
+// 1 / sqrt(mean(x^2) + eps) per row in every consumer thread, from the
+// per-warp sums stage_ll published (after the barrier that follows it).
 template <int NB>
 __device__ __forceinline__ void read_inv(const float* red, int K, float eps, float (&inv)[NB]) {
 #pragma unroll
@@ -486,12 +572,11 @@ __device__ __forceinline__ void dot_rows(const int8_t* w, int nrows, const float
 // last block, this step's K and V rows (qwen_block.zig:191-205: per-head
 // RMSNorm, split-half RoPE, bf16 rounding on append); attn::share_setup with
 // the q, k, v words polled from the tagged QKV output.
-__device__ __forceinline__ bool share_setup_ll(const uint64_t* qkv_row, int head, int pos, bool has_last,
-                                               const float* q_norm, const float* k_norm, const float2* rope,
-                                               int rope_max_pos, float eps, uint32_t tag, float* qb, uint16_t* kvnew,
-                                               uint32_t (&qf)[8][2], const Ctl& c, uint32_t* err) {
+__device__ __noinline__ bool share_setup_ll(const uint64_t* qkv_row, int head, int pos, bool has_last,
+                                            const float* q_norm, const float* k_norm, const float2* rope,
+                                            int rope_max_pos, float eps, uint32_t tag, float* qb, uint16_t* kvnew,
+                                            Ctl c, uint32_t* err) {
     const int lane = threadIdx.x % kWarp;
-    const int g = lane >> 2, t = lane & 3;
     const uint64_t* qsrc = qkv_row + (size_t)(head * kG) * kD;
     const uint64_t* ksrc = qkv_row + kQD + (size_t)head * kD;
     const uint64_t* vsrc = ksrc + (size_t)kNKV * kD;
@@ -518,6 +603,7 @@ __device__ __forceinline__ bool share_setup_ll(const uint64_t* qkv_row, int head
     uint32_t pending = has_last ? 0xFFFFu : 0xFFu;
     uint32_t spins = 0;
     bool ok = true;
+#pragma unroll 1
     while (true) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -584,6 +670,14 @@ __device__ __forceinline__ bool share_setup_ll(const uint64_t* qkv_row, int head
     }
     if (!rope_ok && lane == 0 && err) atomicOr(err, kErrBadIndex);
     __syncwarp();
+    return true;
+}
+
+// The tensor-core B fragments of the two query heads in qb: lanes g < 4 hold
+// (head g / 2, bf16 term g % 2) at dims 16 ks + 2 t (+1, +8, +9).
+__device__ __forceinline__ void q_fragments(const float* qb, uint32_t (&qf)[8][2]) {
+    const int lane = threadIdx.x % kWarp;
+    const int g = lane >> 2, t = lane & 3;
     if (g < 4) {
         const float* qp = qb + (g >> 1) * kD;
         const bool lo_part = g & 1;
@@ -596,14 +690,12 @@ __device__ __forceinline__ bool share_setup_ll(const uint64_t* qkv_row, int head
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) qf[ks][0] = qf[ks][1] = 0u;
     }
-    __syncwarp();
-    return true;
 }
 
 // D = A . B + D for an m16n8k16 tile whose A rows 8..15 are zero: only the
 // row-g outputs (d0, d1) are kept; the zero rows go to scratch registers.
 __device__ __forceinline__ void mma_rows8(float (&d)[2], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-    float z2, z3;
+    float z2, z3;  // rows 8..15: zero, discarded
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%5}, {%7,%8}, "
         "{%9,%10,%11,%11};"
@@ -732,431 +824,425 @@ __device__ __forceinline__ void store_out_ll(uint64_t* out_row, int head, const 
     ll_st(o1 + 0, A1.x * i1, tag); ll_st(o1 + 1, A1.y * i1, tag); ll_st(o1 + 2, A1.z * i1, tag); ll_st(o1 + 3, A1.w * i1, tag);
 }
 
-// ------------------------------------------------------------ the kernel
+// ------------------------------------------------------------ cross-CTA merge
 
-template <int NB>
-__global__ void __launch_bounds__(kFT, 1) decode_flow_kernel(PersistentArgs a) {
-    using LY = Lay<NB>;
-    constexpr uint32_t RB = LY::ring_bytes;
-    constexpr int A = LY::att_item;
-    constexpr unsigned kAll = 0xFFFFFFFFu;
-    extern __shared__ __align__(1024) unsigned char sm[];
-    float* xa = reinterpret_cast<float*>(sm + LY::xa);
-    float* xb = reinterpret_cast<float*>(sm + LY::xb);
-    float* part = reinterpret_cast<float*>(sm + LY::part);
-    float* own = reinterpret_cast<float*>(sm + LY::own);
-    float* qbuf = reinterpret_cast<float*>(sm + LY::qb);
-    uint16_t* kvn = reinterpret_cast<uint16_t*>(sm + LY::kvn);
-    float* res0 = reinterpret_cast<float*>(sm + LY::res);       // layer input x rows [h_lo, h_hi)
-    float* res1 = res0 + NB * kMaxResRows;                        // x1 rows [h_lo, h_hi)
-    float* scl = reinterpret_cast<float*>(sm + LY::scl);
-    float* red = reinterpret_cast<float*>(sm + LY::red);
-    unsigned long long* bestv = reinterpret_cast<unsigned long long*>(sm + LY::best);
-    int* pref = reinterpret_cast<int*>(sm + LY::pref);
-    uint32_t* iend = reinterpret_cast<uint32_t*>(sm + LY::iend);
-    int* flag = reinterpret_cast<int*>(sm + LY::flag);
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + LY::bars);
-    uint64_t* empty = full + kNF;
-    unsigned char* ring = sm + LY::ring;
-
-    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-    const int B = a.B;
-    const int max_len = a.max_blocks * kKvBlock;
-    const Ctl ctl{a.sync + 2, a.err, flag};
-
-    if (threadIdx.x == 0) {
-        *flag = 0;
-        pref[0] = 0;
-        for (int b = 0; b < B; ++b) {
-            const int len = a.positions[b] + 1;
-            if ((len < 1 || len > max_len) && a.err) atomicOr(a.err, kErrBadIndex);
-            pref[b + 1] = pref[b] + (min(max(len, 1), max_len) + kKvBlock - 1) / kKvBlock;
-        }
-    }
-    if (threadIdx.x == kCT) {
-        for (int s = 0; s < kNF; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kCW);
-        }
-        fence_barrier_init();
-    }
-    trace_mark(a, 0);
-    __syncthreads();
-
-    Shares sh;
-    cta_share(kQKV, 1, sh.q_lo, sh.q_hi);
-    cta_share(kH, 1, sh.h_lo, sh.h_hi);
-    cta_share(kI, 1, sh.p_lo, sh.p_hi);
-    cta_share(a.V, 1, sh.v_lo, sh.v_hi);
-    sh.T = pref[B] * kNKV;
-    sh.a_lo = att_lo(blockIdx.x, sh.T);
-    sh.a_hi = att_lo(blockIdx.x + 1, sh.T);
-
-    if (warp == kCW) {
-        producer<NB>(a, sh, pref, ring, full, empty, iend, ctl);
-        return;
-    }
-
-    // ---------------------------------------------------------- consumers
-    uint32_t n_item = 0, rhead = 0;  // ring cursor, as the producer's
-    auto next_item = [&](uint32_t bytes, int& s, uint32_t& parity) -> unsigned char* {
-        const uint32_t start = ring_take<RB>(rhead, item_bytes(bytes));
-        s = (int)(n_item % kNF);
-        parity = (n_item / kNF) & 1u;
-        ++n_item;
-        return ring + start % RB;
-    };
-    auto release = [&](int s) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-    };
-
-    bool ok = true;
-    int ph = 0;
-    const int nq = sh.q_hi - sh.q_lo, nh = sh.h_hi - sh.h_lo, np = sh.p_hi - sh.p_lo;
+// The cross-CTA merge of one (row, kv head): records 0 .. nrec - 1 (record k
+// from CTA first + k, none from CTAs whose attention range is empty) and
+// this CTA's own partial, folded in that order in the log-sum-exp sense,
+// then the normalised output of both query heads as tagged words. Consumer
+// thread t owns query head t / 128, dim t % 128; records are polled eight at
+// a time, all pending words re-read together.
+__device__ __noinline__ bool merge_across_ctas(const uint64_t* rec_bh, int nrec, int first, int T, const float* own,
+                                               uint64_t* out, uint32_t tag, Ctl ctl) {
     const int tid = threadIdx.x;
-
-    for (int l = 0; l < a.L; ++l) {
-        const PersistentLayer& P = a.layers[l];
-        const uint32_t tag = a.tag + (uint32_t)l + 1u;
-        const uint32_t tag_prev = a.tag + (uint32_t)l;  // layer l - 1's x
-        uint16_t* kv_layer = a.kv + (size_t)l * a.kv_layer_elems;
-
-        // ---------------- QKV
-        {
-            for (int i = tid; i < nq; i += kCT) scl[i] = __ldg(P.sqkv + sh.q_lo + i);
-            float2 nw[kH / 512];
-#pragma unroll
-            for (int j = 0; j < kH / 512; ++j) nw[j] = __ldg(reinterpret_cast<const float2*>(P.input_ln) + tid + 256 * j);
-            float ss[NB];
-#pragma unroll
-            for (int b = 0; b < NB; ++b) ss[b] = 0.0f;
-            if (l == 0) stage_embed<NB>(a, xa, nw, ss, res0, sh.h_lo, sh.h_hi);
-            else ok = stage_ll<NB, kH>(a.llx, B, tag_prev, xa, nw, ss, res0, sh.h_lo, sh.h_hi, ctl);
-            publish_ss<NB>(ss, red);
-            if (!(ok = cbar_and(ok))) break;
-            trace_mark(a, 1 + 2 * ph);
-            float inv[NB];
-            read_inv<NB>(red, kH, a.eps, inv);
-            int s;
-            uint32_t par;
-            const unsigned char* item = nq ? next_item((uint32_t)nq * kH, s, par) : nullptr;
-            if (item) {
-                constexpr int R = 4;
-                const int units = (nq + R - 1) / R;
-                bool have = false;
-                for (int u = warp; u < units; u += kCW) {
-                    if (!have) {
-                        if (!(ok = __all_sync(kAll, mbar_wait_ctl(&full[s], par, ctl)))) break;
-                        have = true;
-                    }
-                    const int r0 = u * R;
-                    float acc[R][NB];
-                    dot_rows<NB, R, kH>(reinterpret_cast<const int8_t*>(item) + (size_t)r0 * kH, min(R, nq - r0), xa, B, acc);
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-#pragma unroll
-                        for (int b = 0; b < NB; ++b)
-                            if (b < B && r0 + r < nq && lane == ((r * NB + b) & 31))
-                                ll_st(a.llqkv + (size_t)b * kQKV + sh.q_lo + r0 + r,
-                                      __fmul_rn(__fmul_rn(acc[r][b], inv[b]), scl[r0 + r]), tag);
-                }
-                release(s);
-            }
-            trace_mark(a, 2 + 2 * ph++);
+    const int hh = tid >> 7, d = tid & (kD - 1);
+    const uint64_t* rec0 = rec_bh + hh * kRecHead;
+    const bool all_live = T >= (int)gridDim.x;
+    float Mr = -INFINITY, Lr = 0.0f, Ar = 0.0f;
+    auto fold = [&](float m, float lsum, float av) {
+        if (m == -INFINITY) return;
+        if (m > Mr) {
+            const float cr = expf(Mr - m);
+            Lr *= cr;
+            Ar *= cr;
+            Mr = m;
         }
-        if (!(ok = cbar_and(ok))) break;  // scl and xa are rewritten by the next phases
-
-        // ---------------- ATT
-        trace_mark(a, 1 + 2 * ph);
-        {
-            int par_buf = 0;
-            bool merger = false;
-            int m_b = 0, m_head = 0, m_nrec = 0, m_first = 0;
-            for (int f = sh.a_lo; f < sh.a_hi;) {
-                int b, hd, blk0, nblk;
-                locate(pref, B, f, b, hd, blk0, nblk);
-                const int F0 = f - blk0;
-                const int e = min(sh.a_hi, F0 + nblk);
-                const int nb = e - f;
-                const bool starts = f == F0, ends = e == F0 + nblk;
-                const int pos = a.positions[b];
-                const int kv_len = min(max(pos + 1, 1), max_len);
-                // this warp's blocks of the piece: i = warp, warp + kCW, ...
-                const bool have = warp < nb;
-                const bool holds_last = ends && ((nb - 1) % kCW) == warp;
-                uint16_t* kvnew = kvn + warp * 2 * kD;
-                uint16_t* last_k = nullptr;
-                if (holds_last) {
-                    int id = a.block_table[(size_t)a.seq_of[b] * a.max_blocks + nblk - 1];
-                    if (id < 0 || id >= a.n_pool_blocks) id = 0;  // the producer reports it
-                    last_k = kv_layer + ((size_t)hd * a.n_pool_blocks + id) * 2 * kBlockElems;
-                }
-                uint32_t qf[8][2];
-                if (have && ok)
-                    ok = share_setup_ll(a.llqkv + (size_t)b * kQKV, hd, pos, holds_last, P.q_norm, P.k_norm, a.rope,
-                                        a.rope_max_pos, a.eps, tag, qbuf + warp * kG * kD, kvnew, qf, ctl, a.err);
-                float acc[16][2];
-#pragma unroll
-                for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = 0.0f;
-                float m_run = -INFINITY, l_run = 0.0f;
-                for (int i0 = 0; i0 < nb; i0 += A) {
-                    int s;
-                    uint32_t par;
-                    const unsigned char* item = next_item((uint32_t)min(A, nb - i0) * kSlotBytes, s, par);
-                    int mine = -1;
-                    for (int i = i0; i < min(nb, i0 + A); ++i)
-                        if (i % kCW == warp) mine = i;
-                    if (mine >= 0 && ok) {
-                        ok = __all_sync(kAll, mbar_wait_ctl(&full[s], par, ctl));
-                        if (ok) {
-                            unsigned char* kb = const_cast<unsigned char*>(item) + (size_t)(mine - i0) * kSlotBytes;
-                            const int blk = blk0 + mine;
-                            const int nv = min(kKvBlock, kv_len - blk * kKvBlock);
-                            const bool last = blk == nblk - 1;
-                            if (last) attn::patch_new_row(last_k, kb, nv - 1, kvnew);
-                            if (nv < kKvBlock) {
-                                uint4* vrow = reinterpret_cast<uint4*>(kb + kBlockBytes + nv * kD * 2);
-                                for (int x = lane; x < (kKvBlock - nv) * (kD * 2 / 16); x += kWarp)
-                                    vrow[x] = make_uint4(0u, 0u, 0u, 0u);
-                            }
-                            __syncwarp();
-                            attend_block(kb, nv, qf, acc, m_run, l_run);
-                            if (nv < kKvBlock || last) attn::fence_proxy_async_smem();
-                        }
-                    }
-                    release(s);
-                }
-                float* pbuf = part + (size_t)par_buf * kCW * kPartStride;
-                if (have && ok) warp_partial(acc, l_run, m_run, pbuf + warp * kPartStride);
-                if (!(ok = cbar_and(ok))) break;
-                if (warp == 0) {
-                    float M[kG], L[kG];
-                    float4 A0, A1;
-                    attn::merge_records<false, 8>(pbuf, min(nb, kCW), M, L, A0, A1);
-                    if (starts && ends) {
-                        store_out_ll(a.llattn + (size_t)b * kQD, hd, L, A0, A1, tag);
-                    } else if (ends) {
-                        attn::merged_store_record(M, L, A0, A1, own);
-                    } else {
-                        const int k = (int)blockIdx.x - cta_of(F0, sh.T);
-                        store_record_ll(a.llrec + (((size_t)b * kNKV + hd) * gridDim.x + k) * kRecWords, M, L, A0, A1,
-                                        tag);
-                    }
-                }
-                if (!starts && ends) {
-                    merger = true;
-                    m_b = b;
-                    m_head = hd;
-                    m_first = cta_of(F0, sh.T);
-                    m_nrec = (int)blockIdx.x - m_first;
-                }
-                par_buf ^= 1;
-                f = e;
-            }
-            if (!ok) break;
-            if (merger) {
-                // the CTA holding a row's last block merges the records of the
-                // CTAs before it (in CTA order) and its own, then publishes
-                // the output: thread t owns query head t / 128, dim t % 128
-                if (!(ok = cbar_and(ok))) break;
-                const int hh = tid >> 7, d = tid & (kD - 1);
-                const uint64_t* rec0 = a.llrec + ((size_t)m_b * kNKV + m_head) * gridDim.x * kRecWords + hh * kRecHead;
-                float Mr = -INFINITY, Lr = 0.0f, Ar = 0.0f;
-                auto fold = [&](float m, float lsum, float av) {
-                    if (m == -INFINITY) return;
-                    if (m > Mr) {
-                        const float cr = expf(Mr - m);
-                        Lr *= cr;
-                        Ar *= cr;
-                        Mr = m;
-                    }
-                    const float ex = expf(m - Mr);
-                    Lr = fmaf(lsum, ex, Lr);
-                    Ar = fmaf(av, ex, Ar);
-                };
-                // CTA m_first + k wrote record k, unless its range is empty
-                const bool all_live = sh.T >= (int)gridDim.x;
-                auto live = [&](int k) {
-                    const int c = m_first + k;
-                    return all_live || att_lo(c, sh.T) < att_lo(c + 1, sh.T);
-                };
-                for (int k0 = 0; k0 < m_nrec && ok; k0 += 8) {
-                    uint64_t wm[8], wl[8], wa[8];
-                    uint32_t pending = 0u;
-#pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        if (k0 + u < m_nrec && live(k0 + u)) {
-                            const uint64_t* r = rec0 + (size_t)(k0 + u) * kRecWords;
-                            ll_ld2(r, wm[u], wl[u]);
-                            wa[u] = ll_ld(r + 2 + d);
-                            pending |= 1u << u;
-                        }
-                    uint32_t spins = 0;
-                    while (true) {
-#pragma unroll
-                        for (int u = 0; u < 8; ++u)
-                            if (((pending >> u) & 1u) && ll_ok(wm[u], tag) && ll_ok(wl[u], tag) && ll_ok(wa[u], tag))
-                                pending &= ~(1u << u);
-                        if (!pending) break;
-                        if (!keep_waiting(spins, ctl)) {
-                            ok = false;
-                            break;
-                        }
-#pragma unroll
-                        for (int u = 0; u < 8; ++u)
-                            if ((pending >> u) & 1u) {
-                                const uint64_t* r = rec0 + (size_t)(k0 + u) * kRecWords;
-                                ll_ld2(r, wm[u], wl[u]);
-                                wa[u] = ll_ld(r + 2 + d);
-                            }
-                    }
-#pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        if (ok && k0 + u < m_nrec && live(k0 + u)) fold(ll_val(wm[u]), ll_val(wl[u]), ll_val(wa[u]));
-                }
-                fold(own[hh * kPartHead], own[hh * kPartHead + 1], own[hh * kPartHead + 4 + d]);
-                if (ok) ll_st(a.llattn + (size_t)m_b * kQD + (size_t)(m_head * kG + hh) * kD + d, Ar * (1.0f / Lr), tag);
-            }
+        const float ex = expf(m - Mr);
+        Lr = fmaf(lsum, ex, Lr);
+        Ar = fmaf(av, ex, Ar);
+    };
+#pragma unroll 1
+    for (int k0 = 0; k0 < nrec; k0 += 8) {
+        uint64_t wm[8], wl[8], wa[8];
+        uint32_t live = 0u;
+#pragma unroll 1
+        for (int u = 0; u < 8; ++u) {
+            const int c = first + k0 + u;
+            if (k0 + u < nrec && (all_live || att_lo(c, T) < att_lo(c + 1, T))) live |= 1u << u;
         }
-        trace_mark(a, 2 + 2 * ph++);
-
-        // ---------------- O (+ residual)
-        {
-            for (int i = tid; i < nh; i += kCT) scl[i] = __ldg(P.so + sh.h_lo + i);
-            float ss[NB];
+        uint32_t pending = live;
 #pragma unroll
-            for (int b = 0; b < NB; ++b) ss[b] = 0.0f;
-            if (ok) ok = stage_ll<NB, kQD>(a.llattn, B, tag, xb, nullptr, ss, nullptr, 0, 0, ctl);
-            if (!(ok = cbar_and(ok))) break;
-            trace_mark(a, 1 + 2 * ph);
-            int s;
-            uint32_t par;
-            const unsigned char* item = nh ? next_item((uint32_t)nh * kQD, s, par) : nullptr;
-            if (item) {
-                for (int u = warp; u < nh; u += kCW) {
-                    if (u == warp && !(ok = __all_sync(kAll, mbar_wait_ctl(&full[s], par, ctl)))) break;
-                    float acc[1][NB];
-                    dot_rows<NB, 1, kQD>(reinterpret_cast<const int8_t*>(item) + (size_t)u * kQD, 1, xb, B, acc);
-#pragma unroll
-                    for (int b = 0; b < NB; ++b)
-                        if (b < B && lane == b)
-                            ll_st(a.llx1 + (size_t)b * kH + sh.h_lo + u,
-                                  __fadd_rn(res0[b * kMaxResRows + u], __fmul_rn(acc[0][b], scl[u])), tag);
-                }
-                release(s);
+        for (int u = 0; u < 8; ++u)
+            if ((live >> u) & 1u) {
+                const uint64_t* r = rec0 + (size_t)(k0 + u) * kRecWords;
+                ll_ld2(r, wm[u], wl[u]);
+                wa[u] = ll_ld(r + 2 + d);
             }
-            trace_mark(a, 2 + 2 * ph++);
-        }
-        if (!(ok = cbar_and(ok))) break;
-
-        // ---------------- GU (+ SwiGLU)
-        {
-            for (int i = tid; i < 2 * np; i += kCT) scl[i] = __ldg(P.sgu + 2 * sh.p_lo + i);
-            float2 nw[kH / 512];
+        uint32_t spins = 0;
+#pragma unroll 1
+        while (true) {
 #pragma unroll
-            for (int j = 0; j < kH / 512; ++j) nw[j] = __ldg(reinterpret_cast<const float2*>(P.post_ln) + tid + 256 * j);
-            float ss[NB];
+            for (int u = 0; u < 8; ++u)
+                if (((pending >> u) & 1u) && ll_ok(wm[u], tag) && ll_ok(wl[u], tag) && ll_ok(wa[u], tag))
+                    pending &= ~(1u << u);
+            if (!pending) break;
+            if (!keep_waiting(spins, ctl)) return false;
 #pragma unroll
-            for (int b = 0; b < NB; ++b) ss[b] = 0.0f;
-            if (ok) ok = stage_ll<NB, kH>(a.llx1, B, tag, xa, nw, ss, res1, sh.h_lo, sh.h_hi, ctl);
-            publish_ss<NB>(ss, red);
-            if (!(ok = cbar_and(ok))) break;
-            trace_mark(a, 1 + 2 * ph);
-            float inv[NB];
-            read_inv<NB>(red, kH, a.eps, inv);
-            int s;
-            uint32_t par;
-            const unsigned char* item = np ? next_item((uint32_t)(2 * np) * kH, s, par) : nullptr;
-            if (item) {
-                constexpr int R = 6;  // three (gate, up) pairs
-                const int rows = 2 * np, units = (rows + R - 1) / R;
-                bool have = false;
-                for (int u = warp; u < units; u += kCW) {
-                    if (!have) {
-                        if (!(ok = __all_sync(kAll, mbar_wait_ctl(&full[s], par, ctl)))) break;
-                        have = true;
-                    }
-                    const int r0 = u * R;
-                    float acc[R][NB];
-                    dot_rows<NB, R, kH>(reinterpret_cast<const int8_t*>(item) + (size_t)r0 * kH, min(R, rows - r0), xa, B, acc);
-#pragma unroll
-                    for (int p = 0; p < R / 2; ++p)
-#pragma unroll
-                        for (int b = 0; b < NB; ++b) {
-                            const int row = r0 + 2 * p;
-                            if (b < B && row < rows && lane == ((p * NB + b) & 31)) {
-                                const float gate = __fmul_rn(__fmul_rn(acc[2 * p][b], inv[b]), scl[row]);
-                                const float upv = __fmul_rn(__fmul_rn(acc[2 * p + 1][b], inv[b]), scl[row + 1]);
-                                ll_st(a.llh + (size_t)b * kI + sh.p_lo + (row >> 1), __fmul_rn(silu(gate), upv), tag);
-                            }
-                        }
+            for (int u = 0; u < 8; ++u)
+                if ((pending >> u) & 1u) {
+                    const uint64_t* r = rec0 + (size_t)(k0 + u) * kRecWords;
+                    ll_ld2(r, wm[u], wl[u]);
+                    wa[u] = ll_ld(r + 2 + d);
                 }
-                release(s);
-            }
-            trace_mark(a, 2 + 2 * ph++);
         }
-        if (!(ok = cbar_and(ok))) break;
-
-        // ---------------- D (+ residual)
-        {
-            for (int i = tid; i < nh; i += kCT) scl[i] = __ldg(P.sd + sh.h_lo + i);
-            float ss[NB];
 #pragma unroll
-            for (int b = 0; b < NB; ++b) ss[b] = 0.0f;
-            if (ok) ok = stage_ll<NB, kI>(a.llh, B, tag, xb, nullptr, ss, nullptr, 0, 0, ctl);
-            if (!(ok = cbar_and(ok))) break;
-            trace_mark(a, 1 + 2 * ph);
-            int s;
-            uint32_t par;
-            const unsigned char* item = nh ? next_item((uint32_t)nh * kI, s, par) : nullptr;
-            if (item) {
-                for (int u = warp; u < nh; u += kCW) {
-                    if (u == warp && !(ok = __all_sync(kAll, mbar_wait_ctl(&full[s], par, ctl)))) break;
-                    float acc[1][NB];
-                    dot_rows<NB, 1, kI>(reinterpret_cast<const int8_t*>(item) + (size_t)u * kI, 1, xb, B, acc);
-#pragma unroll
-                    for (int b = 0; b < NB; ++b)
-                        if (b < B && lane == b)
-                            ll_st(a.llx + (size_t)b * kH + sh.h_lo + u,
-                                  __fadd_rn(res1[b * kMaxResRows + u], __fmul_rn(acc[0][b], scl[u])), tag);
-                }
-                release(s);
-            }
-            trace_mark(a, 2 + 2 * ph++);
-        }
-        if (!(ok = cbar_and(ok))) break;
+        for (int u = 0; u < 8; ++u)
+            if ((live >> u) & 1u) fold(ll_val(wm[u]), ll_val(wl[u]), ll_val(wa[u]));
     }
+    fold(own[hh * kPartHead], own[hh * kPartHead + 1], own[hh * kPartHead + 4 + d]);
+    ll_st(out + (size_t)hh * kD + d, Ar * (1.0f / Lr), tag);
+    return true;
+}
 
-    // ---------------- HEAD: final RMSNorm, tied LM head rows, argmax
+// ------------------------------------------------------------ consumer phases
+//
+// Each phase is a function of its own (not inlined): it holds only its own
+// state in registers, and nothing but the layer index lives across phases.
+// The consumer warps' ring cursor lives in shared memory. Every phase ends
+// with a consumer barrier that ANDs the success flags; a false return ends
+// the step for every consumer warp together.
+
+// The consumer side of the ring: the next item's shared-memory address, its
+// barrier slot and phase parity, in the order the producer issued them.
+template <int NB>
+struct Cursor {
+    uint32_t n, head;
+    __device__ __forceinline__ Cursor() {
+        const uint2 c = at<NB, uint2>(Lay<NB>::cur)[threadIdx.x / kWarp];
+        n = c.x;
+        head = c.y;
+    }
+    __device__ __forceinline__ void save() const {
+        __syncwarp();
+        if (threadIdx.x % kWarp == 0) at<NB, uint2>(Lay<NB>::cur)[threadIdx.x / kWarp] = make_uint2(n, head);
+        __syncwarp();
+    }
+    __device__ __forceinline__ const unsigned char* next(uint32_t bytes, int& s, uint32_t& parity) {
+        constexpr uint32_t RB = Lay<NB>::ring_bytes;
+        const uint32_t start = ring_take<RB>(head, item_bytes(bytes));
+        s = (int)(n % kNF);
+        parity = (n / kNF) & 1u;
+        ++n;
+        return at<NB, unsigned char>(Lay<NB>::ring) + start % RB;
+    }
+};
+template <int NB>
+__device__ __forceinline__ void release_item(int s) {
+    __syncwarp();
+    if (threadIdx.x % kWarp == 0) mbar_arrive(empty_bar<NB>(s));
+}
+template <int NB>
+__device__ __forceinline__ bool wait_item(int s, uint32_t parity, const Ctl& ctl) {
+    return __all_sync(0xFFFFFFFFu, mbar_wait_ctl(full_bar<NB>(s), parity, ctl));
+}
+
+// QKV: RMSNorm(input_ln) + this CTA's fused QKV rows (layer 0 stages the
+// embedding rows instead of the previous layer's output).
+template <int NB>
+__device__ __noinline__ bool qkv_phase(const PersistentArgs& a, int l) {
+    using LY = Lay<NB>;
+    const Shares sh = *at<NB, Shares>(LY::shr);
+    const PersistentLayer& P = a.layers[l];
+    const uint32_t tag = a.tag + (uint32_t)l + 1u;
+    const Ctl ctl = ctl_of<NB>(a);
+    const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp, B = a.B;
+    float* xa = at<NB, float>(LY::xa);
+    float* scl = at<NB, float>(LY::scl);
+    float* red = at<NB, float>(LY::red);
+    float* res0 = at<NB, float>(LY::res);
+    const int nq = sh.q_hi - sh.q_lo;
+#pragma unroll 1
+    for (int i = tid; i < nq; i += kCT) scl[i] = __ldg(P.sqkv + sh.q_lo + i);
+    bool ok = true;
+    if (l == 0)
+        stage_embed<NB>(a.tok, B, a.V, a.embed, a.sembed, a.err, xa, P.input_ln, red, res0, sh.h_lo, sh.h_hi);
+    else
+        ok = stage_ll<NB, kH>(a.llx, B, tag - 1u, xa, P.input_ln, red, res0, sh.h_lo, sh.h_hi, ctl);
+    if (!cbar_and(ok)) return false;
+    trace_mark(a, 1 + 10 * l);
+    float inv[NB];
+    read_inv<NB>(red, kH, a.eps, inv);
+    Cursor<NB> cur;
+    if (nq) {
+        int s;
+        uint32_t par;
+        const unsigned char* item = cur.next((uint32_t)nq * kH, s, par);
+        constexpr int R = 4;
+        const int units = (nq + R - 1) / R;
+        if (warp < units) ok = wait_item<NB>(s, par, ctl);
+#pragma unroll 1
+        for (int u = warp; u < units && ok; u += kCW) {
+            const int r0 = u * R;
+            float acc[R][NB];
+            dot_rows<NB, R, kH>(reinterpret_cast<const int8_t*>(item) + (size_t)r0 * kH, min(R, nq - r0), xa, B, acc);
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int b = 0; b < NB; ++b)
+                    if (b < B && r0 + r < nq && lane == ((r * NB + b) & 31))
+                        ll_st(a.llqkv + (size_t)b * kQKV + sh.q_lo + r0 + r,
+                              __fmul_rn(__fmul_rn(acc[r][b], inv[b]), scl[r0 + r]), tag);
+        }
+        release_item<NB>(s);
+    }
+    cur.save();
+    trace_mark(a, 2 + 10 * l);
+    return cbar_and(ok);  // scl and xa are rewritten by the next phases
+}
+
+// ATT: this CTA's range of KV blocks, piece by piece (one piece per
+// (row, kv head) it overlaps); see the file comment.
+template <int NB>
+__device__ __noinline__ bool att_phase(const PersistentArgs& a, int l) {
+    using LY = Lay<NB>;
+    constexpr int A = LY::att_item;
+    const Shares sh = *at<NB, Shares>(LY::shr);
+    const PersistentLayer& P = a.layers[l];
+    const uint32_t tag = a.tag + (uint32_t)l + 1u;
+    const Ctl ctl = ctl_of<NB>(a);
+    const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp, B = a.B;
+    const int max_len = a.max_blocks * kKvBlock;
+    const int* pref = at<NB, int>(LY::pref);
+    float* part = at<NB, float>(LY::part);
+    float* own = at<NB, float>(LY::own);
+    float* qb = at<NB, float>(LY::qb) + warp * kG * kD;
+    uint16_t* kvnew = at<NB, uint16_t>(LY::kvn) + warp * 2 * kD;
+    uint16_t* kv_layer = a.kv + (size_t)l * a.kv_layer_elems;
+    trace_mark(a, 3 + 10 * l);
+    Cursor<NB> cur;
+    bool ok = true;
+    int par_buf = 0;
+    int m_b = -1, m_head = 0, m_nrec = 0, m_first = 0;
+#pragma unroll 1
+    for (int f = sh.a_lo; f < sh.a_hi;) {
+        int b, hd, blk0, nblk;
+        locate(pref, B, f, b, hd, blk0, nblk);
+        const int F0 = f - blk0;
+        const int e = min(sh.a_hi, F0 + nblk);
+        const int nb = e - f;
+        const bool starts = f == F0, ends = e == F0 + nblk;
+        const int pos = a.positions[b];
+        const int kv_len = min(max(pos + 1, 1), max_len);
+        // this warp's blocks of the piece: i = warp, warp + kCW, ...
+        const bool have = warp < nb;
+        const bool holds_last = ends && ((nb - 1) % kCW) == warp;
+        uint16_t* last_k = nullptr;
+        if (holds_last) {
+            int id = a.block_table[(size_t)a.seq_of[b] * a.max_blocks + nblk - 1];
+            if (id < 0 || id >= a.n_pool_blocks) id = 0;  // the producer reports it
+            last_k = kv_layer + ((size_t)hd * a.n_pool_blocks + id) * 2 * kBlockElems;
+        }
+        uint32_t qf[8][2];
+        if (have && ok)
+            ok = share_setup_ll(a.llqkv + (size_t)b * kQKV, hd, pos, holds_last, P.q_norm, P.k_norm, a.rope,
+                                a.rope_max_pos, a.eps, tag, qb, kvnew, ctl, a.err);
+        if (have && ok) q_fragments(qb, qf);
+        float acc[16][2];
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) acc[nt][0] = acc[nt][1] = 0.0f;
+        float m_run = -INFINITY, l_run = 0.0f;
+#pragma unroll 1
+        for (int i0 = 0; i0 < nb; i0 += A) {
+            int s;
+            uint32_t par;
+            const unsigned char* item = cur.next((uint32_t)min(A, nb - i0) * kSlotBytes, s, par);
+            // this warp's block of the item (at most one: A <= kCW)
+            const int mine = i0 + ((warp - i0 % kCW + kCW) % kCW);
+            if (mine < min(nb, i0 + A) && ok) {
+                ok = wait_item<NB>(s, par, ctl);
+                if (ok) {
+                    unsigned char* kb = const_cast<unsigned char*>(item) + (size_t)(mine - i0) * kSlotBytes;
+                    const int blk = blk0 + mine;
+                    const int nv = min(kKvBlock, kv_len - blk * kKvBlock);
+                    const bool last = blk == nblk - 1;
+                    if (last) attn::patch_new_row(last_k, kb, nv - 1, kvnew);
+                    if (nv < kKvBlock) {
+                        uint4* vrow = reinterpret_cast<uint4*>(kb + kBlockBytes + nv * kD * 2);
+#pragma unroll 1
+                        for (int x = lane; x < (kKvBlock - nv) * (kD * 2 / 16); x += kWarp)
+                            vrow[x] = make_uint4(0u, 0u, 0u, 0u);
+                    }
+                    __syncwarp();
+                    attend_block(kb, nv, qf, acc, m_run, l_run);
+                    if (nv < kKvBlock || last) attn::fence_proxy_async_smem();
+                }
+            }
+            release_item<NB>(s);
+        }
+        float* pbuf = part + (size_t)par_buf * kCW * kPartStride;
+        if (have && ok) warp_partial(acc, l_run, m_run, pbuf + warp * kPartStride);
+        if (!(ok = cbar_and(ok))) break;
+        if (warp == 0) {
+            float M[kG], L[kG];
+            float4 A0, A1;
+            attn::merge_records<false, 8>(pbuf, min(nb, kCW), M, L, A0, A1);
+            if (starts && ends) {
+                store_out_ll(a.llattn + (size_t)b * kQD, hd, L, A0, A1, tag);
+            } else if (ends) {
+                attn::merged_store_record(M, L, A0, A1, own);
+            } else {
+                const int k = (int)blockIdx.x - cta_of(F0, sh.T);
+                store_record_ll(a.llrec + (((size_t)b * kNKV + hd) * gridDim.x + k) * kRecWords, M, L, A0, A1, tag);
+            }
+        }
+        if (!starts && ends) {
+            m_b = b;
+            m_head = hd;
+            m_first = cta_of(F0, sh.T);
+            m_nrec = (int)blockIdx.x - m_first;
+        }
+        par_buf ^= 1;
+        f = e;
+    }
+    cur.save();
+    if (ok && m_b >= 0) {
+        // the CTA holding a row's last block merges the records of the CTAs
+        // before it (in CTA order) with its own and publishes the output
+        ok = cbar_and(ok);
+        if (ok)
+            ok = merge_across_ctas(a.llrec + ((size_t)m_b * kNKV + m_head) * gridDim.x * kRecWords, m_nrec, m_first,
+                                   sh.T, own, a.llattn + (size_t)m_b * kQD + (size_t)m_head * kG * kD, tag, ctl);
+    }
+    trace_mark(a, 4 + 10 * l);
+    return cbar_and(ok);
+}
+
+// O (+ residual) and D (+ residual): rows [h_lo, h_hi), one per warp, over
+// the staged attention output (K = 2048) or SwiGLU output (K = 3072).
+template <int NB, int K>
+__device__ __noinline__ bool out_phase(const PersistentArgs& a, int l) {
+    using LY = Lay<NB>;
+    const Shares sh = *at<NB, Shares>(LY::shr);
+    const PersistentLayer& P = a.layers[l];
+    constexpr bool is_o = K == kQD;
+    const uint32_t tag = a.tag + (uint32_t)l + 1u;
+    const Ctl ctl = ctl_of<NB>(a);
+    const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp, B = a.B;
+    float* xb = at<NB, float>(LY::xb);
+    float* scl = at<NB, float>(LY::scl);
+    const float* res = at<NB, float>(LY::res) + (is_o ? 0 : NB * kMaxResRows);
+    const int nh = sh.h_hi - sh.h_lo;
+    const float* sg = is_o ? P.so : P.sd;
+#pragma unroll 1
+    for (int i = tid; i < nh; i += kCT) scl[i] = __ldg(sg + sh.h_lo + i);
+    bool ok = stage_ll<NB, K>(is_o ? a.llattn : a.llh, B, tag, xb, nullptr, nullptr, nullptr, 0, 0, ctl);
+    if (!cbar_and(ok)) return false;
+    constexpr int slot = is_o ? 5 : 9;
+    trace_mark(a, slot + 10 * l);
+    Cursor<NB> cur;
+    uint64_t* dst = is_o ? a.llx1 : a.llx;
+    if (nh) {
+        int s;
+        uint32_t par;
+        const unsigned char* item = cur.next((uint32_t)nh * K, s, par);
+        if (warp < nh) ok = wait_item<NB>(s, par, ctl);
+#pragma unroll 1
+        for (int u = warp; u < nh && ok; u += kCW) {
+            float acc[1][NB];
+            dot_rows<NB, 1, K>(reinterpret_cast<const int8_t*>(item) + (size_t)u * K, 1, xb, B, acc);
+#pragma unroll
+            for (int b = 0; b < NB; ++b)
+                if (b < B && lane == b)
+                    ll_st(dst + (size_t)b * kH + sh.h_lo + u,
+                          __fadd_rn(res[b * kMaxResRows + u], __fmul_rn(acc[0][b], scl[u])), tag);
+        }
+        release_item<NB>(s);
+    }
+    cur.save();
+    trace_mark(a, slot + 1 + 10 * l);
+    return cbar_and(ok);
+}
+
+// GU (+ SwiGLU): RMSNorm(post_ln) + gate/up pairs [p_lo, p_hi).
+template <int NB>
+__device__ __noinline__ bool gu_phase(const PersistentArgs& a, int l) {
+    using LY = Lay<NB>;
+    const Shares sh = *at<NB, Shares>(LY::shr);
+    const PersistentLayer& P = a.layers[l];
+    const uint32_t tag = a.tag + (uint32_t)l + 1u;
+    const Ctl ctl = ctl_of<NB>(a);
+    const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp, B = a.B;
+    float* xa = at<NB, float>(LY::xa);
+    float* scl = at<NB, float>(LY::scl);
+    float* red = at<NB, float>(LY::red);
+    float* res1 = at<NB, float>(LY::res) + NB * kMaxResRows;
+    const int np = sh.p_hi - sh.p_lo;
+#pragma unroll 1
+    for (int i = tid; i < 2 * np; i += kCT) scl[i] = __ldg(P.sgu + 2 * sh.p_lo + i);
+    bool ok = stage_ll<NB, kH>(a.llx1, B, tag, xa, P.post_ln, red, res1, sh.h_lo, sh.h_hi, ctl);
+    if (!cbar_and(ok)) return false;
+    trace_mark(a, 7 + 10 * l);
+    float inv[NB];
+    read_inv<NB>(red, kH, a.eps, inv);
+    Cursor<NB> cur;
+    if (np) {
+        int s;
+        uint32_t par;
+        const unsigned char* item = cur.next((uint32_t)(2 * np) * kH, s, par);
+        constexpr int R = 6;  // three (gate, up) pairs
+        const int rows = 2 * np, units = (rows + R - 1) / R;
+        if (warp < units) ok = wait_item<NB>(s, par, ctl);
+#pragma unroll 1
+        for (int u = warp; u < units && ok; u += kCW) {
+            const int r0 = u * R;
+            float acc[R][NB];
+            dot_rows<NB, R, kH>(reinterpret_cast<const int8_t*>(item) + (size_t)r0 * kH, min(R, rows - r0), xa, B, acc);
+#pragma unroll
+            for (int p = 0; p < R / 2; ++p)
+#pragma unroll
+                for (int b = 0; b < NB; ++b) {
+                    const int row = r0 + 2 * p;
+                    if (b < B && row < rows && lane == ((p * NB + b) & 31)) {
+                        const float gate = __fmul_rn(__fmul_rn(acc[2 * p][b], inv[b]), scl[row]);
+                        const float upv = __fmul_rn(__fmul_rn(acc[2 * p + 1][b], inv[b]), scl[row + 1]);
+                        ll_st(a.llh + (size_t)b * kI + sh.p_lo + (row >> 1), __fmul_rn(silu(gate), upv), tag);
+                    }
+                }
+        }
+        release_item<NB>(s);
+    }
+    cur.save();
+    trace_mark(a, 8 + 10 * l);
+    return cbar_and(ok);
+}
+
+// HEAD: final RMSNorm, this CTA's tied LM head rows, argmax (topK(1),
+// qwen_forward.zig:177-193); the last CTA to finish turns the keys into next
+// tokens and advances the rows.
+template <int NB>
+__device__ __noinline__ void head_phase(const PersistentArgs& a, bool ok) {
+    using LY = Lay<NB>;
+    constexpr unsigned kAll = 0xFFFFFFFFu;
+    const Shares sh = *at<NB, Shares>(LY::shr);
+    const Ctl ctl = ctl_of<NB>(a);
+    const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp, B = a.B;
+    float* xa = at<NB, float>(LY::xa);
+    float* red = at<NB, float>(LY::red);
+    unsigned long long* bestv = at<NB, unsigned long long>(LY::best);
+    const int hslot = 1 + 10 * a.L;
     unsigned long long best[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) best[b] = 0ull;
     if (ok) {
-        float2 nw[kH / 512];
-#pragma unroll
-        for (int j = 0; j < kH / 512; ++j) nw[j] = __ldg(reinterpret_cast<const float2*>(a.final_norm) + tid + 256 * j);
-        float ss[NB];
-#pragma unroll
-        for (int b = 0; b < NB; ++b) ss[b] = 0.0f;
-        ok = stage_ll<NB, kH>(a.llx, B, a.tag + (uint32_t)a.L, xa, nw, ss, nullptr, 0, 0, ctl);
-        publish_ss<NB>(ss, red);
+        ok = stage_ll<NB, kH>(a.llx, B, a.tag + (uint32_t)a.L, xa, a.final_norm, red, nullptr, 0, 0, ctl);
         ok = cbar_and(ok);
     }
     if (ok) {
-        trace_mark(a, 1 + 2 * ph);
+        trace_mark(a, hslot);
         float inv[NB];
         read_inv<NB>(red, kH, a.eps, inv);
         constexpr int R = kHeadRows / kCW;
+        Cursor<NB> cur;
+#pragma unroll 1
         for (int r = sh.v_lo; r < sh.v_hi; r += kHeadRows) {
             const int rows = min(kHeadRows, sh.v_hi - r);
             int s;
             uint32_t par;
-            const unsigned char* item = next_item((uint32_t)rows * kH, s, par);
+            const unsigned char* item = cur.next((uint32_t)rows * kH, s, par);
             const int r0 = warp * R;
             const float sc = r0 + (lane & (R - 1)) < rows ? __ldg(a.sembed + r + r0 + (lane & (R - 1))) : 0.0f;
             if (r0 < rows && ok) {
-                ok = __all_sync(kAll, mbar_wait_ctl(&full[s], par, ctl));
+                ok = wait_item<NB>(s, par, ctl);
                 if (ok) {
                     float acc[R][NB];
                     dot_rows<NB, R, kH>(reinterpret_cast<const int8_t*>(item) + (size_t)r0 * kH, min(R, rows - r0), xa, B, acc);
@@ -1175,21 +1261,21 @@ __global__ void __launch_bounds__(kFT, 1) decode_flow_kernel(PersistentArgs a) {
                     }
                 }
             }
-            release(s);
+            release_item<NB>(s);
         }
     }
-    trace_mark(a, 2 + 2 * ph);
+    trace_mark(a, hslot + 1);
 #pragma unroll
     for (int b = 0; b < NB; ++b)
         if (lane == 0) bestv[warp * NB + b] = best[b];
     ok = cbar_and(ok);
     if (ok && tid < B) {
         unsigned long long m = 0ull;
+#pragma unroll 1
         for (int w = 0; w < kCW; ++w) m = bestv[w * NB + tid] > m ? bestv[w * NB + tid] : m;
         if (m) atomicMax(a.keys + tid, m);
     }
     ok = cbar_and(ok);
-    // the last CTA to finish turns keys into tokens and advances the rows
     if (ok && tid == 0) {
         __threadfence();
         const unsigned prev = atomicAdd(a.sync + 1, 1u);
@@ -1208,12 +1294,65 @@ __global__ void __launch_bounds__(kFT, 1) decode_flow_kernel(PersistentArgs a) {
             if (a.trace) {
                 uint64_t t;
                 asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-                a.trace[3 + 2 * ph] = t;
+                a.trace[hslot + 2] = t;
             }
             a.sync[1] = 0u;
             __threadfence();
         }
     }
+}
+
+// ------------------------------------------------------------ the kernel
+
+template <int NB>
+__global__ void __launch_bounds__(kFT, 1) decode_flow_kernel(const __grid_constant__ PersistentArgs a) {
+    using LY = Lay<NB>;
+    const int warp = threadIdx.x / kWarp;
+    const int max_len = a.max_blocks * kKvBlock;
+    int* pref = at<NB, int>(LY::pref);
+    if (threadIdx.x == 0) {
+        *at<NB, int>(LY::flag) = 0;
+        pref[0] = 0;
+        for (int b = 0; b < a.B; ++b) {
+            const int len = a.positions[b] + 1;
+            if ((len < 1 || len > max_len) && a.err) atomicOr(a.err, kErrBadIndex);
+            pref[b + 1] = pref[b] + (min(max(len, 1), max_len) + kKvBlock - 1) / kKvBlock;
+        }
+        Shares sh;
+        cta_share(kQKV, 1, sh.q_lo, sh.q_hi);
+        cta_share(kH, 1, sh.h_lo, sh.h_hi);
+        cta_share(kI, 1, sh.p_lo, sh.p_hi);
+        cta_share(a.V, 1, sh.v_lo, sh.v_hi);
+        sh.T = pref[a.B] * kNKV;
+        sh.a_lo = att_lo(blockIdx.x, sh.T);
+        sh.a_hi = att_lo(blockIdx.x + 1, sh.T);
+        *at<NB, Shares>(LY::shr) = sh;
+    }
+    if (threadIdx.x < kCW) at<NB, uint2>(LY::cur)[threadIdx.x] = make_uint2(0u, 0u);
+    if (threadIdx.x == kCT) {
+        for (int s = 0; s < kNF; ++s) {
+            mbar_init(full_bar<NB>(s), 1);
+            mbar_init(empty_bar<NB>(s), kCW);
+        }
+        fence_barrier_init();
+    }
+    trace_mark(a, 0);
+    __syncthreads();
+
+    if (warp == kCW) {
+        producer<NB>(a);
+        return;
+    }
+    bool ok = true;
+#pragma unroll 1
+    for (int l = 0; l < a.L && ok; ++l) {
+        ok = qkv_phase<NB>(a, l);
+        if (ok) ok = att_phase<NB>(a, l);
+        if (ok) ok = out_phase<NB, kQD>(a, l);
+        if (ok) ok = gu_phase<NB>(a, l);
+        if (ok) ok = out_phase<NB, kI>(a, l);
+    }
+    head_phase<NB>(a, ok);
 }
 
 template <int NB>
