@@ -167,10 +167,12 @@ ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, c
 ZYNFER_CU_API int zynfer_cu_set_linear_path(ZynferCuCtx *ctx, const char *path);
 /* Decode schedule for zynfer_cu_decode_step / zynfer_cu_generate: "kernels"
  * (one kernel per op, captured in a CUDA graph per batch size), "persistent"
- * (the whole step as one cooperative persistent kernel with grid barriers;
- * int8 models of hidden 1024, intermediate 3072, 16 x 128 query dims, batch
- * <= 8; ZYNFER_CU_UNSUPPORTED otherwise), or "auto" (= "kernels", measured
- * faster at every batch size). Both follow qwen_block.forward (qwen_block.zig:161-235) per layer
+ * (the whole step as one cooperative dataflow kernel: weights and KV blocks
+ * streamed into shared memory ahead of the layer chain, tagged activations
+ * instead of grid barriers; int8 models of hidden 1024, intermediate 3072,
+ * 16 x 128 query and 8 x 128 kv dims, at most 62 layers, batch <= 8;
+ * ZYNFER_CU_UNSUPPORTED otherwise), or "auto" (= "kernels", measured faster
+ * at every batch size). Both follow qwen_block.forward (qwen_block.zig:161-235) per layer
  * and qwen_forward's tied LM head + topK(1) (qwen_forward.zig:163-193). */
 ZYNFER_CU_API int zynfer_cu_set_decode_schedule(ZynferCuCtx *ctx, const char *schedule);
 /* Allocation-free int8 linear (no counterpart in the reference; an addition

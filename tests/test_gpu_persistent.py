@@ -1,10 +1,9 @@
-"""The single-kernel decode schedules against the oracle and against the
-multi-kernel schedule (B200 only): "persistent" (one cooperative kernel per
-step with grid barriers) and "flow" (one cooperative dataflow kernel per step:
-weights and KV blocks streamed into shared memory ahead of the layer chain,
-tagged activations instead of grid barriers). Every test runs for both.
+"""The persistent decode schedule against the oracle and against the
+multi-kernel schedule (B200 only): one cooperative dataflow kernel per step
+(weights and KV blocks streamed into shared memory ahead of the layer chain,
+tagged activations instead of grid barriers).
 
-Both kernels are built for Qwen3-0.6B widths (hidden 1024,
+The kernel is built for Qwen3-0.6B widths (hidden 1024,
 intermediate 3072, 16 x 128 query dims, 8 kv heads), so these tests use those
 widths with 2 layers and a 8192-token vocabulary, which keeps the oracle fast.
 Tolerances: BF16_KV (both sides keep a bf16 KV cache).
@@ -24,13 +23,13 @@ WIDE = dict(vocab=8192, hidden=1024, inter=3072, layers=2, n_q=16, n_kv=8, head_
 SEED, WSTD, NSTD = 5, 0.02, 0.1
 
 
-@pytest.fixture(scope="module", params=["persistent", "flow"])
-def sched(request):
-    return request.param
+@pytest.fixture(scope="module")
+def sched():
+    return "persistent"
 
 
 @pytest.fixture(scope="module")
-def gpu(sched):  # one context (and model) per schedule
+def gpu():
     g = zc.Gpu(0)
     yield g
     g.close()
@@ -151,14 +150,12 @@ def test_schedule_names_and_shape_limits(gpu, wide):
     zc.Model(g2, zc.Arch(**small), zc.W_Q8, max_batch=1, max_seqs=1, max_seq_len=64)
     with pytest.raises(zc.Unsupported):
         g2.set_decode_schedule("persistent")
-    with pytest.raises(zc.Unsupported):
-        g2.set_decode_schedule("flow")
     g2.set_decode_schedule("kernels")
     g2.close()
 
 
 def test_phase_trace_covers_every_phase(wide):
-    """With timing on, the single-kernel step records (start, end) of every phase
+    """With timing on, the persistent step records (start, end) of every phase
     as globaltimer ns: 4 + 10 L entries, each phase starting after the previous
     one ended, and the per-class totals of kernel_time add up to the step."""
     gpu = wide.gpu

@@ -137,10 +137,13 @@ struct AttnDecodeArgs {
 };
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st);
 
-// decode_persistent.cu: one decode step of 1..kPersistentMaxBatch rows as one
-// cooperative persistent kernel (int8 weights, hidden 1024, intermediate
-// 3072, 16 x 128 query dims).
+// decode_flow.cu: one decode step of 1..kPersistentMaxBatch rows as one
+// cooperative dataflow kernel (int8 weights, hidden 1024, intermediate 3072,
+// 16 x 128 query dims, 8 kv heads, at most kFlowMaxLayers layers): weights
+// and KV blocks streamed into a shared-memory ring by a producer warp, tagged
+// activations instead of grid barriers.
 constexpr int kPersistentMaxBatch = 8;
+constexpr int kFlowMaxLayers = 62;
 struct PersistentLayer {
     const int8_t *wqkv, *wo, *wgu, *wd;
     const float *sqkv, *so, *sgu, *sd;
@@ -158,7 +161,7 @@ struct PersistentArgs {
     uint16_t* kv;                   // pool base; layer l at l * kv_layer_elems
     size_t kv_layer_elems;
     const int* block_table;
-    int max_blocks, n_pool_blocks, max_segs;
+    int max_blocks, n_pool_blocks;
     uint32_t* tok;                  // [B] input ids, replaced by the argmax ids
     const int* seq_of;              // [B]
     int* positions;                 // [B], advanced by one
@@ -166,26 +169,18 @@ struct PersistentArgs {
     uint32_t* ids_out;              // [B]
     uint32_t* history;              // nullable [steps][B]
     int* step;
-    float *x, *x1, *qkv, *attn, *h, *partial;
     float* logits;                  // nullable [B][V]
-    unsigned* counters;             // [B][n_kv] attention merge counters, zero between launches
-    unsigned* sync;                 // [3]: barrier arrivals, finished CTAs, abort flag; zero between launches
+    unsigned* sync;                 // [3]: unused, finished CTAs, abort flag; zero between launches
     uint32_t* err;
     uint64_t* trace;                // nullable [4 + 10 L] globaltimer ns: start, then per phase (start, end) as
                                     // seen by CTA 0 (phases QKV, ATT, O, GU, D per layer, then HEAD), then finish
-    // dataflow kernel only: tagged activations (f32 value | 32-bit tag << 32)
+    // tagged activations (f32 value | 32-bit tag << 32)
     uint64_t *llx, *llx1;           // [kPersistentMaxBatch][H]
     uint64_t *llqkv, *llattn, *llh; // [..][qkv rows], [..][n_q d], [..][I]
     uint64_t* llrec;                // flow_record_words(ctas): cross-CTA attention records
     uint32_t tag;                   // this step's tag base: a multiple of 64, fresh per launch; layer l uses tag + l + 1
 };
 inline int persistent_trace_len(int layers) { return 4 + 10 * layers; }
-bool persistent_supported(int device);
-cudaError_t launch_decode_persistent(const PersistentArgs& a, cudaStream_t st);
-// decode_flow.cu: the same step as a dataflow kernel (weights and KV blocks
-// streamed into a shared-memory ring by a producer warp, tagged activations
-// instead of grid barriers); up to 62 layers.
-constexpr int kFlowMaxLayers = 62;
 void prepare_flow_kernels();
 bool flow_supported(int device);
 size_t flow_record_words(int ctas);

@@ -31,8 +31,8 @@ namespace {
 // tensor-core tcgen05 path, or the CUDA-core tiled GEMM (kept for A/B checks).
 enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3 };
 // Decode schedule: separate kernels per op (graph-captured; what auto takes),
-// or one persistent kernel per step for small int8 batches (on request).
-enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2, kSchedFlow = 3 };
+// or one persistent dataflow kernel per step for small int8 batches (on request).
+enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2 };
 constexpr int kGemvMaxRows = 4;  // op-level auto policy: GEMV up to this many rows, tcgen05 above
 constexpr int kGemvMaxM = 16384;  // model auto policy: largest matrix (output rows) for the batch-1 GEMV
 
@@ -131,10 +131,9 @@ struct ZynferCuCtx {
     size_t simt_xn_elems = 0;
     int path_policy = kPathAuto;
     int schedule = kSchedAuto;
-    bool persistent_ok = false;          // model shape and device allow the persistent decode kernel
+    bool persistent_ok = false;          // model shape and device allow the persistent (dataflow) decode kernel
     PersistentLayer* dlayers = nullptr;  // [layers] weight pointers for it
-    unsigned* psync = nullptr;           // [3] its grid-barrier / finish / abort words
-    bool flow_ok = false;                // ... and the dataflow decode kernel
+    unsigned* psync = nullptr;           // [3] its unused / finished-CTA / abort words
     uint64_t* ll = nullptr;              // its tagged activation buffers and attention records
     size_t ll_words = 0;
     uint32_t flow_step = 0;              // launches so far: tag base = 64 (1 + step % 2^25)
@@ -396,13 +395,11 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
 }
 
 // One decode step for the rows already staged in dtok/dseq/dpos.
-// "auto" takes the kernel graph: with the tcgen05 linears it measured faster
-// than the persistent kernel (whose linear phases run on CUDA cores) at every
-// batch size, batch 1 included.
+// "auto" takes the kernel graph: it measured faster than the persistent
+// dataflow kernel (whose linear phases run on CUDA cores) at every batch size,
+// batch 1 included.
 bool use_persistent(const ZynferCuCtx* c, int B) {
-    if (B > kPersistentMaxBatch) return false;
-    if (c->schedule == kSchedFlow) return c->flow_ok;
-    return c->persistent_ok && c->schedule == kSchedPersistent;
+    return B <= kPersistentMaxBatch && c->persistent_ok && c->schedule == kSchedPersistent;
 }
 
 void enqueue_decode_persistent(ZynferCuCtx* c, int B, bool want_logits) {
@@ -415,32 +412,26 @@ void enqueue_decode_persistent(ZynferCuCtx* c, int B, bool want_logits) {
     a.rope = c->rope; a.rope_max_pos = (int)m.max_seq_len;
     a.kv = c->kv; a.kv_layer_elems = c->kv_layer_elems;
     a.block_table = c->table_dev; a.max_blocks = c->max_blocks; a.n_pool_blocks = c->n_blocks;
-    a.max_segs = decode_max_segs(c->max_blocks);
     a.tok = c->dtok; a.seq_of = c->dseq; a.positions = c->dpos;
     a.keys = c->dkeys; a.ids_out = c->dids; a.history = c->dhist; a.step = c->dstep;
-    a.x = c->dx; a.x1 = c->dx1; a.qkv = c->dqkv; a.attn = c->dattn; a.h = c->dh; a.partial = c->dpart;
     a.logits = want_logits ? c->dlogits : nullptr;
-    a.counters = c->dcnt; a.sync = c->psync; a.err = c->derr;
+    a.sync = c->psync; a.err = c->derr;
     const int tl = persistent_trace_len((int)m.layers);
     if (c->timing && !c->ptrace && dalloc(c, &c->ptrace, (size_t)tl) != ZYNFER_CU_OK) c->ptrace = nullptr;
     a.trace = c->timing ? c->ptrace : nullptr;
-    if (c->schedule == kSchedFlow) {
-        const size_t act = (size_t)kPersistentMaxBatch;
-        a.llx = c->ll;
-        a.llx1 = a.llx + act * m.hidden;
-        a.llqkv = a.llx1 + act * m.hidden;
-        a.llattn = a.llqkv + act * c->qkv_rows;
-        a.llh = a.llattn + act * c->qd;
-        a.llrec = a.llh + act * m.inter;
-        // tags are unique per (launch, layer): 64 (1 + step) + layer + 1
-        a.tag = 64u * (1u + (c->flow_step++ % (1u << 25)));
-        launch_decode_flow(a, c->stream);
-    } else {
-        launch_decode_persistent(a, c->stream);
-    }
+    const size_t act = (size_t)kPersistentMaxBatch;
+    a.llx = c->ll;
+    a.llx1 = a.llx + act * m.hidden;
+    a.llqkv = a.llx1 + act * m.hidden;
+    a.llattn = a.llqkv + act * c->qkv_rows;
+    a.llh = a.llattn + act * c->qd;
+    a.llrec = a.llh + act * m.inter;
+    // tags are unique per (launch, layer): 64 (1 + step) + layer + 1
+    a.tag = 64u * (1u + (c->flow_step++ % (1u << 25)));
+    launch_decode_flow(a, c->stream);
     c->step_launches = 1;
     if (a.trace) {
-        // phase p lasts from its start to the next phase's start (its grid barrier included)
+        // phase p lasts from its start to the next phase's start (its input wait included)
         c->ptrace_host.resize(tl);
         if (cudaMemcpyAsync(c->ptrace_host.data(), c->ptrace, tl * 8, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
             cudaStreamSynchronize(c->stream) != cudaSuccess)
@@ -855,8 +846,11 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     }
     if (!make_tmap_k_major(&c->tm_embed, c->embed, c->wkind, H, V, 128))
         return fail(c, ZYNFER_CU_INTERNAL, "cuTensorMapEncodeTiled failed for the embedding");
-    // persistent decode kernel: weight pointers per layer and its sync words
-    c->persistent_ok = q8 && H == 1024 && I == 3072 && c->qd == 2048 && persistent_supported(c->device);
+    // persistent dataflow decode kernel: weight pointers per layer, its sync
+    // words, tagged activations [8][H] x2, [8][qkv], [8][qd], [8][I] and the
+    // cross-CTA attention records (zero tags are never valid)
+    c->persistent_ok = q8 && H == 1024 && I == 3072 && c->qd == 2048 && m.n_kv == 8 &&
+                       m.layers <= (uint32_t)kFlowMaxLayers && flow_supported(c->device);
     if (c->persistent_ok) {
         std::vector<PersistentLayer> pl(m.layers);
         for (uint32_t l = 0; l < m.layers; ++l) {
@@ -870,11 +864,6 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
                  "persistent layer table");
         if ((rc = dalloc(c, &c->psync, 3)) != ZYNFER_CU_OK) return rc;
         cudaMemset(c->psync, 0, 3 * sizeof(unsigned));
-    }
-    // dataflow decode kernel: tagged activations [8][H] x2, [8][qkv], [8][qd],
-    // [8][I] and the cross-CTA attention records (zero tags are never valid)
-    c->flow_ok = c->persistent_ok && m.layers <= (uint32_t)kFlowMaxLayers && m.n_kv == 8 && flow_supported(c->device);
-    if (c->flow_ok) {
         const int sms = c->caps.sm_count > 0 ? c->caps.sm_count : device_sm_count();
         c->ll_words = (size_t)kPersistentMaxBatch * (2 * H + c->qkv_rows + c->qd + I) + flow_record_words(sms);
         if ((rc = dalloc(c, &c->ll, c->ll_words)) != ZYNFER_CU_OK) return rc;
@@ -1140,8 +1129,7 @@ int zynfer_cu_decode_step(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* 
     cudaEventRecord(c->ev0, c->stream);
     if (eager) {
         enqueue_decode(c, (int)batch, logits != nullptr);
-        c->path = persistent ? (c->schedule == kSchedFlow ? "decode:flow" : "decode:persistent")
-                             : (batch <= 8 ? "decode:gemv:eager" : "decode:gemm:eager");
+        c->path = persistent ? "decode:persistent" : (batch <= 8 ? "decode:gemv:eager" : "decode:gemm:eager");
     } else {
         cudaGraphExec_t g;
         if ((rc = get_graph(c, (int)batch, &g))) return rc;
@@ -1202,7 +1190,7 @@ int zynfer_cu_generate(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* fir
     c->last_step_ns = (uint64_t)(ms * 1e6 / steps);
     ZC_CHECK(c, cudaMemcpy(out_ids, c->dhist, (size_t)steps * batch * 4, cudaMemcpyDeviceToHost), "history");
     for (uint32_t i = 0; i < batch; ++i) c->seq_len[seqs[i]] += steps;
-    c->path = persistent ? std::string(c->schedule == kSchedFlow ? "generate:flow" : "generate:persistent")
+    c->path = persistent ? std::string("generate:persistent")
                          : std::string(batch <= 8 ? "generate:gemv" : "generate:gemm") + (c->timing ? ":eager" : ":graph");
     return ZYNFER_CU_OK;
 }
@@ -1316,14 +1304,9 @@ int zynfer_cu_set_decode_schedule(ZynferCuCtx* c, const char* schedule) {
     else if (!strcmp(schedule, "persistent")) {
         if (c->ready && !c->persistent_ok)
             return fail(c, ZYNFER_CU_UNSUPPORTED, "the persistent decode kernel needs int8 weights, hidden 1024, "
-                                                  "intermediate 3072, 2048 query dims and cooperative launch");
-        c->schedule = kSchedPersistent;
-    } else if (!strcmp(schedule, "flow")) {
-        if (c->ready && !c->flow_ok)
-            return fail(c, ZYNFER_CU_UNSUPPORTED, "the dataflow decode kernel needs int8 weights, hidden 1024, "
                                                   "intermediate 3072, 16 x 128 query and 8 x 128 kv dims, at most "
                                                   "62 layers, 100+ SMs and cooperative launch");
-        c->schedule = kSchedFlow;
+        c->schedule = kSchedPersistent;
     } else {
         return fail(c, ZYNFER_CU_INVALID, std::string("unknown decode schedule ") + schedule);
     }

@@ -48,7 +48,6 @@ void prepare_all_kernels() {
     prepare_gemv_kernels();
     prepare_gemm_simt_kernels();
     prepare_attn_kernels();
-    prepare_persistent_kernels();
     prepare_flow_kernels();
     prepare_tc_kernels();
 }
