@@ -20,6 +20,29 @@ import time
 KV_BYTES_PER_TOKEN_HEAD = 2 * 128 * 2  # K and V rows, bf16
 
 
+def phase_breakdown(trace, layers: int) -> dict:
+    """Mean per-layer microseconds of each phase of the last persistent step,
+    as seen by CTA 0: "work" runs from the phase's start (its input staged)
+    to its end (its outputs written), "wait" from its end to the next
+    phase's start (the other CTAs' outputs arriving)."""
+    import numpy as np
+
+    t = trace.astype(np.int64)
+    P = 5 * layers + 1
+    if t.size < 4 + 10 * layers:
+        return {}
+    st, en = t[1:2 * P:2], t[2:2 * P + 1:2]
+    nxt = np.append(st[1:], t[3 + 2 * (P - 1)])
+    out = {}
+    for k, name in enumerate(("qkv", "attention", "o", "gate_up", "down")):
+        idx = np.arange(k, 5 * layers, 5)
+        out[name] = {"work": round(float(np.mean(en[idx] - st[idx])) / 1e3, 2),
+                     "wait": round(float(np.mean(nxt[idx] - en[idx])) / 1e3, 2)}
+    out["lm_head"] = {"work": round(float(en[-1] - st[-1]) / 1e3, 2),
+                      "finish": round(float(t[3 + 2 * (P - 1)] - en[-1]) / 1e3, 2)}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--seqs", type=int, default=64)
@@ -30,6 +53,8 @@ def main():
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--path", default="auto", help="linear kernel family (auto, gemv, tcgen05, simt)")
     ap.add_argument("--schedule", default="auto", help="decode schedule (auto, kernels, persistent)")
+    ap.add_argument("--phases", action="store_true",
+                    help="persistent schedule: add the per-phase breakdown of CTA 0's phase trace (mean over layers)")
     ap.add_argument("--window", default="decode", choices=["decode", "prefill"],
                     help="what runs between cudaProfilerStart/Stop: the timed decode steps, or one more prefill")
     ap.add_argument("--weights", default="q8", choices=["q8", "bf16"])
@@ -78,6 +103,7 @@ def main():
     model.generate(slots, nxt, args.steps)
     times = {name: gpu.kernel_time(cls) for name, cls in
              (("attention", zc.K_ATTN), ("linear", zc.K_LINEAR), ("lm_head", zc.K_LMHEAD), ("other", zc.K_OTHER))}
+    phases = phase_breakdown(gpu.phase_trace(), args.layers) if args.phases and args.schedule == "persistent" else None
     gpu.set_timing(False)
 
     kv_tok = sum(sum(c + 1 + s for c in ctx) for s in range(args.steps)) / args.steps
@@ -92,6 +118,8 @@ def main():
         "attn_bytes_per_launch": int(attn_bytes),
         "attn_gbs": round(attn_bytes / (ms_attn / max(1, n_attn) / 1e3) / 1e9, 1) if n_attn else None,
     }
+    if phases:
+        line["phases_us"] = phases
     print(json.dumps(line), flush=True)
     gpu.close()
 
