@@ -1,5 +1,5 @@
 // Pieces shared by the decode attention kernel (attn.cu) and the persistent
-// decode kernel (decode_persistent.cu): tensor-core fragment helpers and the
+// decode kernel (decode_flow.cu): tensor-core fragment helpers and the
 // end-of-share flush with its log-sum-exp merge (attentionInto,
 // src/backends/cpu/ops.zig:285-354, split over KV blocks).
 #pragma once
