@@ -223,31 +223,27 @@ struct Shares {
     int h_lo, h_hi;  // O / down rows (hidden)
     int p_lo, p_hi;  // gate/up pairs
     int v_lo, v_hi;  // LM head rows
-    int a_lo, a_hi;  // attention blocks (flattened)
-    int T;           // attention blocks in all
+    // attention: this CTA's piece, blocks [blk0, blk0 + nb) of (row b, kv
+    // head hd) whose cache holds nblk blocks; it is CTA k of the m CTAs
+    // first .. first + m - 1 that share that (row, head)
+    int b, hd, blk0, nb, nblk, k, m, first;
 };
 
-// Flattened attention blocks: f = n_kv pref[b] + head nblk(b) + blk.
-__device__ __forceinline__ void locate(const int* pref, int B, int f, int& b, int& head, int& blk, int& nblk) {
-    int l = 0, h = B - 1;
-    while (l < h) {
-        const int mid = (l + h + 1) / 2;
-        if (kNKV * pref[mid] <= f) l = mid;
-        else h = mid - 1;
-    }
-    b = l;
-    nblk = pref[l + 1] - pref[l];
-    const int r = f - kNKV * pref[l];
-    head = r / nblk;
-    blk = r % nblk;
+// Attention partition. The (row b, kv head) pairs s = b n_kv + head, in
+// order, own contiguous groups of CTAs [first(s), first(s + 1)), at least one
+// each, sized in proportion to their KV blocks (P = blocks before s, T = all
+// blocks, S = pairs, G = CTAs): first(s) = floor(P (G - S) / T) + s. CTA k of
+// a group of m takes blocks [k n / m, (k + 1) n / m) of its pair's n, so no
+// CTA holds blocks of two pairs and the group's last CTA holds the last block.
+__device__ __forceinline__ int group_first(const int* pref, int B, int s, int T) {
+    const int S = B * kNKV;
+    if (s >= S) return (int)gridDim.x;
+    const int b = s / kNKV, head = s % kNKV;
+    const unsigned long long P = (unsigned long long)kNKV * pref[b] + (unsigned long long)head * (pref[b + 1] - pref[b]);
+    return (int)(P * (gridDim.x - S) / (unsigned long long)T) + s;
 }
-// First flattened attention block of CTA c's range [att_lo(c), att_lo(c + 1)).
-__device__ __forceinline__ int att_lo(int c, int T) { return (int)((unsigned)c * (unsigned)T / gridDim.x); }
-// CTA whose attention range holds flattened block f (ranges may be empty
-// when there are fewer blocks than CTAs).
-__device__ __forceinline__ int cta_of(int f, int T) {
-    return (int)(((unsigned)(f + 1) * gridDim.x - 1u) / (unsigned)T);
-}
+// CTA k of a group of m over n blocks holds any (its range is not empty).
+__device__ __forceinline__ bool group_live(int k, int n, int m) { return (k + 1) * n / m > k * n / m; }
 
 __device__ __forceinline__ void trace_mark(const PersistentArgs& a, int slot) {
     if (a.trace && blockIdx.x == 0 && threadIdx.x == 0) {
@@ -356,7 +352,6 @@ template <int NB>
 __device__ __noinline__ void producer(const PersistentArgs& a) {
     constexpr int A = Lay<NB>::att_item;
     const Shares sh = *at<NB, Shares>(Lay<NB>::shr);
-    const int* pref = at<NB, int>(Lay<NB>::pref);
     const Ctl ctl = ctl_of<NB>(a);
     Prod p{0u, 0u, 0u, 0u, 1};
 #pragma unroll 1
@@ -365,14 +360,7 @@ __device__ __noinline__ void producer(const PersistentArgs& a) {
         const uint16_t* kv_layer = a.kv + (size_t)l * a.kv_layer_elems;
         prod_linear<NB>(p, P.wqkv + (size_t)sh.q_lo * kH, (uint32_t)(sh.q_hi - sh.q_lo) * kH, ctl);
 #pragma unroll 1
-        for (int f = sh.a_lo; f < sh.a_hi;) {
-            int b, hd, blk, nblk;
-            locate(pref, a.B, f, b, hd, blk, nblk);
-            const int e = min(sh.a_hi, f - blk + nblk);
-#pragma unroll 1
-            for (int i = 0; i < e - f; i += A) prod_att<NB>(p, a, kv_layer, b, hd, blk + i, min(A, e - f - i), ctl);
-            f = e;
-        }
+        for (int i = 0; i < sh.nb; i += A) prod_att<NB>(p, a, kv_layer, sh.b, sh.hd, sh.blk0 + i, min(A, sh.nb - i), ctl);
         prod_linear<NB>(p, P.wo + (size_t)sh.h_lo * kQD, (uint32_t)(sh.h_hi - sh.h_lo) * kQD, ctl);
         prod_linear<NB>(p, P.wgu + (size_t)2 * sh.p_lo * kH, (uint32_t)(2 * (sh.p_hi - sh.p_lo)) * kH, ctl);
         prod_linear<NB>(p, P.wd + (size_t)sh.h_lo * kI, (uint32_t)(sh.h_hi - sh.h_lo) * kI, ctl);
@@ -526,11 +514,25 @@ __device__ __forceinline__ void read_inv(const float* red, int K, float eps, flo
     }
 }
 
+// 16-byte loads from shared memory by 32-bit shared address (explicit
+// ld.shared, whatever the compiler can infer about the pointer it came from).
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
 // acc[r][b] = sum_k W[r][k] xs[b][k] for R int8 rows of K in shared memory
 // (row stride K), nrows of them real; every lane ends with the sums.
 template <int NB, int R, int K>
 __device__ __forceinline__ void dot_rows(const int8_t* w, int nrows, const float* xs, int B, float (&acc)[R][NB]) {
     const int lane = threadIdx.x % kWarp;
+    const uint32_t wa = smem_addr(w), xa = smem_addr(xs);
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -541,7 +543,7 @@ __device__ __forceinline__ void dot_rows(const int8_t* w, int nrows, const float
         uint4 wv[R];
 #pragma unroll
         for (int r = 0; r < R; ++r)
-            wv[r] = r < nrows ? *reinterpret_cast<const uint4*>(w + (size_t)r * K + k0) : make_uint4(0u, 0u, 0u, 0u);
+            wv[r] = r < nrows ? lds_u4(wa + (uint32_t)(r * K + k0)) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             float wf[R][4];
@@ -550,7 +552,7 @@ __device__ __forceinline__ void dot_rows(const int8_t* w, int nrows, const float
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
                 if (b >= B) break;
-                const float4 xv = *reinterpret_cast<const float4*>(xs + b * K + swz(k0 + 4 * q));
+                const float4 xv = lds_f4(xa + (uint32_t)(b * K + swz(k0 + 4 * q)) * 4u);
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
                     acc[r][b] = fmaf(wf[r][0], xv.x, acc[r][b]);
@@ -827,70 +829,112 @@ __device__ __forceinline__ void store_out_ll(uint64_t* out_row, int head, const 
 // ------------------------------------------------------------ cross-CTA merge
 
 // The cross-CTA merge of one (row, kv head): records 0 .. nrec - 1 (record k
-// from CTA first + k, none from CTAs whose attention range is empty) and
-// this CTA's own partial, folded in that order in the log-sum-exp sense,
-// then the normalised output of both query heads as tagged words. Consumer
-// thread t owns query head t / 128, dim t % 128; records are polled eight at
-// a time, all pending words re-read together.
-__device__ __noinline__ bool merge_across_ctas(const uint64_t* rec_bh, int nrec, int first, int T, const float* own,
-                                               uint64_t* out, uint32_t tag, Ctl ctl) {
-    const int tid = threadIdx.x;
-    const int hh = tid >> 7, d = tid & (kD - 1);
-    const uint64_t* rec0 = rec_bh + hh * kRecHead;
-    const bool all_live = T >= (int)gridDim.x;
-    float Mr = -INFINITY, Lr = 0.0f, Ar = 0.0f;
-    auto fold = [&](float m, float lsum, float av) {
-        if (m == -INFINITY) return;
-        if (m > Mr) {
-            const float cr = expf(Mr - m);
-            Lr *= cr;
-            Ar *= cr;
-            Mr = m;
-        }
-        const float ex = expf(m - Mr);
-        Lr = fmaf(lsum, ex, Lr);
-        Ar = fmaf(av, ex, Ar);
-    };
+// from CTA k of the group, none from CTAs of the group that hold no block) and
+// this CTA's own partial, combined in the log-sum-exp sense; the normalised
+// output of both query heads is published as tagged words. Warp w polls
+// records w, w + 8, w + 16 (every pending word of them re-read together, so
+// the poll ends one round trip after the last record lands) and folds them
+// in order; the warps' partials go to shared memory (slots 0..7 of `part`,
+// the own partial after them) and warp 0 merges them in warp order.
+// Called by all consumer warps; returns false on a timeout or abort.
+__device__ __noinline__ bool merge_across_ctas(const uint64_t* rec_bh, int nrec, int n, int m, const float* own,
+                                               float* part, uint64_t* out, uint32_t tag, Ctl ctl) {
+    constexpr int kPer = 3;  // records per warp and round
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+    float M[kG] = {-INFINITY, -INFINITY}, L[kG] = {0.0f, 0.0f};
+    float A[kG][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+    bool ok = true;
 #pragma unroll 1
-    for (int k0 = 0; k0 < nrec; k0 += 8) {
-        uint64_t wm[8], wl[8], wa[8];
-        uint32_t live = 0u;
-#pragma unroll 1
-        for (int u = 0; u < 8; ++u) {
-            const int c = first + k0 + u;
-            if (k0 + u < nrec && (all_live || att_lo(c, T) < att_lo(c + 1, T))) live |= 1u << u;
-        }
-        uint32_t pending = live;
+    for (int k0 = 0; k0 < nrec && ok; k0 += kPer * kCW) {
+        // words of record j: [h][m, l] and [h][acc 4 lane .. 4 lane + 3]
+        uint64_t w[kPer][kG][3][2];
+        uint32_t pending = 0u;
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if ((live >> u) & 1u) {
-                const uint64_t* r = rec0 + (size_t)(k0 + u) * kRecWords;
-                ll_ld2(r, wm[u], wl[u]);
-                wa[u] = ll_ld(r + 2 + d);
+        for (int j = 0; j < kPer; ++j) {
+            const int k = k0 + warp + kCW * j;
+            if (k < nrec && group_live(k, n, m)) pending |= 1u << j;
+        }
+        const uint32_t live = pending;
+        auto load = [&](int j) {
+            const uint64_t* r = rec_bh + (size_t)(k0 + warp + kCW * j) * kRecWords;
+#pragma unroll
+            for (int h = 0; h < kG; ++h) {
+                ll_ld2(r + h * kRecHead, w[j][h][0][0], w[j][h][0][1]);
+                ll_ld2(r + h * kRecHead + 2 + 4 * lane, w[j][h][1][0], w[j][h][1][1]);
+                ll_ld2(r + h * kRecHead + 4 + 4 * lane, w[j][h][2][0], w[j][h][2][1]);
             }
+        };
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+            if ((live >> j) & 1u) load(j);
         uint32_t spins = 0;
 #pragma unroll 1
         while (true) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (((pending >> u) & 1u) && ll_ok(wm[u], tag) && ll_ok(wl[u], tag) && ll_ok(wa[u], tag))
-                    pending &= ~(1u << u);
+            for (int j = 0; j < kPer; ++j) {
+                if (!((pending >> j) & 1u)) continue;
+                bool ready = true;
+#pragma unroll
+                for (int h = 0; h < kG; ++h)
+#pragma unroll
+                    for (int q = 0; q < 3; ++q) ready = ready && ll_ok(w[j][h][q][0], tag) && ll_ok(w[j][h][q][1], tag);
+                if (ready) pending &= ~(1u << j);
+            }
             if (!pending) break;
-            if (!keep_waiting(spins, ctl)) return false;
+            if (!keep_waiting(spins, ctl)) {
+                ok = false;
+                break;
+            }
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if ((pending >> u) & 1u) {
-                    const uint64_t* r = rec0 + (size_t)(k0 + u) * kRecWords;
-                    ll_ld2(r, wm[u], wl[u]);
-                    wa[u] = ll_ld(r + 2 + d);
-                }
+            for (int j = 0; j < kPer; ++j)
+                if ((pending >> j) & 1u) load(j);
         }
+        if (!ok) break;
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if ((live >> u) & 1u) fold(ll_val(wm[u]), ll_val(wl[u]), ll_val(wa[u]));
+        for (int j = 0; j < kPer; ++j) {
+            if (!((live >> j) & 1u)) continue;
+#pragma unroll
+            for (int h = 0; h < kG; ++h) {
+                const float m = ll_val(w[j][h][0][0]), lsum = ll_val(w[j][h][0][1]);
+                if (m == -INFINITY) continue;
+                if (m > M[h]) {
+                    const float cr = expf(M[h] - m);
+                    L[h] *= cr;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) A[h][e] *= cr;
+                    M[h] = m;
+                }
+                const float ex = expf(m - M[h]);
+                L[h] = fmaf(lsum, ex, L[h]);
+                A[h][0] = fmaf(ll_val(w[j][h][1][0]), ex, A[h][0]);
+                A[h][1] = fmaf(ll_val(w[j][h][1][1]), ex, A[h][1]);
+                A[h][2] = fmaf(ll_val(w[j][h][2][0]), ex, A[h][2]);
+                A[h][3] = fmaf(ll_val(w[j][h][2][1]), ex, A[h][3]);
+            }
+        }
     }
-    fold(own[hh * kPartHead], own[hh * kPartHead + 1], own[hh * kPartHead + 4 + d]);
-    ll_st(out + (size_t)hh * kD + d, Ar * (1.0f / Lr), tag);
+    // warp partial -> slot `warp` ([h][m, l, -, -, acc[128]]); the own
+    // partial -> slot kCW
+    float* rec = part + (size_t)warp * kPartStride;
+#pragma unroll
+    for (int h = 0; h < kG; ++h) {
+        if (lane == 0) {
+            rec[h * kPartHead] = M[h];
+            rec[h * kPartHead + 1] = L[h];
+        }
+        *reinterpret_cast<float4*>(rec + h * kPartHead + 4 + 4 * lane) = make_float4(A[h][0], A[h][1], A[h][2], A[h][3]);
+    }
+    if (warp == 0) {
+        float* o = part + (size_t)kCW * kPartStride;
+        for (int i = lane; i < kPartStride; i += kWarp) o[i] = own[i];
+    }
+    if (!cbar_and(ok)) return false;
+    if (warp == 0) {
+        float Mm[kG], Lm[kG];
+        float4 A0, A1;
+        attn::merge_records<false, 8>(part, kCW + 1, Mm, Lm, A0, A1);
+        store_out_ll(out, 0, Lm, A0, A1, tag);
+    }
     return true;
 }
 
@@ -990,8 +1034,10 @@ __device__ __noinline__ bool qkv_phase(const PersistentArgs& a, int l) {
     return cbar_and(ok);  // scl and xa are rewritten by the next phases
 }
 
-// ATT: this CTA's range of KV blocks, piece by piece (one piece per
-// (row, kv head) it overlaps); see the file comment.
+// ATT: this CTA's piece of one (row, kv head): its KV blocks, one per warp
+// per ring item, merged in shared memory, then either published (the CTA
+// holds the whole row), written as a record, or merged with the group's
+// records (the group's last CTA); see the file comment.
 template <int NB>
 __device__ __noinline__ bool att_phase(const PersistentArgs& a, int l) {
     using LY = Lay<NB>;
@@ -1000,9 +1046,8 @@ __device__ __noinline__ bool att_phase(const PersistentArgs& a, int l) {
     const PersistentLayer& P = a.layers[l];
     const uint32_t tag = a.tag + (uint32_t)l + 1u;
     const Ctl ctl = ctl_of<NB>(a);
-    const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp, B = a.B;
+    const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     const int max_len = a.max_blocks * kKvBlock;
-    const int* pref = at<NB, int>(LY::pref);
     float* part = at<NB, float>(LY::part);
     float* own = at<NB, float>(LY::own);
     float* qb = at<NB, float>(LY::qb) + warp * kG * kD;
@@ -1011,16 +1056,9 @@ __device__ __noinline__ bool att_phase(const PersistentArgs& a, int l) {
     trace_mark(a, 3 + 10 * l);
     Cursor<NB> cur;
     bool ok = true;
-    int par_buf = 0;
-    int m_b = -1, m_head = 0, m_nrec = 0, m_first = 0;
-#pragma unroll 1
-    for (int f = sh.a_lo; f < sh.a_hi;) {
-        int b, hd, blk0, nblk;
-        locate(pref, B, f, b, hd, blk0, nblk);
-        const int F0 = f - blk0;
-        const int e = min(sh.a_hi, F0 + nblk);
-        const int nb = e - f;
-        const bool starts = f == F0, ends = e == F0 + nblk;
+    if (sh.nb > 0) {
+        const int b = sh.b, hd = sh.hd, blk0 = sh.blk0, nb = sh.nb, nblk = sh.nblk;
+        const bool starts = blk0 == 0, ends = blk0 + nb == nblk;
         const int pos = a.positions[b];
         const int kv_len = min(max(pos + 1, 1), max_len);
         // this warp's blocks of the piece: i = warp, warp + kCW, ...
@@ -1069,40 +1107,30 @@ __device__ __noinline__ bool att_phase(const PersistentArgs& a, int l) {
             }
             release_item<NB>(s);
         }
-        float* pbuf = part + (size_t)par_buf * kCW * kPartStride;
-        if (have && ok) warp_partial(acc, l_run, m_run, pbuf + warp * kPartStride);
-        if (!(ok = cbar_and(ok))) break;
-        if (warp == 0) {
+        if (have && ok) warp_partial(acc, l_run, m_run, part + warp * kPartStride);
+        ok = cbar_and(ok);
+        if (ok && warp == 0) {
             float M[kG], L[kG];
             float4 A0, A1;
-            attn::merge_records<false, 8>(pbuf, min(nb, kCW), M, L, A0, A1);
+            attn::merge_records<false, 8>(part, min(nb, kCW), M, L, A0, A1);
             if (starts && ends) {
                 store_out_ll(a.llattn + (size_t)b * kQD, hd, L, A0, A1, tag);
             } else if (ends) {
                 attn::merged_store_record(M, L, A0, A1, own);
             } else {
-                const int k = (int)blockIdx.x - cta_of(F0, sh.T);
-                store_record_ll(a.llrec + (((size_t)b * kNKV + hd) * gridDim.x + k) * kRecWords, M, L, A0, A1, tag);
+                store_record_ll(a.llrec + (((size_t)b * kNKV + hd) * gridDim.x + sh.k) * kRecWords, M, L, A0, A1, tag);
             }
         }
-        if (!starts && ends) {
-            m_b = b;
-            m_head = hd;
-            m_first = cta_of(F0, sh.T);
-            m_nrec = (int)blockIdx.x - m_first;
+        if (ok && !starts && ends) {
+            // the group's last CTA merges the records of the CTAs before it
+            // with its own and publishes the output
+            ok = cbar_and(ok);  // warp 0 has written `own`
+            if (ok)
+                ok = merge_across_ctas(a.llrec + ((size_t)b * kNKV + hd) * gridDim.x * kRecWords, sh.k, nblk, sh.m,
+                                       own, part, a.llattn + (size_t)b * kQD + (size_t)hd * kG * kD, tag, ctl);
         }
-        par_buf ^= 1;
-        f = e;
     }
     cur.save();
-    if (ok && m_b >= 0) {
-        // the CTA holding a row's last block merges the records of the CTAs
-        // before it (in CTA order) with its own and publishes the output
-        ok = cbar_and(ok);
-        if (ok)
-            ok = merge_across_ctas(a.llrec + ((size_t)m_b * kNKV + m_head) * gridDim.x * kRecWords, m_nrec, m_first,
-                                   sh.T, own, a.llattn + (size_t)m_b * kQD + (size_t)m_head * kG * kD, tag, ctl);
-    }
     trace_mark(a, 4 + 10 * l);
     return cbar_and(ok);
 }
@@ -1323,9 +1351,22 @@ __global__ void __launch_bounds__(kFT, 1) decode_flow_kernel(const __grid_consta
         cta_share(kH, 1, sh.h_lo, sh.h_hi);
         cta_share(kI, 1, sh.p_lo, sh.p_hi);
         cta_share(a.V, 1, sh.v_lo, sh.v_hi);
-        sh.T = pref[a.B] * kNKV;
-        sh.a_lo = att_lo(blockIdx.x, sh.T);
-        sh.a_hi = att_lo(blockIdx.x + 1, sh.T);
+        // this CTA's attention piece: its (row, kv head) group and share
+        const int T = pref[a.B] * kNKV, S = a.B * kNKV, c = (int)blockIdx.x;
+        int lo = 0, hi = S - 1;  // the last pair whose group starts at or before c
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) / 2;
+            if (group_first(pref, a.B, mid, T) <= c) lo = mid;
+            else hi = mid - 1;
+        }
+        sh.first = group_first(pref, a.B, lo, T);
+        sh.m = group_first(pref, a.B, lo + 1, T) - sh.first;
+        sh.k = c - sh.first;
+        sh.b = lo / kNKV;
+        sh.hd = lo % kNKV;
+        sh.nblk = pref[sh.b + 1] - pref[sh.b];
+        sh.blk0 = sh.k * sh.nblk / sh.m;
+        sh.nb = (sh.k + 1) * sh.nblk / sh.m - sh.blk0;
         *at<NB, Shares>(LY::shr) = sh;
     }
     if (threadIdx.x < kCW) at<NB, uint2>(LY::cur)[threadIdx.x] = make_uint2(0u, 0u);
