@@ -799,34 +799,28 @@ __device__ __forceinline__ void warp_partial(float (&acc)[16][2], float l_run, f
         *reinterpret_cast<float2*>(pg + 4 + nt * 8 + 2 * t) = make_float2(acc[nt][0], acc[nt][1]);
 }
 
-// A merged (m, l, acc) of both query heads in the lane layout of
-// attn::merge_records (lane owns dims 4 lane .. 4 lane + 3) as a tagged
-// record or as the normalised output of (row b, kv head).
-__device__ __forceinline__ void store_record_ll(uint64_t* rec, const float (&M)[kG], const float (&L)[kG],
-                                                const float4& A0, const float4& A1, uint32_t tag) {
-    const int lane = threadIdx.x % kWarp;
-    if (lane == 0) {
-        ll_st(rec + 0, M[0], tag);
-        ll_st(rec + 1, L[0], tag);
-        ll_st(rec + kRecHead, M[1], tag);
-        ll_st(rec + kRecHead + 1, L[1], tag);
-    }
-    uint64_t* a0 = rec + 2 + 4 * lane;
-    uint64_t* a1 = rec + kRecHead + 2 + 4 * lane;
-    ll_st(a0 + 0, A0.x, tag); ll_st(a0 + 1, A0.y, tag); ll_st(a0 + 2, A0.z, tag); ll_st(a0 + 3, A0.w, tag);
-    ll_st(a1 + 0, A1.x, tag); ll_st(a1 + 1, A1.y, tag); ll_st(a1 + 2, A1.z, tag); ll_st(a1 + 3, A1.w, tag);
-}
-__device__ __forceinline__ void store_out_ll(uint64_t* out_row, int head, const float (&L)[kG], const float4& A0,
-                                             const float4& A1, uint32_t tag) {
-    const int lane = threadIdx.x % kWarp;
-    const float i0 = 1.0f / L[0], i1 = 1.0f / L[1];
-    uint64_t* o0 = out_row + (size_t)head * kG * kD + 4 * lane;
-    uint64_t* o1 = o0 + kD;
-    ll_st(o0 + 0, A0.x * i0, tag); ll_st(o0 + 1, A0.y * i0, tag); ll_st(o0 + 2, A0.z * i0, tag); ll_st(o0 + 3, A0.w * i0, tag);
-    ll_st(o1 + 0, A1.x * i1, tag); ll_st(o1 + 1, A1.y * i1, tag); ll_st(o1 + 2, A1.z * i1, tag); ll_st(o1 + 3, A1.w * i1, tag);
-}
-
 // ------------------------------------------------------------ cross-CTA merge
+
+// Merge of `count` shared-memory partials (slots base + j kPartStride, [h][m,
+// l, -, -, acc[128]]) in the log-sum-exp sense by all consumer threads at once:
+// thread t owns query head t / 128, dim t % 128. Returns that thread's
+// (M, L, A); the slot order fixes the result.
+__device__ __forceinline__ void merge_slots(const float* base, int count, float& M, float& L, float& A) {
+    const int hh = threadIdx.x >> 7, d = threadIdx.x & (kD - 1);
+    const float* b = base + hh * kPartHead;
+    M = -INFINITY;
+#pragma unroll 1
+    for (int j = 0; j < count; ++j) M = fmaxf(M, b[j * kPartStride]);
+    L = 0.0f;
+    A = 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < count; ++j) {
+        const float m = b[j * kPartStride];
+        const float c = m == -INFINITY ? 0.0f : expf(m - M);
+        L = fmaf(b[j * kPartStride + 1], c, L);
+        A = fmaf(b[j * kPartStride + 4 + d], c, A);
+    }
+}
 
 // The cross-CTA merge of one (row, kv head): records 0 .. nrec - 1 (record k
 // from CTA k of the group, none from CTAs of the group that hold no block) and
@@ -929,12 +923,9 @@ __device__ __noinline__ bool merge_across_ctas(const uint64_t* rec_bh, int nrec,
         for (int i = lane; i < kPartStride; i += kWarp) o[i] = own[i];
     }
     if (!cbar_and(ok)) return false;
-    if (warp == 0) {
-        float Mm[kG], Lm[kG];
-        float4 A0, A1;
-        attn::merge_records<false, 8>(part, kCW + 1, Mm, Lm, A0, A1);
-        store_out_ll(out, 0, Lm, A0, A1, tag);
-    }
+    float Mm, Lm, Am;
+    merge_slots(part, kCW + 1, Mm, Lm, Am);
+    ll_st(out + threadIdx.x, Am * (1.0f / Lm), tag);  // thread t: head t / 128, dim t % 128
     return true;
 }
 
@@ -1109,22 +1100,33 @@ __device__ __noinline__ bool att_phase(const PersistentArgs& a, int l) {
         }
         if (have && ok) warp_partial(acc, l_run, m_run, part + warp * kPartStride);
         ok = cbar_and(ok);
-        if (ok && warp == 0) {
-            float M[kG], L[kG];
-            float4 A0, A1;
-            attn::merge_records<false, 8>(part, min(nb, kCW), M, L, A0, A1);
+        if (ok) {
+            // the warps' partials merged by all threads, thread t owning
+            // (query head t / 128, dim t % 128)
+            float M, L, Av;
+            merge_slots(part, min(nb, kCW), M, L, Av);
+            const int hh = threadIdx.x >> 7, d = threadIdx.x & (kD - 1);
             if (starts && ends) {
-                store_out_ll(a.llattn + (size_t)b * kQD, hd, L, A0, A1, tag);
+                ll_st(a.llattn + (size_t)b * kQD + (size_t)(hd * kG + hh) * kD + d, Av * (1.0f / L), tag);
             } else if (ends) {
-                attn::merged_store_record(M, L, A0, A1, own);
+                if (d == 0) {
+                    own[hh * kPartHead] = M;
+                    own[hh * kPartHead + 1] = L;
+                }
+                own[hh * kPartHead + 4 + d] = Av;
             } else {
-                store_record_ll(a.llrec + (((size_t)b * kNKV + hd) * gridDim.x + sh.k) * kRecWords, M, L, A0, A1, tag);
+                uint64_t* rec = a.llrec + (((size_t)b * kNKV + hd) * gridDim.x + sh.k) * kRecWords + hh * kRecHead;
+                if (d == 0) {
+                    ll_st(rec, M, tag);
+                    ll_st(rec + 1, L, tag);
+                }
+                ll_st(rec + 2 + d, Av, tag);
             }
         }
         if (ok && !starts && ends) {
             // the group's last CTA merges the records of the CTAs before it
             // with its own and publishes the output
-            ok = cbar_and(ok);  // warp 0 has written `own`
+            ok = cbar_and(ok);  // `own` is written
             if (ok)
                 ok = merge_across_ctas(a.llrec + ((size_t)b * kNKV + hd) * gridDim.x * kRecWords, sh.k, nblk, sh.m,
                                        own, part, a.llattn + (size_t)b * kQD + (size_t)hd * kG * kD, tag, ctl);
