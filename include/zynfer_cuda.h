@@ -27,8 +27,12 @@
  * Fault injection (host side, for tests of the error paths): the environment
  * variable ZYNFER_CUDA_FAIL_AT, or zynfer_cu_set_fail_at, takes
  * "alloc:N" (the N-th device allocation after the call fails with OOM),
- * "upload" (the next weight upload fails with INTERNAL) or "launch" (the next
- * call that would launch kernels fails with LAUNCH before launching any).
+ * "upload" (the next weight upload fails with INTERNAL), "launch" (the next
+ * call that would launch kernels fails with LAUNCH before launching any) or
+ * "wait" (the next "persistent" decode step of a model with two or more
+ * layers polls one input with a tag that nothing writes: its bounded device
+ * wait runs out after a few seconds, every CTA stops, and the call returns
+ * TIMEOUT with the context still usable).
  */
 #ifndef ZYNFER_CUDA_H
 #define ZYNFER_CUDA_H

@@ -115,6 +115,26 @@ def test_long_context_rows_match_oracle(wide, oracle_wide):
             check_logits(sessions[r].forward([toks[r]]), logits[r], f"long row {r} step {step}")
 
 
+def test_device_wait_timeout_is_reported(wide, oracle_wide):
+    """A device wait that runs out ends the step with DeviceTimeout and leaves
+    the context usable. Injected on the host (ZYNFER_CUDA_FAIL_AT=wait): one
+    layer input is polled with a tag that nothing writes, so the kernel's
+    bounded wait gives up, every CTA stops through the abort flag, and no
+    fault or hang is involved. The next step of the same sequence then
+    matches the oracle (the failed step advanced nothing)."""
+    ids = O.synth_tokens(30, SEED, 41, WIDE["vocab"])
+    wide.prefill(9, ids, want_logits=False)
+    s = oracle_wide.session(64)
+    s.forward(ids, want_logits=False)
+    wide.gpu.set_fail_at("wait")
+    with pytest.raises(zc.DeviceTimeout):
+        wide.decode_step([9], [7])
+    assert wide.seq_len(9) == 30
+    am, logits = wide.decode_step([9], [7], want_logits=True)
+    check_logits(s.forward([7]), logits[0], "step after the timeout")
+    assert int(am[0]) == int(np.argmax(logits[0]))
+
+
 def test_generate_equals_stepwise(wide, sched):
     ids = O.synth_tokens(40, SEED, 21, WIDE["vocab"])
     wide.prefill(10, ids, want_logits=False)

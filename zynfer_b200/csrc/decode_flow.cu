@@ -991,8 +991,9 @@ __device__ __noinline__ bool qkv_phase(const PersistentArgs& a, int l) {
     bool ok = true;
     if (l == 0)
         stage_embed<NB>(a.tok, B, a.V, a.embed, a.sembed, a.err, xa, P.input_ln, red, res0, sh.h_lo, sh.h_hi);
-    else
-        ok = stage_ll<NB, kH>(a.llx, B, tag - 1u, xa, P.input_ln, red, res0, sh.h_lo, sh.h_hi, ctl);
+    else  // (an injected stall polls a tag that nothing writes, so the bounded wait runs out)
+        ok = stage_ll<NB, kH>(a.llx, B, l == a.stall_layer ? (tag - 1u) ^ 0x80000000u : tag - 1u, xa, P.input_ln, red,
+                              res0, sh.h_lo, sh.h_hi, ctl);
     if (!cbar_and(ok)) return false;
     trace_mark(a, 1 + 10 * l);
     float inv[NB];

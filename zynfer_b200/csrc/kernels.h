@@ -179,6 +179,8 @@ struct PersistentArgs {
     uint64_t *llqkv, *llattn, *llh; // [..][qkv rows], [..][n_q d], [..][I]
     uint64_t* llrec;                // flow_record_words(ctas): cross-CTA attention records
     uint32_t tag;                   // this step's tag base: a multiple of 64, fresh per launch; layer l uses tag + l + 1
+    int stall_layer;                // fault injection: when l >= 1, layer l's QKV input is polled with a tag that
+                                    // nothing writes, so its bounded wait runs out (-1: off)
 };
 inline int persistent_trace_len(int layers) { return 4 + 10 * layers; }
 void prepare_flow_kernels();

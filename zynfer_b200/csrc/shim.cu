@@ -72,6 +72,7 @@ struct ZynferCuCtx {
     long alloc_count = 0;
     bool fail_upload = false;
     bool fail_launch = false;
+    bool fail_wait = false;  // the next persistent decode step stalls on a device wait
     std::vector<void*> allocs;
     std::vector<void*> pinned;
 
@@ -212,6 +213,8 @@ void parse_fail_spec(ZynferCuCtx* c, const char* spec) {
         c->fail_upload = true;
     } else if (strcmp(spec, "launch") == 0) {
         c->fail_launch = true;
+    } else if (strcmp(spec, "wait") == 0) {
+        c->fail_wait = true;
     }
 }
 
@@ -428,6 +431,11 @@ void enqueue_decode_persistent(ZynferCuCtx* c, int B, bool want_logits) {
     a.llrec = a.llh + act * m.inter;
     // tags are unique per (launch, layer): 64 (1 + step) + layer + 1
     a.tag = 64u * (1u + (c->flow_step++ % (1u << 25)));
+    a.stall_layer = -1;
+    if (c->fail_wait && m.layers >= 2) {
+        c->fail_wait = false;
+        a.stall_layer = 1;
+    }
     launch_decode_flow(a, c->stream);
     c->step_launches = 1;
     if (a.trace) {
