@@ -78,28 +78,46 @@ struct QkvSource {
 // holds the row's last block (has_last), this step's key (RMSNorm(k_norm) +
 // RoPE) and value, rounded to bf16, go to kvnew[0..127] / kvnew[128..255].
 // Every load is issued before any is used. qb: 2 x 128 f32 of shared memory.
-__device__ __forceinline__ void share_setup(const QkvSource& src, int b, int head, int pos, bool has_last, float* qb,
-                                            uint16_t* kvnew, uint32_t (&qf)[8][2]) {
+// The norm weights and the RoPE row of pos (ShareAux) come from buffers no
+// kernel of the step writes, so they may be loaded before griddepcontrol.wait.
+struct ShareAux {
+    float qn[4], kn[4];
+    float2 c2[2];
+    bool rope_ok;
+};
+__device__ __forceinline__ ShareAux share_aux(const QkvSource& src, int pos) {
+    const int lane = threadIdx.x % kWarp;
+    ShareAux x;
+    x.rope_ok = pos >= 0 && pos < src.rope_max_pos;
+    const float2* cs = src.rope + (size_t)(x.rope_ok ? pos : 0) * (kD / 2);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        x.qn[j] = __ldg(src.q_norm + lane + 32 * j);
+        x.kn[j] = __ldg(src.k_norm + lane + 32 * j);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) x.c2[j] = __ldg(cs + lane + 32 * j);
+    return x;
+}
+__device__ __forceinline__ void share_setup(const QkvSource& src, const ShareAux& aux, int b, int head,
+                                            bool has_last, float* qb, uint16_t* kvnew, uint32_t (&qf)[8][2]) {
     const int lane = threadIdx.x % kWarp;
     const int g = lane >> 2, t = lane & 3;
     const float* qsrc = src.qkv + (size_t)b * src.qkv_rows + (size_t)(head * kG) * kD;
     const float* ksrc = src.qkv + (size_t)b * src.qkv_rows + src.qd + (size_t)head * kD;
     const float* vsrc = ksrc + (size_t)src.n_kv * kD;
-    const bool rope_ok = pos >= 0 && pos < src.rope_max_pos;
-    const float2* cs = src.rope + (size_t)(rope_ok ? pos : 0) * (kD / 2);
-    float qv[kG][4], qn[4], kr[4], vr[4], kn[4];
-    float2 c2[2];
+    const bool rope_ok = aux.rope_ok;
+    const float(&qn)[4] = aux.qn;
+    const float(&kn)[4] = aux.kn;
+    const float2(&c2)[2] = aux.c2;
+    float qv[kG][4], kr[4], vr[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
 #pragma unroll
         for (int hh = 0; hh < kG; ++hh) qv[hh][j] = __ldcg(qsrc + hh * kD + lane + 32 * j);
-        qn[j] = __ldg(src.q_norm + lane + 32 * j);
         kr[j] = has_last ? __ldcg(ksrc + lane + 32 * j) : 0.0f;
         vr[j] = has_last ? __ldcg(vsrc + lane + 32 * j) : 0.0f;
-        kn[j] = has_last ? __ldg(src.k_norm + lane + 32 * j) : 0.0f;
     }
-#pragma unroll
-    for (int j = 0; j < 2; ++j) c2[j] = __ldg(cs + lane + 32 * j);
     auto norm_rope = [&](float (&v)[4], const float (&w)[4]) {
         float ss = 0.0f;
 #pragma unroll

@@ -109,10 +109,14 @@ void launch_gemm_simt(const LinearArgs& a, cudaStream_t st);
 
 // attn.cu
 // Decode attention splits each (row, kv head) into warp shares of >=
-// kMinBlocksPerWarp blocks; at most decode_max_segs(max_blocks) records of
-// one (row, kv head) reach global memory.
+// kMinBlocksPerWarp blocks and a CTA's (at least 4) warps hold consecutive
+// shares, so a (row, kv head) meets at most max_blocks / (4 kMinBlocksPerWarp)
+// + 2 CTAs: that many records of one (row, kv head) reach global memory.
+// Two blocks per warp keeps a one-row step on about half the SMs, so the next
+// projection's CTAs start on the others under programmatic dependent launch
+// (one block per warp measured 1.03 against 0.95 ms per token).
 constexpr int kMinBlocksPerWarp = 2;
-inline int decode_max_segs(int max_blocks) { return max_blocks / kMinBlocksPerWarp + 2; }
+inline int decode_max_segs(int max_blocks) { return max_blocks / (4 * kMinBlocksPerWarp) + 2; }
 struct AttnDecodeArgs {
     // this step's q, k, v: the raw fused-QKV output [B][(n_q + 2 n_kv) d]; the
     // kernel applies the per-head RMSNorm + RoPE and appends K/V to the cache
