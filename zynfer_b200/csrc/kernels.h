@@ -114,7 +114,8 @@ void launch_gemm_simt(const LinearArgs& a, cudaStream_t st);
 // + 2 CTAs: that many records of one (row, kv head) reach global memory.
 // Two blocks per warp keeps a one-row step on about half the SMs, so the next
 // projection's CTAs start on the others under programmatic dependent launch
-// (one block per warp measured 1.03 against 0.95 ms per token).
+// (one block per warp measured 1.03 against 0.95 ms per token; three or four
+// were no faster for one row and 1-4 % slower for two).
 constexpr int kMinBlocksPerWarp = 2;
 inline int decode_max_segs(int max_blocks) { return max_blocks / (4 * kMinBlocksPerWarp) + 2; }
 struct AttnDecodeArgs {
