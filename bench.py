@@ -20,6 +20,16 @@ device->host argmax inside the timed region). `roofline` comes from CUDA
 events around every attention launch in an instrumented pass of the same
 steps right after the timed region. `cpu_baseline` times the oracle
 (the CPU restatement of the reference path) on a bounded sample.
+
+    python bench.py --sweep gemv [--sweep-calls C] [--sweep-shape MxK]
+
+prints one JSON line per case of the int8 linear sweep instead: matvecQ8 /
+matmulQ8 (ops.zig:181-228) shapes 3072x1024 (QKV as 2048+512+512),
+4096x1024 (the model's QKV, 2048+1024+1024), 1024x2048, 6144x1024, 1024x3072
+and 151936x1024 at 1 and 8 activation rows, through zynfer_cu_linear with
+device pointers. Each call reads another of R weight copies (R x m x k above
+twice the L2), CUDA events around every call on the library's stream give
+its time, and achieved GB/s = (m k + 4 m + 4 B k + 4 B m) / time.
 """
 from __future__ import annotations
 
@@ -42,9 +52,9 @@ SEED = 20250601
 KV_BYTES_PER_TOKEN_LAYER = 2 * 8 * 128 * 2  # K + V, 8 kv heads, d = 128, bf16
 # DRAM bytes (read + write) per algorithmic byte of attn_decode_kernel, from one
 # ncu capture of 32 sequences at context 2048 (profiles/attn_decode_b32_ctx2048.txt:
-# 275.4 MB for 269.3 MB); the traffic grows with the KV bytes, so a launch of this
+# 275.1 MB for 269.3 MB); the traffic grows with the KV bytes, so a launch of this
 # workload moves about this ratio times its algorithmic bytes.
-ATTN_TRAFFIC_RATIO = 275.43 / 269.3
+ATTN_TRAFFIC_RATIO = 275.06 / 269.3
 
 
 def parse():
@@ -56,6 +66,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=16)
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", choices=["gemv"], default=None)
+    ap.add_argument("--sweep-calls", type=int, default=200)
+    ap.add_argument("--sweep-shape", default=None, help="one shape of the sweep, as MxK")
     return ap.parse_args()
 
 
@@ -312,8 +325,88 @@ def run_ours(args):
     gpu.close()
 
 
+GEMV_SHAPES = [(3072, 1024), (4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072), (151936, 1024)]
+L2_BYTES = 126 * 2**20
+
+
+def cpu_linear_us(m: int, k: int, batch: int, budget_s: float = 1.0) -> float:
+    """Oracle matvecQ8 (one row) / matmulQ8 (batch columns), one host thread,
+    microseconds per call over a bounded number of calls."""
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(SEED)
+    q = rng.integers(-127, 128, size=(m, k), dtype=np.int8)
+    s = rng.random(m, dtype=np.float32) * np.float32(0.01)
+    x = rng.standard_normal((k,) if batch == 1 else (k, batch)).astype(np.float32)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        if batch == 1:
+            O.matvec_q8(q, s, x)
+        else:
+            O.matmul_q8(q, s, x)
+        calls += 1
+        dt = time.perf_counter() - t0
+        if dt > budget_s or calls >= 20:
+            return dt / calls * 1e6
+
+
+def run_gemv_sweep(args):
+    import torch
+    from zynfer_b200 import cuda as zc
+    peak, peak_kind = measured_peaks()
+    gpu = zc.Gpu(0)
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED)
+    shapes = GEMV_SHAPES
+    if args.sweep_shape:
+        shapes = [tuple(int(v) for v in args.sweep_shape.lower().split("x"))]
+    for (m, k) in shapes:
+        copies = max(2, -(-2 * L2_BYTES // (m * k)))
+        w = torch.randint(-127, 128, (copies, m, k), dtype=torch.int8, device=dev, generator=g)
+        sc = torch.rand((copies, m), device=dev, generator=g) * 0.01
+        cpu_us = {}
+        for batch in (1, 8):
+            x = torch.randn((batch, k), device=dev, generator=g)
+            y = torch.empty((batch, m), device=dev)
+            ref = (x @ w[0].float().t()) * sc[0]
+            for path in (("auto",) if batch == 1 else ("auto", "gemv")):
+                gpu.set_linear_path(path)
+                for i in range(copies):  # warm-up: tensor maps, scratch
+                    gpu.linear(zc.W_Q8, w[i], sc[i], x, batch, m, k, y)
+                gpu.sync()
+                gpu.linear(zc.W_Q8, w[0], sc[0], x, batch, m, k, y)
+                gpu.sync()
+                err = float(((y - ref).abs().max() / ref.abs().max().clamp_min(1e-30)).item())
+                calls = max(args.sweep_calls, 2 * copies)
+                gpu.set_timing(True)
+                for i in range(calls):
+                    gpu.linear(zc.W_Q8, w[i % copies], sc[i % copies], x, batch, m, k, y)
+                n, ms = gpu.kernel_time(zc.K_LINEAR)
+                gpu.set_timing(False)
+                us = ms / max(1, n) * 1e3
+                nbytes = m * k + 4 * m + 4 * batch * k + 4 * batch * m
+                gbs = nbytes / (us * 1e-6) / 1e9
+                if batch not in cpu_us:
+                    cpu_us[batch] = cpu_linear_us(m, k, batch)
+                print(json.dumps({
+                    "sweep": "gemv", "m": m, "k": k, "batch": batch, "path": path, "kernel_path": gpu.last_path,
+                    "us_per_call": round(us, 3), "bytes_per_call": nbytes, "achieved_gbs": round(gbs, 1),
+                    "peak_gbs": peak, "peak_kind": peak_kind, "frac": round(gbs / peak, 4),
+                    "rotation_copies": copies, "calls": n, "max_rel_err_vs_torch_f32": err,
+                    "cpu_us_per_call": round(cpu_us[batch], 1), "cpu_threads": 1,
+                    "cpu_kind": "port (oracle matvecQ8 / matmulQ8)"}), flush=True)
+        del w, sc
+        torch.cuda.empty_cache()
+    gpu.set_linear_path("auto")
+    gpu.close()
+
+
 def main():
     args = parse()
+    if args.sweep == "gemv":
+        run_gemv_sweep(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -165,7 +165,7 @@ ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, c
                      const float *x, uint32_t batch, uint32_t m, uint32_t k, float *y);
 /* Kernel family for linear layers: "auto" (model schedules: CUDA-core GEMV for
  * one activation row except the LM head, tcgen05 tensor cores otherwise;
- * zynfer_cu_linear: GEMV up to 4 rows), "gemv",
+ * zynfer_cu_linear likewise: the GEMV for one row of at most 16384 outputs), "gemv",
  * "tcgen05", or "simt" (the CUDA-core tiled GEMM, kept for comparisons).
  * Applies to later calls of this context. */
 ZYNFER_CU_API int zynfer_cu_set_linear_path(ZynferCuCtx *ctx, const char *path);

@@ -111,6 +111,24 @@ def test_linear_q8_each_path(gpu, path, m, k, batch):  # ops.zig:181-197 on ever
         assert O.expect_close(ref, got[b], 2e-4, 2e-4), (path, b, d.max_abs, d.failing_index)
 
 
+@pytest.mark.parametrize("m,k,batch,expect", [(4096, 1024, 1, "linear:gemv"), (1024, 3072, 1, "linear:gemv"),
+                                              (4096, 1024, 2, "linear:tcgen05"), (16512, 1024, 1, "linear:tcgen05")])
+def test_linear_q8_auto_reports_the_kernel_it_ran(gpu, m, k, batch, expect):  # ops.zig:181-197
+    # auto: the GEMV for one activation row of at most 16384 outputs, tcgen05 otherwise
+    w = O.synth_normal(m * k, 33, m + k, 0.02).reshape(m, k)
+    q, s = O.pack_row_q8(w)
+    x = O.synth_normal(batch * k, 34, batch, 1.0).reshape(batch, k)
+    y = torch.empty((batch, m), dtype=torch.float32, device="cuda")
+    gpu.set_linear_path("auto")
+    gpu.linear(zc.W_Q8, dev(q), dev(s), dev(x), batch, m, k, y)
+    gpu.sync()
+    assert gpu.last_path == expect
+    got = host(y)
+    for b in range(batch):
+        ref = O.matvec_q8(q, s, x[b])
+        assert O.expect_close(ref, got[b], 2e-4, 2e-4), (b, O.diff(ref, got[b]).max_abs)
+
+
 @pytest.mark.parametrize("path", ["tcgen05", "simt"])
 @pytest.mark.parametrize("batch", [5, 64, 200])
 def test_linear_bf16_each_path(gpu, path, batch):  # ops.zig:133-141 on bf16-widened weights

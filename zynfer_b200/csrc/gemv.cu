@@ -7,8 +7,11 @@
 // magic-number trick, and multiplies against activations staged once per CTA
 // in shared memory (optionally RMS-normalised on the way in). The shared
 // layout is swizzled so the 16-byte activation reads of a warp hit 32
-// distinct banks. A persistent grid (a few CTAs per SM) walks row groups so
-// the activation staging cost is paid ~600 times, not once per row group.
+// distinct banks. A persistent grid (one wave of resident CTAs) walks row
+// groups so the activation staging cost is paid once per CTA, not once per
+// row group. A warp holds a whole row group's weights in registers (K <= 3072
+// for one row per warp): all of its loads are in flight at once, and the
+// first group's are issued before griddepcontrol.wait.
 // Epilogues: scale, residual add, SwiGLU over interleaved (gate, up) rows,
 // and a fused argmax for the LM head (orderable 64-bit key, atomicMax).
 #include <algorithm>
@@ -45,14 +48,43 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
     const int K = a.K;
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     pdl_launch_dependents();
-    {
-        // the weights do not depend on the previous kernel: pull this warp's
-        // first row group toward L2 while that kernel finishes
-        const int row_bytes = WK == kWQ8 ? K : 2 * K;
-        const int r0 = (blockIdx.x * kWarps + warp) * R;
-        const char* wb = reinterpret_cast<const char*>(a.w);
+
+    constexpr int kElems = WK == kWQ8 ? 16 : 8;     // k values per 16-byte load
+    const int row_bytes = WK == kWQ8 ? K : 2 * K;
+    const int iters = K / (kElems * kWarp);          // K is a multiple of 512 (int8) / 256 (bf16)
+    const int groups = (a.M + R - 1) / R;
+    const char* wbase = reinterpret_cast<const char*>(a.w);
+    const int g_first = blockIdx.x * kWarps + warp;
+
+    // A row group of up to kHeld 16-byte loads per lane is read whole into
+    // registers, every load in flight at once; the first group's loads are
+    // issued before griddepcontrol.wait (the weights do not depend on the
+    // previous kernel), so only the activations are read after it.
+    constexpr int kHeld = 6;
+    constexpr int kMaxIt = kHeld / R;
+    const bool held = iters <= kMaxIt;
+    uint4 wv[kMaxIt][R];
+    auto load_group = [&](int g) {
+        const int r0 = g * R;
+#pragma unroll
+        for (int it = 0; it < kMaxIt; ++it) {
+            if (it < iters) {
+                const int k0 = it * kElems * kWarp + lane * kElems;
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int row = min(r0 + r, a.M - 1);
+                    wv[it][r] = ldg_stream(wbase + (size_t)row * row_bytes + (size_t)k0 * (WK == kWQ8 ? 1 : 2));
+                }
+            }
+        }
+    };
+    if (held) {
+        if (g_first < groups) load_group(g_first);
+    } else {
+        // pull this warp's first row group toward L2 while the previous kernel finishes
+        const int r0 = g_first * R;
         for (int r = 0; r < R && r0 + r < a.M; ++r)
-            for (int off = lane * 128; off < row_bytes; off += kWarp * 128) prefetch_l2(wb + (size_t)(r0 + r) * row_bytes + off);
+            for (int off = lane * 128; off < row_bytes; off += kWarp * 128) prefetch_l2(wbase + (size_t)(r0 + r) * row_bytes + off);
     }
     pdl_wait();
 
@@ -85,13 +117,38 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
 #pragma unroll
     for (int b = 0; b < NB; ++b) best[b] = 0ull;
 
-    constexpr int kElems = WK == kWQ8 ? 16 : 8;     // k values per 16-byte load
-    const int row_bytes = WK == kWQ8 ? K : 2 * K;
-    const int iters = K / (kElems * kWarp);          // K is a multiple of 512 (int8) / 256 (bf16)
-    const int groups = (a.M + R - 1) / R;
-    const char* wbase = reinterpret_cast<const char*>(a.w);
+    // acc[r][b] += W[r0 + r][k0 .. k0 + kElems) . x[b][same]
+    auto dot_chunk = [&](const uint4 (&wr)[R], int k0, float (&acc)[R][NB]) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            float w[kElems];
+            if constexpr (WK == kWQ8) {
+                i8x4_to_f32(wr[r].x, w[0], w[1], w[2], w[3]);
+                i8x4_to_f32(wr[r].y, w[4], w[5], w[6], w[7]);
+                i8x4_to_f32(wr[r].z, w[8], w[9], w[10], w[11]);
+                i8x4_to_f32(wr[r].w, w[12], w[13], w[14], w[15]);
+            } else {
+                w[0] = bf16lo(wr[r].x); w[1] = bf16hi(wr[r].x);
+                w[2] = bf16lo(wr[r].y); w[3] = bf16hi(wr[r].y);
+                w[4] = bf16lo(wr[r].z); w[5] = bf16hi(wr[r].z);
+                w[6] = bf16lo(wr[r].w); w[7] = bf16hi(wr[r].w);
+            }
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                const float* xb = xs + b * K;
+#pragma unroll
+                for (int q = 0; q < kElems / 4; ++q) {
+                    const float4 xv = *reinterpret_cast<const float4*>(xb + swz<WK>(k0 + 4 * q));
+                    acc[r][b] = fmaf(w[4 * q + 0], xv.x, acc[r][b]);
+                    acc[r][b] = fmaf(w[4 * q + 1], xv.y, acc[r][b]);
+                    acc[r][b] = fmaf(w[4 * q + 2], xv.z, acc[r][b]);
+                    acc[r][b] = fmaf(w[4 * q + 3], xv.w, acc[r][b]);
+                }
+            }
+        }
+    };
 
-    for (int g = blockIdx.x * kWarps + warp; g < groups; g += gridDim.x * kWarps) {
+    for (int g = g_first; g < groups; g += gridDim.x * kWarps) {
         const int r0 = g * R;
         float acc[R][NB];
 #pragma unroll
@@ -99,40 +156,21 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
 #pragma unroll
             for (int b = 0; b < NB; ++b) acc[r][b] = 0.0f;
 
-        for (int it = 0; it < iters; ++it) {
-            const int k0 = it * kElems * kWarp + lane * kElems;
-            uint4 wv[R];
+        if (held) {
+            if (g != g_first) load_group(g);
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int row = min(r0 + r, a.M - 1);
-                wv[r] = ldg_stream(wbase + (size_t)row * row_bytes + (size_t)k0 * (WK == kWQ8 ? 1 : 2));
-            }
+            for (int it = 0; it < kMaxIt; ++it)
+                if (it < iters) dot_chunk(wv[it], it * kElems * kWarp + lane * kElems, acc);
+        } else {
+            for (int it = 0; it < iters; ++it) {
+                const int k0 = it * kElems * kWarp + lane * kElems;
+                uint4 wr[R];
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                float w[kElems];
-                if constexpr (WK == kWQ8) {
-                    i8x4_to_f32(wv[r].x, w[0], w[1], w[2], w[3]);
-                    i8x4_to_f32(wv[r].y, w[4], w[5], w[6], w[7]);
-                    i8x4_to_f32(wv[r].z, w[8], w[9], w[10], w[11]);
-                    i8x4_to_f32(wv[r].w, w[12], w[13], w[14], w[15]);
-                } else {
-                    w[0] = bf16lo(wv[r].x); w[1] = bf16hi(wv[r].x);
-                    w[2] = bf16lo(wv[r].y); w[3] = bf16hi(wv[r].y);
-                    w[4] = bf16lo(wv[r].z); w[5] = bf16hi(wv[r].z);
-                    w[6] = bf16lo(wv[r].w); w[7] = bf16hi(wv[r].w);
+                for (int r = 0; r < R; ++r) {
+                    const int row = min(r0 + r, a.M - 1);
+                    wr[r] = ldg_stream(wbase + (size_t)row * row_bytes + (size_t)k0 * (WK == kWQ8 ? 1 : 2));
                 }
-#pragma unroll
-                for (int b = 0; b < NB; ++b) {
-                    const float* xb = xs + b * K;
-#pragma unroll
-                    for (int q = 0; q < kElems / 4; ++q) {
-                        const float4 xv = *reinterpret_cast<const float4*>(xb + swz<WK>(k0 + 4 * q));
-                        acc[r][b] = fmaf(w[4 * q + 0], xv.x, acc[r][b]);
-                        acc[r][b] = fmaf(w[4 * q + 1], xv.y, acc[r][b]);
-                        acc[r][b] = fmaf(w[4 * q + 2], xv.z, acc[r][b]);
-                        acc[r][b] = fmaf(w[4 * q + 3], xv.w, acc[r][b]);
-                    }
-                }
+                dot_chunk(wr, k0, acc);
             }
         }
 #pragma unroll
@@ -186,8 +224,11 @@ void launch_nb(const LinearArgs& a, cudaStream_t st) {
     const size_t smem = (size_t)NB * a.K * sizeof(float);
     const int groups = (a.M + R - 1) / R;
     auto pick = [&](auto kern) {
-        // resident CTAs per SM: bounded by threads (2048 / 256) and shared memory
-        const int per_sm = std::max(1, std::min(8, (int)((220 * 1024) / (smem + 2048))));
+        // resident CTAs per SM (threads, registers, shared memory): the grid
+        // never exceeds one wave, and warps loop over the remaining row groups
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1)
+            per_sm = 1;
         const int want = (groups + kWarps - 1) / kWarps;
         launch_pdl(kern, std::min(want, per_sm * device_sm_count()), kThreads, smem, st, a);
     };

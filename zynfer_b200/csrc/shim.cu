@@ -33,7 +33,6 @@ enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3 };
 // Decode schedule: separate kernels per op (graph-captured; what auto takes),
 // or one persistent dataflow kernel per step for small int8 batches (on request).
 enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2 };
-constexpr int kGemvMaxRows = 4;  // op-level auto policy: GEMV up to this many rows, tcgen05 above
 constexpr int kGemvMaxM = 16384;  // model auto policy: largest matrix (output rows) for the batch-1 GEMV
 
 struct LayerDev {
@@ -350,9 +349,10 @@ const CUtensorMap* b_map(ZynferCuCtx* c, int wkind, int K, int nt) {
 
 // y = linear(norm_w ? rmsnorm(x) : x) with the epilogue `epi`, on the path the
 // policy picks: GEMV (x staged in shared memory) for a few rows, tcgen05 for more.
-void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtensorMap* tmA, int M, int K,
-            const float* x, int N, float* y, int epi, const float* resid, const float* norm_w,
-            unsigned long long* keys, int wkind = -1) {
+// Returns the kernel family it launched (kPathGemv, kPathTc or kPathSimt).
+int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtensorMap* tmA, int M, int K,
+           const float* x, int N, float* y, int epi, const float* resid, const float* norm_w,
+           unsigned long long* keys, int wkind = -1) {
     if (wkind < 0) wkind = c->wkind;
     LinearArgs a;
     a.w = w; a.scale = s; a.wkind = wkind; a.M = M; a.K = K; a.x = x; a.ldx = K; a.N = N;
@@ -395,6 +395,7 @@ void linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtens
         c->step_launches += 2;
     }
     tend(c, te);
+    return path;
 }
 
 // One decode step for the rows already staged in dtok/dseq/dpos.
@@ -1284,12 +1285,11 @@ int zynfer_cu_linear(ZynferCuCtx* c, int wkind, const void* w, const float* scal
         it = c->amaps.emplace(key, tm).first;
     }
     c->step_launches = 0;
-    linear(c, ZYNFER_CU_K_LINEAR, w, wk == kWQ8 ? scale : nullptr, &it->second, (int)m, (int)k, x, (int)batch, y,
-           kEpiNone, nullptr, nullptr, nullptr, wk);
+    const int p = linear(c, ZYNFER_CU_K_LINEAR, w, wk == kWQ8 ? scale : nullptr, &it->second, (int)m, (int)k, x,
+                         (int)batch, y, kEpiNone, nullptr, nullptr, nullptr, wk);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "linear launch");
-    const int p = c->path_policy == kPathAuto ? (batch <= (uint32_t)kGemvMaxRows ? kPathGemv : kPathTc) : c->path_policy;
-    c->path = p == kPathGemv && batch <= 8 ? "linear:gemv" : (p == kPathSimt ? "linear:simt" : "linear:tcgen05");
+    c->path = p == kPathGemv ? "linear:gemv" : (p == kPathSimt ? "linear:simt" : "linear:tcgen05");
     return ZYNFER_CU_OK;
 }
 
