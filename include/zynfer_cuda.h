@@ -32,7 +32,10 @@
  * "wait" (the next "persistent" decode step of a model with two or more
  * layers polls one input with a tag that nothing writes: its bounded device
  * wait runs out after a few seconds, every CTA stops, and the call returns
- * TIMEOUT with the context still usable).
+ * TIMEOUT with the context still usable). zynfer_cu_set_fail_at(NULL, "wait")
+ * arms the same for the next zynfer_cu_linear_q8_static call, which has no
+ * context: none of its CTAs loads the first K stage, its bounded waits run
+ * out, and zynfer_cu_linear_q8_static_status reports TIMEOUT.
  */
 #ifndef ZYNFER_CUDA_H
 #define ZYNFER_CUDA_H
@@ -133,6 +136,14 @@ ZYNFER_CU_API int zynfer_cu_seq_reset(ZynferCuCtx *ctx, uint32_t seq);
 ZYNFER_CU_API int zynfer_cu_seq_len(const ZynferCuCtx *ctx, uint32_t seq, uint32_t *len);
 /* K or V of one layer for positions [0, len): out [n_kv][len][head_dim] f32. */
 ZYNFER_CU_API int zynfer_cu_kv_read(ZynferCuCtx *ctx, uint32_t seq, uint32_t layer, int which_v, float *out);
+/* Seeded stand-in for a prefill, for test and benchmark workloads at long
+ * contexts: resets `seq` and fills its cache, every layer, positions [0, n),
+ * then sets its length to n. K (code 100) and V (code 101) of layer l use
+ * the generator of synth_rng.h with key(seed, ((l + 1) << 8) | code); the
+ * element (kv head h, position p, dim j) is bf16(normal(key, (h n + p) d + j,
+ * std 1)). A CPU restatement that fills a dense KvCache (kv_cache.zig:14-33)
+ * the same way holds bit-identical K/V. */
+ZYNFER_CU_API int zynfer_cu_kv_fill_synthetic(ZynferCuCtx *ctx, uint32_t seq, uint32_t n, uint64_t seed);
 
 /* ---- forward ---- */
 /* Session.prefillLastLogits (qwen_forward.zig:89-160): resets `seq`, runs the
@@ -191,15 +202,52 @@ ZYNFER_CU_API int zynfer_cu_set_decode_schedule(ZynferCuCtx *ctx, const char *sc
  * row scales, 768 KiB) is a file-scope device array that every GPU loading
  * the library holds until the process exits.
  * Limits: batch <= ZYNFER_CU_STATIC_MAX_ROWS, k <= ZYNFER_CU_STATIC_MAX_K,
- * k and m multiples of 128, x 16-byte aligned; otherwise ZYNFER_CU_INVALID.
+ * k and m multiples of 128, m < 2^31, x 16-byte aligned, y and scale 4-byte
+ * aligned; otherwise ZYNFER_CU_INVALID.
  * The first call on a device resolves the array's device address and sets
  * kernel attributes on that device; make it before any stream capture. All
  * calls share the array, so calls that overlap on the GPU (other streams,
- * other threads) race: serialise them. */
+ * other threads) race: serialise them. The return value covers the launch
+ * only: the kernel's bounded device waits report through a device error word
+ * that is also a file-scope array, read by zynfer_cu_linear_q8_static_status
+ * after the caller has synchronised its stream. */
 #define ZYNFER_CU_STATIC_MAX_ROWS 64
 #define ZYNFER_CU_STATIC_MAX_K 4096
 ZYNFER_CU_API int zynfer_cu_linear_q8_static(const int8_t *w, const float *scale, const float *x,
                                              uint32_t batch, uint32_t m, uint32_t k, float *y, void *stream);
+/* Device error word of zynfer_cu_linear_q8_static on the current device
+ * (no counterpart in the reference): ZYNFER_CU_OK when every call since the
+ * last clear finished its waits, ZYNFER_CU_TIMEOUT when one ran out (that
+ * call's y is not valid). clear != 0 resets the word. Synchronous (plain
+ * cudaMemcpy of 4 bytes, nothing allocated); call it after synchronising the
+ * stream of the calls it covers. */
+ZYNFER_CU_API int zynfer_cu_linear_q8_static_status(int clear);
+/* attentionInto (ops.zig:285-354) for one decode token per sequence, the
+ * kernel the decode step runs for layer `layer`: qkv [batch][(n_q + 2 n_kv)
+ * head_dim] holds each row's raw q, k, v projections (device); the kernel
+ * applies the layer's per-head RMSNorm to q and k and split-half RoPE at
+ * position p = the sequence's length (qwen_block.zig:190-194, ops.zig:233-261),
+ * writes this token's K/V (bf16) into the sequence's paged cache of that layer
+ * at p, and attends over the p + 1 cached positions with a log-sum-exp merge of
+ * its KV splits. out [batch][n_q][head_dim] (device). The sequence's length is
+ * not advanced (the decode step does that once for all layers), so a repeated
+ * call rewrites the same position. seqs is a host array of distinct slots;
+ * qkv and out 16-byte aligned. Synchronises; device-side index checks return
+ * INVALID. */
+ZYNFER_CU_API int zynfer_cu_attn_decode(ZynferCuCtx *ctx, uint32_t layer, const uint32_t *seqs, uint32_t batch,
+                                        const float *qkv, float *out);
+/* Per-head RMSNorm (ops.zig:49-67 with the q_norm / k_norm weights,
+ * qwen_block.zig:190-191) and split-half RoPE (ops.zig:233-261) of `rows`
+ * tokens at positions pos0 .. pos0 + rows - 1, from the fused projection rows
+ * qkv [rows][(n_q + 2 n_kv) head_dim] (device). q_out [n_q][rows][head_dim] and
+ * k_out [n_kv][rows][head_dim] are heads-major, the layout attentionInto takes
+ * (tokensHeadsToHeadsTokens, ops.zig:355-373). Needs the model's RoPE table:
+ * pos0 + rows <= max_seq_len. Synchronises. */
+ZYNFER_CU_API int zynfer_cu_rmsnorm_qk_rope(ZynferCuCtx *ctx, const float *qkv, uint32_t rows, const float *q_norm,
+                                            const float *k_norm, uint32_t pos0, float *q_out, float *k_out);
+/* siluMul (ops.zig:36-42): out[i] = silu(gate[i]) * up[i], device pointers,
+ * the arithmetic of every SwiGLU epilogue. */
+ZYNFER_CU_API int zynfer_cu_swiglu(ZynferCuCtx *ctx, const float *gate, const float *up, uint64_t n, float *out);
 /* packRowQ8 (ops.zig:145-162) on the device, bit-exact. */
 ZYNFER_CU_API int zynfer_cu_pack_q8(ZynferCuCtx *ctx, const float *w, uint32_t rows, uint32_t cols, int8_t *q,
                       float *scale);
@@ -224,6 +272,13 @@ ZYNFER_CU_API int zynfer_cu_step_launches(const ZynferCuCtx *ctx);
 /* Host->device and device->host bytes copied by decode/generate/prefill calls
  * since the last reset (reset != 0 clears after reading). */
 ZYNFER_CU_API int zynfer_cu_io_bytes(ZynferCuCtx *ctx, uint64_t *h2d, uint64_t *d2h, int reset);
+/* Allocation events since zynfer_cu_model_init ("decode does not allocate",
+ * tiny_block.zig:385-401): device = device allocations (cudaMalloc, CUDA
+ * graph instantiation), host = growths of host containers past their
+ * reserved capacity. The first decode of a batch size captures its graph
+ * (one event of each); later decode steps and generate calls of that batch
+ * size add none. */
+ZYNFER_CU_API int zynfer_cu_alloc_events(const ZynferCuCtx *ctx, uint64_t *device, uint64_t *host);
 
 #ifdef __cplusplus
 }

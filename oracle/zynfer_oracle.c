@@ -804,8 +804,12 @@ int zo_session_fill_kv(ZoSession *s, size_t n, uint64_t seed) {
     const ZoArch *a = &s->m->a;
     if (n > s->max_seq) return ZO_INVALID;
     const size_t d = a->head_dim;
-    for (uint32_t l = 0; l < a->layers; l++) {
-        for (int which = 0; which < 2; which++) {
+    /* every (layer, K|V) plane is independent: threads split them, values unchanged */
+#pragma omp parallel for schedule(dynamic, 1) num_threads(s->m->threads)
+    for (int lw = 0; lw < (int)(2 * a->layers); lw++) {
+        const uint32_t l = (uint32_t)lw / 2;
+        const int which = lw % 2;
+        {
             const uint64_t key = zs_key(seed, zs_layer_stream(l, (uint32_t)(100 + which)));
             const float k = (float)(1.0 / ZS_IH4_SIGMA);
             float *dst = which ? s->vc[l] : s->kc[l];

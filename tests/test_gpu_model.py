@@ -208,3 +208,26 @@ def test_block_forward_matches_oracle_block():  # qwen_block.zig:161-235, one la
     got = m.block_forward(0, 0, x[64:])
     exp = s.block(0, x[64:])
     assert O.expect_close(exp, got, 2e-3, 2e-3)
+
+
+def test_decode_allocates_nothing(small):  # tiny_block.zig:385-401
+    """After the first decode of a batch size (which captures its graph), decode
+    steps and generate calls of that batch size allocate neither device memory
+    nor host containers."""
+    torch = pytest.importorskip("torch")
+    slots = [7, 8, 9, 10]
+    for sq in slots:
+        small.prefill(sq, O.synth_tokens(20, SEED, 60 + sq, SMALL["vocab"]), want_logits=False)
+    toks = [1, 2, 3, 4]
+    small.decode_step(slots, toks)                     # captures the batch-4 graph
+    small.decode_step(slots, toks, want_logits=True)
+    small.generate(slots, toks, 2)
+    torch.cuda.synchronize()
+    before = small.gpu.alloc_events()
+    free_before = torch.cuda.mem_get_info(0)[0]
+    for i in range(64):
+        small.decode_step(slots, toks, want_logits=(i % 8 == 0))
+    small.generate(slots, toks, 8)
+    torch.cuda.synchronize()
+    assert small.gpu.alloc_events() == before
+    assert torch.cuda.mem_get_info(0)[0] == free_before

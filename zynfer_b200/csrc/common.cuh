@@ -56,6 +56,10 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float& f0, float& f1, fl
     f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - magic;
 }
 
+// siluScalar (ops.zig:44-46): x * (1 / (1 + e^-x)), the one definition every
+// SwiGLU epilogue and the standalone siluMul kernel use.
+__device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);

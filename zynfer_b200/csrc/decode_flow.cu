@@ -206,7 +206,6 @@ __device__ __forceinline__ uint32_t item_bytes(uint32_t bytes) { return (bytes +
 __device__ __forceinline__ int swz(int k) {
     return (k & ~15) | (((((k >> 2) & 3) + ((k >> 5) & 3)) & 3) << 2) | (k & 3);
 }
-__device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 __device__ __forceinline__ uint32_t u4get(const uint4& v, int q) {
     return q == 0 ? v.x : q == 1 ? v.y : q == 2 ? v.z : v.w;
 }

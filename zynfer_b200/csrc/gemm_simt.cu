@@ -14,7 +14,6 @@ namespace {
 constexpr int BM = 128, BN = 64, BK = 32, THREADS = 256;
 constexpr int WPAD = BM + 4, XPAD = BN + 4;
 
-__device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 
 template <int WK, int EPI>
 __global__ void __launch_bounds__(THREADS) gemm_simt_kernel(LinearArgs a) {

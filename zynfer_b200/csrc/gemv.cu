@@ -37,7 +37,6 @@ __device__ __forceinline__ int swz(int k) {
     }
 }
 
-__device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 
 template <int WK, int NB, int R, int EPI>
 __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {

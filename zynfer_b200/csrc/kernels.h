@@ -57,6 +57,10 @@ void launch_copy_rows_u16(const uint16_t* src, int rows, int cols, uint16_t* dst
                           int dst_offset, cudaStream_t st);
 void launch_unpack_rows_i8(const int8_t* src, const float* ssrc, int rows, int cols, int8_t* dst,
                            float* sdst, int src_stride, int src_offset, cudaStream_t st);
+// Seeded stand-in cache of one sequence (positions [0, n) of every layer);
+// table_row = that sequence's device block-table row.
+void launch_kv_fill(uint16_t* kv, size_t kv_layer_elems, const int* table_row, int n_pool_blocks, int layers,
+                    int n_kv, int n, uint64_t seed, uint32_t* err, cudaStream_t st);
 
 // norm.cu
 void launch_rmsnorm(const float* x, const float* w, float* y, int rows, int cols, float eps,
@@ -76,7 +80,7 @@ struct QkvArgs {
     int pos0;
     const int* row_seq;
     int seq0;
-    // paged bf16 cache
+    // paged bf16 cache (nullable: then k and v go only to the staging buffers)
     uint16_t* kv_layer;         // this layer's pool base: [n_kv][blocks][K, V][16][d], kv_swizzle rows
     const int* block_table;     // [seqs][max_blocks]
     int max_blocks;
@@ -100,6 +104,7 @@ struct FinalizeArgs {
     int B;                     // <= 1024 (one CTA)
 };
 void launch_bf16_to_f32(const uint16_t* src, size_t n, float* dst, cudaStream_t st);
+void launch_silu_mul(const float* g, const float* u, size_t n, float* o, cudaStream_t st);
 void launch_finalize(const FinalizeArgs& a, cudaStream_t st);
 
 // gemv.cu (N <= 8)

@@ -128,16 +128,18 @@ __global__ void qkv_post_kernel(QkvArgs a) {
     }
     const int which = (h - a.n_q) / a.n_kv;  // 0 = k, 1 = v
     const int kvh = (h - a.n_q) % a.n_kv;
-    const int seq = a.row_seq ? a.row_seq[t] : a.seq0;
-    const int bi = pos / kKvBlock;
-    int blk = -1;
-    if (bi < a.max_blocks) blk = a.block_table[(size_t)seq * a.max_blocks + bi];
-    if (blk < 0 || blk >= a.n_pool_blocks) {
-        if (lane == 0 && a.err) atomicOr(a.err, kErrBadIndex);
-    } else {
-        uint16_t* dst = a.kv_layer + (((size_t)kvh * a.n_pool_blocks + blk) * 2 + which) * kKvBlock * d;
+    if (a.kv_layer) {
+        const int seq = a.row_seq ? a.row_seq[t] : a.seq0;
+        const int bi = pos / kKvBlock;
+        int blk = -1;
+        if (bi < a.max_blocks) blk = a.block_table[(size_t)seq * a.max_blocks + bi];
+        if (blk < 0 || blk >= a.n_pool_blocks) {
+            if (lane == 0 && a.err) atomicOr(a.err, kErrBadIndex);
+        } else {
+            uint16_t* dst = a.kv_layer + (((size_t)kvh * a.n_pool_blocks + blk) * 2 + which) * kKvBlock * d;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) dst[kv_swizzle(pos % kKvBlock, lane + 32 * j)] = f32_to_bf16_rne(v[j]);
+            for (int j = 0; j < 4; ++j) dst[kv_swizzle(pos % kKvBlock, lane + 32 * j)] = f32_to_bf16_rne(v[j]);
+        }
     }
     float* stage = which == 0 ? a.k_stage : a.v_stage;
     if (stage) {
@@ -145,6 +147,21 @@ __global__ void qkv_post_kernel(QkvArgs a) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = a.stage_round_bf16 ? bf16_round(v[j]) : v[j];
     }
+}
+
+// siluMul (ops.zig:36-42): o = silu(g) * u, elementwise.
+__global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, size_t n,
+                                float* __restrict__ o) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        o[i] = __fmul_rn(silu(g[i]), u[i]);
+}
+
+void launch_silu_mul(const float* g, const float* u, size_t n, float* o, cudaStream_t st) {
+    size_t blocks = (n + 255) / 256;
+    if (blocks > (size_t)device_sm_count() * 8) blocks = (size_t)device_sm_count() * 8;
+    launch_pdl(silu_mul_kernel, (int)(blocks ? blocks : 1), 256, 0, st, g, u, n, o);
 }
 
 void launch_qkv_post(const QkvArgs& a, cudaStream_t st) {
@@ -195,6 +212,7 @@ void prepare_norm_kernels() {
     configure_kernel((const void*)embed_kernel, 0);
     configure_kernel((const void*)qkv_post_kernel, 0);
     configure_kernel((const void*)finalize_kernel, 0);
+    configure_kernel((const void*)silu_mul_kernel, 0);
 }
 
 }  // namespace zc

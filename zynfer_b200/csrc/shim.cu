@@ -57,14 +57,27 @@ struct TimedEvent {
     int cls;
 };
 
+// A decode graph of one batch size and the linear kernel families it holds
+// (bit kPath* of `paths`), so the path label of a graph launch names them.
+struct GraphEntry {
+    cudaGraphExec_t exec = nullptr;
+    unsigned paths = 0;
+};
+
 }  // namespace
 
 struct ZynferCuCtx {
     int device = -1;
     cudaStream_t stream = nullptr;
     std::string err;
-    std::string path = "none";
+    char path[96] = "none";  // label of the last call's kernels; a fixed buffer, written without allocating
+    unsigned step_paths = 0;  // linear families (bit kPath*) launched since the last reset
     ZynferCuCaps caps{};
+    // allocation events after zynfer_cu_model_init: device allocations
+    // (cudaMalloc, graph instantiation) and growth of host containers beyond
+    // their reserved capacity. A decode step of a batch size seen before adds
+    // neither (tiny_block.zig:385-401 pins the same for host memory).
+    uint64_t dev_alloc_events = 0, host_alloc_events = 0;
 
     // fault injection
     long fail_alloc_at = -1;
@@ -140,7 +153,7 @@ struct ZynferCuCtx {
     uint64_t* ptrace = nullptr;          // its phase timestamps when timing is on
     std::vector<uint64_t> ptrace_host;
 
-    std::map<int, cudaGraphExec_t> graphs;
+    std::map<int, GraphEntry> graphs;
     int step_launches = 0;  // kernels enqueued by the last decode step
     uint64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device bytes of decode/generate calls
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -188,6 +201,8 @@ int dalloc(ZynferCuCtx* c, T** p, size_t count) {
         cudaGetLastError();
         return fail(c, ZYNFER_CU_OOM, std::string("cudaMalloc(") + std::to_string(bytes) + "): " + cudaGetErrorString(e));
     }
+    c->dev_alloc_events += 1;
+    if (c->allocs.size() == c->allocs.capacity()) c->host_alloc_events += 1;
     c->allocs.push_back(v);
     *p = reinterpret_cast<T*>(v);
     return ZYNFER_CU_OK;
@@ -222,6 +237,19 @@ bool take_launch_fault(ZynferCuCtx* c) {
     c->fail_launch = false;
     c->err = "injected launch failure (ZYNFER_CUDA_FAIL_AT=launch)";
     return true;
+}
+
+// Path label "<call>:<linear kernel families>[:<mode>]" into the context's
+// fixed buffer (no allocation): e.g. "decode:gemv+tcgen05:graph".
+void set_path(ZynferCuCtx* c, const char* call, unsigned paths, const char* mode) {
+    char fam[48] = "";
+    const char* names[4] = {"auto", "gemv", "simt", "tcgen05"};
+    for (int b = 1; b < 4; ++b)
+        if (paths & (1u << b)) {
+            if (fam[0]) strncat(fam, "+", sizeof(fam) - strlen(fam) - 1);
+            strncat(fam, names[b], sizeof(fam) - strlen(fam) - 1);
+        }
+    snprintf(c->path, sizeof(c->path), "%s%s%s%s%s", call, fam[0] ? ":" : "", fam, mode ? ":" : "", mode ? mode : "");
 }
 
 // Map an HF tensor name (qwen3.zig:86-132) to its device destination.
@@ -366,6 +394,7 @@ int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtenso
     if (path == kPathTc && (!tmA || N > c->tc_tpad || K > c->tc_kmax || K > kPlanesMaxK)) path = kPathSimt;
     TimedEvent* te;
     tbegin(c, cls, &te);
+    c->step_paths |= 1u << path;
     if (path == kPathGemv) {
         launch_gemv(a, c->stream);
         c->step_launches += 1;
@@ -515,6 +544,7 @@ int ensure_blocks(ZynferCuCtx* c, uint32_t seq, uint32_t upto_len) {
         const int b = c->free_blocks.back();
         c->free_blocks.pop_back();
         c->table_host[(size_t)seq * c->max_blocks + bl.size()] = b;
+        if (bl.size() == bl.capacity()) c->host_alloc_events += 1;  // reserved to max_blocks at init
         bl.push_back(b);
         c->table_dirty[seq] = 1;
     }
@@ -574,7 +604,7 @@ void set_io_views(ZynferCuCtx* c, int B) {
     c->dpos = reinterpret_cast<int*>(c->dio + 2 * B);
 }
 
-int get_graph(ZynferCuCtx* c, int B, cudaGraphExec_t* out) {
+int get_graph(ZynferCuCtx* c, int B, GraphEntry* out) {
     auto it = c->graphs.find(B);
     if (it != c->graphs.end()) {
         *out = it->second;
@@ -582,6 +612,7 @@ int get_graph(ZynferCuCtx* c, int B, cudaGraphExec_t* out) {
     }
     cudaGraph_t g = nullptr;
     ZC_CHECK(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed), "begin capture");
+    c->step_paths = 0;
     enqueue_decode(c, B, false);
     cudaError_t e = cudaStreamEndCapture(c->stream, &g);
     if (e != cudaSuccess) return cuda_fail(c, e, "end capture");
@@ -589,8 +620,13 @@ int get_graph(ZynferCuCtx* c, int B, cudaGraphExec_t* out) {
     e = cudaGraphInstantiate(&ge, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return cuda_fail(c, e, "graph instantiate");
-    c->graphs[B] = ge;
-    *out = ge;
+    c->dev_alloc_events += 1;   // the executable graph holds device memory
+    c->host_alloc_events += 1;  // and a map node
+    GraphEntry ent;
+    ent.exec = ge;
+    ent.paths = c->step_paths;
+    c->graphs[B] = ent;
+    *out = ent;
     return ZYNFER_CU_OK;
 }
 
@@ -691,7 +727,7 @@ void zynfer_cu_destroy(ZynferCuCtx* c) {
     // driver reclaims everything and no CUDA call may be made.
     if (c->device >= 0 && cudaSetDevice(c->device) == cudaSuccess) {
         if (c->stream) cudaStreamSynchronize(c->stream);
-        for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+        for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second.exec);
         for (auto& t : c->tev) {
             cudaEventDestroy(t.a);
             cudaEventDestroy(t.b);
@@ -713,10 +749,17 @@ int zynfer_cu_caps(const ZynferCuCtx* c, ZynferCuCaps* out) {
 
 const char* zynfer_cu_last_error(const ZynferCuCtx* c) { return c ? c->err.c_str() : "null context"; }
 
-const char* zynfer_cu_last_path(const ZynferCuCtx* c) { return c ? c->path.c_str() : "null context"; }
+const char* zynfer_cu_last_path(const ZynferCuCtx* c) { return c ? c->path : "null context"; }
 
 int zynfer_cu_set_fail_at(ZynferCuCtx* c, const char* spec) {
-    if (!c) return ZYNFER_CU_INVALID;
+    if (!c) {
+        // process-wide: only the allocation-free linear, which has no context
+        if (spec && !strcmp(spec, "wait")) {
+            static_linear_arm_stall();
+            return ZYNFER_CU_OK;
+        }
+        return ZYNFER_CU_INVALID;
+    }
     parse_fail_spec(c, spec);
     return ZYNFER_CU_OK;
 }
@@ -800,8 +843,10 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     c->kv_layer_elems = (size_t)c->n_blocks * 2 * m.n_kv * kKvBlock * hd;
     ALLOC(c->kv, c->kv_layer_elems * m.layers);
     c->free_blocks.clear();
+    c->free_blocks.reserve(c->n_blocks);
     for (int b = c->n_blocks - 1; b >= 0; --b) c->free_blocks.push_back(b);
     c->seq_blocks.assign(m.max_seqs, {});
+    for (auto& bl : c->seq_blocks) bl.reserve(c->max_blocks);  // decode never grows a block list
     c->seq_len.assign(m.max_seqs, 0);
     c->table_dirty.assign(m.max_seqs, 0);
     if ((rc = halloc(c, &c->table_host, (size_t)m.max_seqs * c->max_blocks)) != ZYNFER_CU_OK) return rc;
@@ -886,6 +931,9 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     cudaMemset(c->derr, 0, 4);
     cudaMemset(c->dstep, 0, 4);
     ZC_CHECK(c, cudaDeviceSynchronize(), "model init");
+    c->allocs.reserve(c->allocs.size() + 64);  // op-level scratch growth later does not move the list
+    c->dev_alloc_events = 0;
+    c->host_alloc_events = 0;
     c->ready = true;
     return ZYNFER_CU_OK;
 }
@@ -1080,6 +1128,110 @@ int zynfer_cu_kv_read(ZynferCuCtx* c, uint32_t seq, uint32_t layer, int which_v,
     return ZYNFER_CU_OK;
 }
 
+int zynfer_cu_kv_fill_synthetic(ZynferCuCtx* c, uint32_t seq, uint32_t n, uint64_t seed) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    if (seq >= c->d.max_seqs) return fail(c, ZYNFER_CU_INVALID, "sequence id out of range");
+    if (n > c->d.max_seq_len) return fail(c, ZYNFER_CU_INVALID, "n exceeds max_seq_len");
+    if (c->d.head_dim != 128) return fail(c, ZYNFER_CU_UNSUPPORTED, "head_dim must be 128");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    release_seq(c, seq);
+    int rc = ensure_blocks(c, seq, n);
+    if (rc) return rc;
+    if ((rc = upload_table_rows(c, &seq, 1))) return rc;
+    launch_kv_fill(c->kv, c->kv_layer_elems, c->table_dev + (size_t)seq * c->max_blocks, c->n_blocks,
+                   (int)c->d.layers, (int)c->d.n_kv, (int)n, seed, c->derr, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "kv fill launch");
+    if ((rc = check_device_error(c))) return rc;
+    c->seq_len[seq] = n;
+    set_path(c, "kv_fill", 0, nullptr);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_attn_decode(ZynferCuCtx* c, uint32_t layer, const uint32_t* seqs, uint32_t batch, const float* qkv,
+                          float* out) {
+    if (!c) return ZYNFER_CU_INVALID;
+    if (!seqs || !qkv || !out) return fail(c, ZYNFER_CU_INVALID, "null argument");
+    int rc = validate_batch(c, seqs, batch, 1);
+    if (rc) return rc;
+    if (layer >= c->d.layers) return fail(c, ZYNFER_CU_INVALID, "layer out of range");
+    if (reinterpret_cast<uintptr_t>(qkv) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+        return fail(c, ZYNFER_CU_INVALID, "qkv and out must be 16-byte aligned");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    for (uint32_t i = 0; i < batch; ++i)
+        if ((rc = ensure_blocks(c, seqs[i], c->seq_len[seqs[i]] + 1))) return rc;
+    if ((rc = upload_table_rows(c, seqs, batch))) return rc;
+    set_io_views(c, (int)batch);
+    for (uint32_t i = 0; i < batch; ++i) {
+        c->hio[i] = 0;
+        c->hio[batch + i] = seqs[i];
+        c->hio[2 * batch + i] = c->seq_len[seqs[i]];
+    }
+    ZC_CHECK(c, cudaMemcpyAsync(c->dio, c->hio, (size_t)3 * batch * 4, cudaMemcpyHostToDevice, c->stream), "stage");
+    const ZynferCuModelDesc& m = c->d;
+    const LayerDev& Ld = c->L[layer];
+    AttnDecodeArgs aa{};
+    aa.qkv = qkv; aa.q_norm = Ld.q_norm; aa.k_norm = Ld.k_norm; aa.rope = c->rope;
+    aa.rope_max_pos = (int)m.max_seq_len; aa.eps = m.eps;
+    aa.kv_layer = c->kv + layer * c->kv_layer_elems; aa.block_table = c->table_dev;
+    aa.max_blocks = c->max_blocks; aa.n_pool_blocks = c->n_blocks;
+    aa.seq_of = c->dseq; aa.positions = c->dpos; aa.B = (int)batch; aa.n_q = m.n_q; aa.n_kv = m.n_kv;
+    aa.d = m.head_dim; aa.max_segs = decode_max_segs(c->max_blocks); aa.partial = c->dpart;
+    aa.counters = c->dcnt; aa.out = out; aa.err = c->derr;
+    launch_attn_decode(aa, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "attention launch");
+    if ((rc = check_device_error(c))) return rc;
+    set_path(c, "attn_decode", 0, nullptr);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_rmsnorm_qk_rope(ZynferCuCtx* c, const float* qkv, uint32_t rows, const float* q_norm,
+                              const float* k_norm, uint32_t pos0, float* q_out, float* k_out) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    if (!qkv || !q_norm || !k_norm || !q_out || !k_out || rows == 0) return fail(c, ZYNFER_CU_INVALID, "bad arguments");
+    if ((uint64_t)pos0 + rows > c->d.max_seq_len) return fail(c, ZYNFER_CU_INVALID, "positions beyond max_seq_len");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    const ZynferCuModelDesc& m = c->d;
+    QkvArgs qa{};
+    qa.qkv = qkv; qa.T = (int)rows; qa.n_q = m.n_q; qa.n_kv = m.n_kv; qa.d = m.head_dim;
+    qa.q_norm = q_norm; qa.k_norm = k_norm; qa.eps = m.eps;
+    qa.rope = c->rope; qa.rope_max_pos = (int)m.max_seq_len;
+    qa.row_pos = nullptr; qa.pos0 = (int)pos0; qa.row_seq = nullptr; qa.seq0 = 0;
+    qa.kv_layer = nullptr; qa.block_table = nullptr; qa.max_blocks = 0; qa.n_pool_blocks = 0;
+    qa.q_out = q_out; qa.q_heads_major = 1; qa.k_stage = k_out; qa.v_stage = nullptr;
+    qa.stage_round_bf16 = 0; qa.err = c->derr;
+    launch_qkv_post(qa, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "norm/rope launch");
+    int rc = check_device_error(c);
+    if (rc) return rc;
+    set_path(c, "rmsnorm_qk_rope", 0, nullptr);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_swiglu(ZynferCuCtx* c, const float* gate, const float* up, uint64_t n, float* out) {
+    if (!c || c->device < 0) return ZYNFER_CU_INVALID;
+    if (!gate || !up || !out || n == 0) return fail(c, ZYNFER_CU_INVALID, "bad swiglu arguments");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    launch_silu_mul(gate, up, (size_t)n, out, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "swiglu launch");
+    set_path(c, "swiglu", 0, nullptr);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_alloc_events(const ZynferCuCtx* c, uint64_t* device, uint64_t* host) {
+    if (!c || !device || !host) return ZYNFER_CU_INVALID;
+    *device = c->dev_alloc_events;
+    *host = c->host_alloc_events;
+    return ZYNFER_CU_OK;
+}
+
 int zynfer_cu_prefill(ZynferCuCtx* c, uint32_t seq, const uint32_t* tokens, uint32_t n, float* last_logits,
                       uint32_t* argmax) {
     if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
@@ -1097,6 +1249,7 @@ int zynfer_cu_prefill(ZynferCuCtx* c, uint32_t seq, const uint32_t* tokens, uint
     const ZynferCuModelDesc& m = c->d;
     ZC_CHECK(c, cudaMemcpyAsync(c->ptok, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream), "prompt upload");
     cudaEventRecord(c->ev0, c->stream);
+    c->step_paths = 0;
     launch_embed(c->embed, c->sembed, c->wkind, c->ptok, n, m.hidden, m.vocab, c->px, c->derr, c->stream);
     enqueue_prefill_layers(c, seq, (int)n, 0, m.layers);
     linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, &c->tm_embed, m.vocab, m.hidden, c->px + (size_t)(n - 1) * m.hidden, 1,
@@ -1115,7 +1268,7 @@ int zynfer_cu_prefill(ZynferCuCtx* c, uint32_t seq, const uint32_t* tokens, uint
     c->last_step_ns = (uint64_t)(ms * 1e6);
     if (argmax) *argmax = c->hids[0];
     c->seq_len[seq] = n;
-    c->path = "prefill:simt";
+    set_path(c, "prefill", c->step_paths, nullptr);
     return ZYNFER_CU_OK;
 }
 
@@ -1135,15 +1288,18 @@ int zynfer_cu_decode_step(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* 
     ZC_CHECK(c, cudaMemsetAsync(c->dstep, 0, 4, c->stream), "step counter");
     const bool persistent = use_persistent(c, (int)batch);
     const bool eager = logits != nullptr || c->timing || persistent;
-    cudaEventRecord(c->ev0, c->stream);
-    if (eager) {
-        enqueue_decode(c, (int)batch, logits != nullptr);
-        c->path = persistent ? "decode:persistent" : (batch <= 8 ? "decode:gemv:eager" : "decode:gemm:eager");
-    } else {
-        cudaGraphExec_t g;
+    unsigned paths = 0;
+    if (!eager) {
+        GraphEntry g;
         if ((rc = get_graph(c, (int)batch, &g))) return rc;
-        ZC_CHECK(c, cudaGraphLaunch(g, c->stream), "graph launch");
-        c->path = batch <= 8 ? "decode:gemv:graph" : "decode:gemm:graph";
+        cudaEventRecord(c->ev0, c->stream);
+        ZC_CHECK(c, cudaGraphLaunch(g.exec, c->stream), "graph launch");
+        paths = g.paths;
+    } else {
+        cudaEventRecord(c->ev0, c->stream);
+        c->step_paths = 0;
+        enqueue_decode(c, (int)batch, logits != nullptr);
+        paths = c->step_paths;
     }
     cudaEventRecord(c->ev1, c->stream);
     cudaError_t e = cudaGetLastError();
@@ -1162,6 +1318,8 @@ int zynfer_cu_decode_step(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* 
         argmax[i] = c->hids[i];
         c->seq_len[seqs[i]] += 1;
     }
+    if (persistent) set_path(c, "decode", 0, "persistent");
+    else set_path(c, "decode", paths, eager ? "eager" : "graph");
     return ZYNFER_CU_OK;
 }
 
@@ -1182,13 +1340,15 @@ int zynfer_cu_generate(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* fir
     if ((rc = stage_batch(c, seqs, first, batch))) return rc;
     ZC_CHECK(c, cudaMemsetAsync(c->dstep, 0, 4, c->stream), "step counter");
     const bool persistent = use_persistent(c, (int)batch);
-    cudaGraphExec_t g = nullptr;
+    GraphEntry g;
     if (!c->timing && !persistent && (rc = get_graph(c, (int)batch, &g))) return rc;
+    c->step_paths = 0;
     cudaEventRecord(c->ev0, c->stream);
     for (uint32_t s = 0; s < steps; ++s) {
         if (c->timing || persistent) enqueue_decode(c, (int)batch, false);
-        else ZC_CHECK(c, cudaGraphLaunch(g, c->stream), "graph launch");
+        else ZC_CHECK(c, cudaGraphLaunch(g.exec, c->stream), "graph launch");
     }
+    const unsigned paths = (c->timing || persistent) ? c->step_paths : g.paths;
     cudaEventRecord(c->ev1, c->stream);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "generate launch");
@@ -1199,8 +1359,8 @@ int zynfer_cu_generate(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* fir
     c->last_step_ns = (uint64_t)(ms * 1e6 / steps);
     ZC_CHECK(c, cudaMemcpy(out_ids, c->dhist, (size_t)steps * batch * 4, cudaMemcpyDeviceToHost), "history");
     for (uint32_t i = 0; i < batch; ++i) c->seq_len[seqs[i]] += steps;
-    c->path = persistent ? std::string("generate:persistent")
-                         : std::string(batch <= 8 ? "generate:gemv" : "generate:gemm") + (c->timing ? ":eager" : ":graph");
+    if (persistent) set_path(c, "generate", 0, "persistent");
+    else set_path(c, "generate", paths, c->timing ? "eager" : "graph");
     return ZYNFER_CU_OK;
 }
 
@@ -1218,6 +1378,7 @@ int zynfer_cu_block_forward(ZynferCuCtx* c, uint32_t layer, uint32_t seq, const 
     if ((rc = upload_table_rows(c, &seq, 1))) return rc;
     const ZynferCuModelDesc& m = c->d;
     const int H = m.hidden;
+    c->step_paths = 0;
     if (pos0 == 0) {
         ZC_CHECK(c, cudaMemcpyAsync(c->px, x, (size_t)t * H * 4, cudaMemcpyHostToDevice, c->stream), "x upload");
         enqueue_prefill_layers(c, seq, (int)t, layer, layer + 1);
@@ -1254,7 +1415,7 @@ int zynfer_cu_block_forward(ZynferCuCtx* c, uint32_t layer, uint32_t seq, const 
     if (e != cudaSuccess) return cuda_fail(c, e, "block launch");
     if ((rc = check_device_error(c))) return rc;
     c->seq_len[seq] = pos0 + t;
-    c->path = pos0 == 0 ? "block:prefill" : "block:decode";
+    set_path(c, pos0 == 0 ? "block:prefill" : "block:decode", c->step_paths, nullptr);
     return ZYNFER_CU_OK;
 }
 
@@ -1289,7 +1450,7 @@ int zynfer_cu_linear(ZynferCuCtx* c, int wkind, const void* w, const float* scal
                          (int)batch, y, kEpiNone, nullptr, nullptr, nullptr, wk);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "linear launch");
-    c->path = p == kPathGemv ? "linear:gemv" : (p == kPathSimt ? "linear:simt" : "linear:tcgen05");
+    set_path(c, "linear", 1u << p, nullptr);
     return ZYNFER_CU_OK;
 }
 
@@ -1300,7 +1461,7 @@ int zynfer_cu_set_linear_path(ZynferCuCtx* c, const char* path) {
     else if (!strcmp(path, "simt")) c->path_policy = kPathSimt;
     else if (!strcmp(path, "tcgen05")) c->path_policy = kPathTc;
     else return fail(c, ZYNFER_CU_INVALID, std::string("unknown linear path ") + path);
-    for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);  // graphs bake the old choice
+    for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second.exec);  // graphs bake the old choice
     c->graphs.clear();
     return ZYNFER_CU_OK;
 }

@@ -79,6 +79,55 @@ void launch_fill(float* out, size_t n, float v, cudaStream_t st) {
     fill_kernel<<<grid_for(n), 256, 0, st>>>(out, n, v);
 }
 
+// Seeded stand-in for a prefilled cache of one sequence: positions [0, n) of
+// every layer. K (code 100) and V (code 101) of layer l draw from key(seed,
+// layer_stream(l, code)); element (kv head h, position p, dim j) is
+// normal(key, (h n + p) d + j, 1) rounded to bf16, written into the paged
+// block of position p at its swizzled place. One thread per 16-byte chunk
+// (8 dims) of one row.
+__global__ void kv_fill_kernel(uint16_t* __restrict__ kv, size_t kv_layer_elems, const int* __restrict__ table,
+                               int n_pool_blocks, int layers, int n_kv, int n, uint64_t seed, float k,
+                               uint32_t* err) {
+    constexpr int d = 128, chunks_per_row = d / 8;
+    const size_t total = (size_t)layers * 2 * n_kv * n * chunks_per_row;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % chunks_per_row);
+        size_t r = i / chunks_per_row;
+        const int p = (int)(r % n);
+        r /= n;
+        const int h = (int)(r % n_kv);
+        r /= n_kv;
+        const int which = (int)(r % 2);
+        const int l = (int)(r / 2);
+        const int blk = table[p / kKvBlock];
+        if (blk < 0 || blk >= n_pool_blocks) {
+            if (err) atomicOr(err, kErrBadIndex);
+            continue;
+        }
+        const uint64_t key = zs_key(seed, zs_layer_stream((uint32_t)l, (uint32_t)(100 + which)));
+        const uint64_t base = ((uint64_t)h * n + p) * d + 8 * c;
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const uint32_t lo = f32_to_bf16_rne(zs_normal(key, base + 2 * e, k));
+            const uint32_t hi = f32_to_bf16_rne(zs_normal(key, base + 2 * e + 1, k));
+            w[e] = lo | (hi << 16);
+        }
+        uint16_t* dst = kv + (size_t)l * kv_layer_elems + (((size_t)h * n_pool_blocks + blk) * 2 + which) * kKvBlock * d +
+                        kv_swizzle(p % kKvBlock, 8 * c);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+void launch_kv_fill(uint16_t* kv, size_t kv_layer_elems, const int* table_row, int n_pool_blocks, int layers,
+                    int n_kv, int n, uint64_t seed, uint32_t* err, cudaStream_t st) {
+    if (n <= 0) return;
+    const size_t total = (size_t)layers * 2 * n_kv * n * 16;
+    const float k = (float)(1.0 / ZS_IH4_SIGMA);
+    kv_fill_kernel<<<grid_for(total), 256, 0, st>>>(kv, kv_layer_elems, table_row, n_pool_blocks, layers, n_kv, n,
+                                                    seed, k, err);
+}
+
 // One warp per source row.
 __global__ void pack_q8_rows_kernel(const float* __restrict__ w, int rows, int cols,
                                     int8_t* __restrict__ q, float* __restrict__ scale,

@@ -104,7 +104,6 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-__device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 
 template <int WK>
 constexpr uint32_t make_idesc(int N) {
@@ -192,6 +191,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     unit_coords(u, mt, nt);
                     const int kb0 = 0, kb1 = nkb;
                     for (int kb = kb0; kb < kb1 && npre < STAGES; ++kb, ++npre) {
+                        if (a.stall && npre == 0) continue;  // stage 0 never arrives
                         mbar_arrive_expect_tx(&full[npre], STAGE);
                         tma_load_2d(smem + npre * STAGE, &tmA, kb * (WK == kWQ8 ? kKB : kKB / 2), mt * kBM,
                                     &full[npre]);
@@ -218,6 +218,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                         mbar_arrive_expect_tx(&full[s], STAGE);
                         tma_load_2d(as, &tmA, kx, mt * kBM, &full[s]);
                     }
+                    if (a.stall && i == 0) continue;
 #pragma unroll
                     for (int p = 0; p < P; ++p)
                         tma_load_2d(bs + p * NT * kKB, &tmB, kx, p * a.t_pad + nt * NT, &full[s]);

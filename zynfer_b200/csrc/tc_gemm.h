@@ -35,6 +35,7 @@ struct TcArgs {
     const float* resid;
     unsigned long long* argmax_keys;
     uint32_t* err;
+    int stall;  // fault injection: 1 = no CTA loads its first stage, so the MMA warp's bounded wait runs out
 };
 
 struct TcLaunch {
@@ -53,5 +54,7 @@ void launch_tc_gemm(const TcLaunch& L, cudaStream_t st);
 // (1 = use launch_tc_gemm), and its launcher (no argmax epilogue, T <= 64).
 int tc_cluster_size(int M, int T, int K, int wkind, int epi, int sms);
 void launch_tc_cluster(const TcLaunch& L, int S, cudaStream_t st);
+// The next allocation-free linear call launches with TcArgs::stall set.
+void static_linear_arm_stall();
 
 }  // namespace zc

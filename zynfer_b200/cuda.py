@@ -95,6 +95,7 @@ _SIGS = {
     "zynfer_cu_seq_reset": (C.c_int, [VP, U32]),
     "zynfer_cu_seq_len": (C.c_int, [VP, U32, C.POINTER(U32)]),
     "zynfer_cu_kv_read": (C.c_int, [VP, U32, U32, C.c_int, VP]),
+    "zynfer_cu_kv_fill_synthetic": (C.c_int, [VP, U32, U32, U64]),
     "zynfer_cu_prefill": (C.c_int, [VP, U32, VP, U32, VP, VP]),
     "zynfer_cu_decode_step": (C.c_int, [VP, VP, VP, U32, VP, VP]),
     "zynfer_cu_generate": (C.c_int, [VP, VP, VP, U32, U32, VP, C.POINTER(C.c_float)]),
@@ -104,6 +105,10 @@ _SIGS = {
     "zynfer_cu_set_decode_schedule": (C.c_int, [VP, C.c_char_p]),
     "zynfer_cu_phase_trace": (C.c_int, [VP, VP, C.c_int]),
     "zynfer_cu_linear_q8_static": (C.c_int, [VP, VP, VP, U32, U32, U32, VP, VP]),
+    "zynfer_cu_linear_q8_static_status": (C.c_int, [C.c_int]),
+    "zynfer_cu_attn_decode": (C.c_int, [VP, U32, VP, U32, VP, VP]),
+    "zynfer_cu_rmsnorm_qk_rope": (C.c_int, [VP, VP, U32, VP, VP, U32, VP, VP]),
+    "zynfer_cu_swiglu": (C.c_int, [VP, VP, VP, U64, VP]),
     "zynfer_cu_pack_q8": (C.c_int, [VP, VP, U32, U32, VP, VP]),
     "zynfer_cu_rmsnorm": (C.c_int, [VP, VP, VP, U32, U32, C.c_float, VP]),
     "zynfer_cu_set_timing": (C.c_int, [VP, C.c_int]),
@@ -111,6 +116,7 @@ _SIGS = {
     "zynfer_cu_last_step_ns": (U64, [VP]),
     "zynfer_cu_step_launches": (C.c_int, [VP]),
     "zynfer_cu_io_bytes": (C.c_int, [VP, C.POINTER(U64), C.POINTER(U64), C.c_int]),
+    "zynfer_cu_alloc_events": (C.c_int, [VP, C.POINTER(U64), C.POINTER(U64)]),
 }
 EXPORTS = tuple(_SIGS)
 
@@ -154,6 +160,21 @@ def linear_q8_static(w, scale, x, batch: int, m: int, k: int, y, stream=None):
     rc = lib().zynfer_cu_linear_q8_static(_ptr(w), _ptr(scale), _ptr(x), batch, m, k, _ptr(y), _ptr(stream))
     if rc != OK:
         raise _ERRORS.get(rc, CudaError)(f"zynfer_cu_linear_q8_static failed with status {rc}")
+
+
+def linear_q8_static_status(clear: bool = True) -> int:
+    """zynfer_cu_linear_q8_static_status: the status its device error word
+    holds (OK, or TIMEOUT when a bounded device wait ran out); call after
+    synchronising the stream the calls ran on."""
+    return int(lib().zynfer_cu_linear_q8_static_status(int(clear)))
+
+
+def arm_static_wait_fault():
+    """zynfer_cu_set_fail_at(NULL, "wait"): the next allocation-free linear
+    call skips its first K stage, so its bounded device waits run out."""
+    rc = lib().zynfer_cu_set_fail_at(None, b"wait")
+    if rc != OK:
+        raise _ERRORS.get(rc, CudaError)("zynfer_cu_set_fail_at(NULL, wait) failed")
 
 
 @dataclass
@@ -243,6 +264,16 @@ class Gpu:
         """"auto" | "kernels" | "persistent" (one cooperative kernel per decode step)."""
         self.check(lib().zynfer_cu_set_decode_schedule(self.h, schedule.encode()))
 
+    def swiglu(self, gate, up, n, out):
+        """siluMul (ops.zig:36-42) on device pointers."""
+        self.check(lib().zynfer_cu_swiglu(self.h, _ptr(gate), _ptr(up), n, _ptr(out)))
+
+    def alloc_events(self):
+        """(device, host) allocation events since model init."""
+        d, h = U64(), U64()
+        self.check(lib().zynfer_cu_alloc_events(self.h, C.byref(d), C.byref(h)))
+        return int(d.value), int(h.value)
+
     def pack_q8(self, w, rows, cols, q, scale):
         self.check(lib().zynfer_cu_pack_q8(self.h, _ptr(w), rows, cols, _ptr(q), _ptr(scale)))
 
@@ -330,6 +361,20 @@ class Model:
         n = U32()
         self.gpu.check(lib().zynfer_cu_seq_len(self.gpu.h, seq, C.byref(n)))
         return int(n.value)
+
+    def kv_fill_synthetic(self, seq: int, n: int, seed: int):
+        """Reset `seq` and fill positions [0, n) of every layer with the seeded stand-in K/V."""
+        self.gpu.check(lib().zynfer_cu_kv_fill_synthetic(self.gpu.h, seq, n, seed))
+
+    def attn_decode(self, layer: int, seqs, qkv, out):
+        """Decode attention of `layer` (device qkv [B][(n_q + 2 n_kv) d] -> out [B][n_q][d])."""
+        s = np.ascontiguousarray(seqs, np.uint32)
+        self.gpu.check(lib().zynfer_cu_attn_decode(self.gpu.h, layer, _ptr(s), s.size, _ptr(qkv), _ptr(out)))
+
+    def rmsnorm_qk_rope(self, qkv, rows: int, q_norm, k_norm, pos0: int, q_out, k_out):
+        """Per-head q/k RMSNorm + RoPE of `rows` tokens (device pointers, heads-major outputs)."""
+        self.gpu.check(lib().zynfer_cu_rmsnorm_qk_rope(self.gpu.h, _ptr(qkv), rows, _ptr(q_norm), _ptr(k_norm),
+                                                       pos0, _ptr(q_out), _ptr(k_out)))
 
     def kv(self, seq: int, layer: int, which_v: bool):
         a = self.arch
