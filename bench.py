@@ -30,6 +30,26 @@ and 151936x1024 at 1 and 8 activation rows, through zynfer_cu_linear with
 device pointers. Each call reads another of R weight copies (R x m x k above
 twice the L2), CUDA events around every call on the library's stream give
 its time, and achieved GB/s = (m k + 4 m + 4 B k + 4 B m) / time.
+
+At one GPU the line also carries two more workloads of the same model:
+* "batch1" (one sequence, context 2048, 256 greedy tokens on the device):
+  ms/token, tok/s and the fraction of the HBM roofline (weights + KV bytes
+  per token / measured peak), with the argmax agreement of every timed token
+  against the oracle (teacher-forced). The context is the seeded stand-in
+  cache of zynfer_cu_kv_fill_synthetic (the oracle fills the same values):
+  the same bytes and kernels as after a 2048-token prefill, without a CPU
+  prefill.
+* "prefill" (512 seeded tokens through a bf16-weight model, f32
+  accumulate): ms per prefill from CUDA events, TFLOP/s of the algorithmic
+  FLOPs against the measured bf16 peak, and the last-token logits of the
+  reference tools' golden fixture prompt on the same kind of model.
+
+    python bench.py --case SEQS,CTX,LAYERS [--steps K] [--warmup W] [--schedule S]
+                    [--path P] [--weights q8|bf16] [--window decode|prefill] [--phases]
+
+times one fixed batch of SEQS sequences prefilled with CTX seeded tokens on
+a model of LAYERS layers (a small case for profiler captures): K greedy steps
+on the device, then per-kernel-class CUDA events; one JSON line.
 """
 from __future__ import annotations
 
@@ -50,6 +70,19 @@ METRIC = "Qwen3-0.6B int8 decode tok/s"
 N_SEQS = 64
 SEED = 20250601
 KV_BYTES_PER_TOKEN_LAYER = 2 * 8 * 128 * 2  # K + V, 8 kv heads, d = 128, bf16
+# Qwen3-0.6B int8 weights read per decode token: 28 x (QKV 4096x1024 + O
+# 1024x2048 + gate/up 6144x1024 + down 1024x3072) int8, their f32 row scales,
+# the four norm vectors per layer, the tied 151936x1024 LM head with its
+# scales, and the final norm.
+LINEAR_PARAMS_PER_LAYER = 4096 * 1024 + 1024 * 2048 + 6144 * 1024 + 1024 * 3072
+WEIGHT_BYTES_PER_TOKEN = (28 * (LINEAR_PARAMS_PER_LAYER + 4 * (4096 + 1024 + 6144 + 1024) + 4 * (2 * 1024 + 2 * 128))
+                          + 151936 * 1024 + 4 * 151936 + 4 * 1024)
+BATCH1_CTX, BATCH1_STEPS = 2048, 256
+PREFILL_T = 512
+GOLDEN_SEED = 20251201
+# An argmax differs from the oracle's only at a near tie: the oracle's top two
+# logits within this bound (the stated bf16-KV logit tolerance of the tests).
+ARGMAX_TIE = 1.5e-2
 # DRAM bytes (read + write) per algorithmic byte of attn_decode_kernel, from one
 # ncu capture of 32 sequences at context 2048 (profiles/attn_decode_b32_ctx2048.txt:
 # 275.1 MB for 269.3 MB); the traffic grows with the KV bytes, so a launch of this
@@ -69,6 +102,17 @@ def parse():
     ap.add_argument("--sweep", choices=["gemv"], default=None)
     ap.add_argument("--sweep-calls", type=int, default=200)
     ap.add_argument("--sweep-shape", default=None, help="one shape of the sweep, as MxK")
+    ap.add_argument("--no-batch1", action="store_true", help="skip the one-sequence context-2048 workload")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the 512-token bf16 prefill workload")
+    ap.add_argument("--batch1-steps", type=int, default=BATCH1_STEPS)
+    ap.add_argument("--case", default=None, help="SEQS,CTX,LAYERS: one fixed decode batch (profiling case)")
+    ap.add_argument("--schedule", default="auto", help="--case: decode schedule (auto, kernels, persistent)")
+    ap.add_argument("--path", default="auto", help="--case: linear kernel family (auto, gemv, tcgen05, simt)")
+    ap.add_argument("--weights", default="q8", choices=["q8", "bf16"], help="--case: weight storage")
+    ap.add_argument("--window", default="decode", choices=["decode", "prefill"],
+                    help="--case: what runs between cudaProfilerStart/Stop")
+    ap.add_argument("--phases", action="store_true",
+                    help="--case with the persistent schedule: per-phase times from CTA 0's phase trace")
     return ap.parse_args()
 
 
@@ -84,6 +128,16 @@ def measured_peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def measured_peak_tflops():
+    """Burst bf16 tensor peak (a prefill is timed alone): measured, else the fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
 
 
 class ClockSampler:
@@ -138,12 +192,20 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(mean_ctx: int, n_seqs: int, steps: int, threads: int, warmup: int = 1):
+def oracle_model(threads: int):
+    """The oracle's int8 Qwen3-0.6B on the benchmark's seeded weights."""
+    from oracle import oracle as O
+    return O.Model(O.QWEN3_0_6B, O.W_Q8, kv_bf16=True, seed=SEED, w_std=0.02, norm_std=0.0, threads=threads)
+
+
+def cpu_baseline(mean_ctx: int, n_seqs: int, steps: int, threads: int, warmup: int = 1, m=None):
     """Oracle int8 decode (the reference path restated in C, all host threads
     splitting each matvec's rows) on n_seqs sequences at context mean_ctx,
     whose caches are filled with seeded values instead of a CPU prefill."""
-    from oracle import oracle as O
-    m = O.Model(O.QWEN3_0_6B, O.W_Q8, kv_bf16=True, seed=SEED, w_std=0.02, norm_std=0.0, threads=threads)
+    own = m is None
+    if own:
+        m = oracle_model(threads)
+    m.set_threads(threads)
     sessions = []
     for i in range(n_seqs):
         s = m.session(mean_ctx + steps + warmup + 2)
@@ -160,7 +222,8 @@ def cpu_baseline(mean_ctx: int, n_seqs: int, steps: int, threads: int, warmup: i
     dt = time.perf_counter() - t0
     for s in sessions:
         s.close()
-    m.close()
+    if own:
+        m.close()
     return n_seqs * steps / dt, dt
 
 
@@ -190,6 +253,95 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_batch1(model, gpu, oracle, slot: int, steps: int, warmup: int, peak: float):
+    """One sequence at context 2048, `steps` greedy tokens on the device (the
+    one-row GEMV graph), timed with CUDA events; then the oracle, fed the
+    GPU's tokens, checks every timed argmax (a flip only at a near tie)."""
+    import numpy as np
+
+    TIE = ARGMAX_TIE
+    first = 4242
+    model.kv_fill_synthetic(slot, BATCH1_CTX, SEED)
+    model.generate([slot], [first], warmup)                 # captures the batch-1 graph
+    model.kv_fill_synthetic(slot, BATCH1_CTX, SEED)         # back to context 2048
+    out, ms = model.generate([slot], [first], steps)
+    path = gpu.last_path
+    ids = out[:, 0]
+    agree = near_ties = 0
+    if oracle is not None:
+        s = oracle.session(BATCH1_CTX + steps + 2)
+        s.fill_kv(BATCH1_CTX, SEED)
+        _, logits = s.greedy(first, steps, teacher=ids, want_logits=True)
+        s.close()
+        for i in range(steps):
+            if int(np.argmax(logits[i])) == int(ids[i]):
+                agree += 1
+            else:
+                top2 = np.sort(logits[i])[-2:]
+                if top2[1] - top2[0] <= TIE and logits[i][int(ids[i])] >= top2[1] - TIE:
+                    near_ties += 1
+    mean_kv = BATCH1_CTX + (steps + 1) / 2.0                 # step i reads 2048 + i + 1 positions
+    bytes_tok = WEIGHT_BYTES_PER_TOKEN + mean_kv * 28 * KV_BYTES_PER_TOKEN_LAYER
+    ms_tok = ms / steps
+    gbs = bytes_tok / (ms_tok / 1e3) / 1e9
+    return {"workload": f"one sequence, context {BATCH1_CTX}, {steps} greedy tokens (int8 weights, bf16 KV)",
+            "ms_per_token": round(ms_tok, 4), "tok_s": round(1e3 / ms_tok, 1),
+            "roofline": {"bound": "hbm", "bytes_per_token": int(bytes_tok), "achieved": round(gbs, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4)},
+            "argmax_vs_oracle": None if oracle is None else
+            {"tokens": steps, "equal": agree, "near_tie_flips": near_ties, "mismatch": steps - agree - near_ties},
+            "context_source": "seeded stand-in cache of 2048 positions (zynfer_cu_kv_fill_synthetic; the "
+                              "oracle fills the same bf16 values)",
+            "path": path}
+
+
+def prefill_flops(T: int) -> float:
+    """Algorithmic FLOPs of a T-token prefill: every linear of every layer on
+    T rows, causal attention (QK and PV per visible pair), LM head on the last row."""
+    linear = 2.0 * 28 * LINEAR_PARAMS_PER_LAYER * T
+    attn = 28 * 16 * (T * (T + 1) / 2) * 128 * 4
+    return linear + attn + 2.0 * 151936 * 1024
+
+
+def run_prefill(local: int, runs: int = 5):
+    """512 seeded tokens through a bf16-weight Qwen3-0.6B (f32 accumulate),
+    CUDA-event time per prefill (median of `runs`), and the golden fixture."""
+    import numpy as np
+
+    from zynfer_b200 import cuda as zc
+    from zynfer_b200 import workload
+    gpu = zc.Gpu(local)
+    try:
+        m = zc.Model(gpu, zc.QWEN3_0_6B, zc.W_BF16, max_batch=1, max_seqs=1, max_seq_len=PREFILL_T,
+                     max_prefill=PREFILL_T, prefill_kv_f32=True)
+        m.fill_synthetic(GOLDEN_SEED, 0.02, 0.1)
+        ids = workload.tokens(PREFILL_T, SEED, 3)
+        for _ in range(2):
+            m.prefill(0, ids, want_logits=False)
+        times = []
+        for _ in range(runs):
+            m.prefill(0, ids, want_logits=False)
+            times.append(gpu.last_step_ns / 1e6)
+        path = gpu.last_path
+        ms = statistics.median(times)
+        g = np.load(os.path.join(ROOT, "tests", "golden", "qwen3_bf16_bos23.npz"))
+        logits, _ = m.prefill(0, g["tokens"])
+        err = max(float(np.max(np.abs(g["np_sample_vals"] - logits[g["np_sample_idx"]]))),
+                  float(np.max(np.abs(g["np_top_vals"] - logits[g["np_top_ids"]]))))
+    finally:
+        gpu.close()
+    flops = prefill_flops(PREFILL_T)
+    tf = flops / (ms / 1e3) / 1e12
+    peak, kind = measured_peak_tflops()
+    return {"workload": f"{PREFILL_T}-token prefill, bf16 weights, f32 accumulate, last-token logits",
+            "ms": round(ms, 4), "runs_ms": [round(t, 4) for t in times],
+            "roofline": {"bound": "tensor", "flops": flops, "achieved": round(tf, 1), "peak": peak,
+                         "peak_kind": kind, "unit": "TFLOP/s", "frac": round(tf / peak, 4)},
+            "golden_fixture": {"prompt": [int(t) for t in g["tokens"]], "max_abs_vs_reference_numpy": err,
+                               "bound": 2e-3, "ok": err <= 2e-3},
+            "path": path}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -212,7 +364,7 @@ def run_ours(args):
     total_steps = args.warmup + args.steps + args.e2e_steps + args.profile_steps
     mine = shard.assign_sequences(lens, world, total_steps)[rank]
     B = len(mine)
-    max_len = max(lens[i] for i in mine) + total_steps + 16
+    max_len = max(max(lens[i] for i in mine) + total_steps + 16, BATCH1_CTX + args.batch1_steps + 64)
     gpu = zc.Gpu(local)
     model = zc.Model(gpu, zc.QWEN3_0_6B, zc.W_Q8, max_batch=B, max_seqs=B, max_seq_len=max_len,
                      max_prefill=4096)
@@ -240,6 +392,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
     clk = clocks.stop()
+    timed_path = gpu.last_path  # the kernels of the timed steps (the graph), before any instrumented pass
     barrier()
     nxt = out[-1].tolist()
     t_max = shard.max_over_ranks(dev_ms, dev)
@@ -262,13 +415,14 @@ def run_ours(args):
     d2h_all = shard.sum_over_ranks(d2h, dev) / max(1, args.e2e_steps)
     e2e_value = N_SEQS * args.e2e_steps / e2e_max
 
-    # instrumented pass: CUDA events around every attention launch
+    # instrumented pass: CUDA events around every kernel class
     ctx_prof = [model.seq_len(s) for s in slots]
     gpu.set_timing(True)
     model.generate(slots, nxt, args.profile_steps)
     n_attn, ms_attn = gpu.kernel_time(zc.K_ATTN)
     n_lin, ms_lin = gpu.kernel_time(zc.K_LINEAR)
     n_lm, ms_lm = gpu.kernel_time(zc.K_LMHEAD)
+    n_oth, ms_oth = gpu.kernel_time(zc.K_OTHER)
     gpu.set_timing(False)
     # algorithmic bytes per attention launch (one layer): K+V of every cached
     # position (bf16) + q in and attention out (f32), averaged over the pass
@@ -278,14 +432,31 @@ def run_ours(args):
     achieved = attn_bytes / (attn_avg_ms / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
     achieved_all = shard.sum_over_ranks(achieved, dev) / world
+    per_step = lambda v: round(v / args.profile_steps, 4)  # noqa: E731
+    mine_row = [float(B), dev_ms / args.steps, ms_attn / args.profile_steps, ms_lin / args.profile_steps,
+                ms_lm / args.profile_steps, float(sum(ctx_before)) / max(1, B)]
+    rows = shard.gather_over_ranks(mine_row, dev)
 
-    cpu = None
+    cpu = batch1 = prefill = None
+    oracle = None
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline and args.no_batch1):
+        oracle = oracle_model(os.cpu_count() or 1)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         mean_ctx = int(round(sum(ctx_before) / len(ctx_before)))
         threads = os.cpu_count() or 1
-        v, dt = cpu_baseline(mean_ctx, 2, 12, threads)
+        v, dt = cpu_baseline(mean_ctx, 2, 12, threads, m=oracle)
+        v1, dt1 = cpu_baseline(mean_ctx, 1, 3, 1, m=oracle)
         cpu = {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"2 sequences x 12 greedy steps at context {mean_ctx} (caches seeded, no CPU prefill)"}
+               "sample": f"2 sequences x 12 greedy steps at context {mean_ctx} (caches seeded, no CPU prefill)",
+               "single_thread": {"value": round(v1, 4), "unit": "tok/s", "cores": 1,
+                                 "sample": f"1 sequence x 3 greedy steps at context {mean_ctx}"}}
+    if rank == 0 and world == 1 and not args.no_batch1:
+        batch1 = run_batch1(model, gpu, oracle, 0, args.batch1_steps, max(3, args.warmup), peak)
+    if oracle is not None:
+        oracle.set_threads(1)
+        oracle.close()
+    if rank == 0 and world == 1 and not args.no_prefill:
+        prefill = run_prefill(local)
 
     if rank == 0:
         mean_ctx = sum(ctx_before) / len(ctx_before)
@@ -312,16 +483,121 @@ def run_ours(args):
                          "launches_timed": n_attn,
                          "note": "CUDA events around each attention launch in an instrumented pass of "
                                  f"{args.profile_steps} steps right after the timed region"},
-            "kernel_ms_per_step": {"attention": round(ms_attn / args.profile_steps, 4),
-                                   "linear": round(ms_lin / args.profile_steps, 4),
-                                   "lm_head": round(ms_lm / args.profile_steps, 4)},
+            "kernel_ms_per_step": {"attention": per_step(ms_attn), "linear": per_step(ms_lin),
+                                   "lm_head": per_step(ms_lm), "other": per_step(ms_oth)},
+            "per_rank": [{"rank": r, "batch": int(row[0]), "ms_per_step": round(row[1], 4),
+                          "attention_ms": round(row[2], 4), "linear_ms": round(row[3], 4),
+                          "lm_head_ms": round(row[4], 4), "mean_context": round(row[5], 1)}
+                         for r, row in enumerate(rows)],
             "cpu_baseline": cpu,
             "clocks": clk, "gpu_launches": launches, "prefill_s": round(prefill_s, 2),
-            "path": gpu.last_path,
+            "path": timed_path,
         }
+        if batch1 is not None:
+            line["batch1"] = batch1
+        if prefill is not None:
+            line["prefill"] = prefill
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    gpu.close()
+
+
+KV_BYTES_PER_TOKEN_HEAD = 2 * 128 * 2  # K and V rows, bf16
+
+
+def phase_breakdown(trace, layers: int) -> dict:
+    """Mean per-layer microseconds of each phase of the last persistent step,
+    as seen by CTA 0: "work" runs from the phase's start (its input staged)
+    to its end (its outputs written), "wait" from its end to the next
+    phase's start (the other CTAs' outputs arriving)."""
+    import numpy as np
+
+    t = trace.astype(np.int64)
+    P = 5 * layers + 1
+    if t.size < 4 + 10 * layers:
+        return {}
+    st, en = t[1:2 * P:2], t[2:2 * P + 1:2]
+    nxt = np.append(st[1:], t[3 + 2 * (P - 1)])
+    out = {}
+    for k, name in enumerate(("qkv", "attention", "o", "gate_up", "down")):
+        idx = np.arange(k, 5 * layers, 5)
+        out[name] = {"work": round(float(np.mean(en[idx] - st[idx])) / 1e3, 2),
+                     "wait": round(float(np.mean(nxt[idx] - en[idx])) / 1e3, 2)}
+    out["lm_head"] = {"work": round(float(en[-1] - st[-1]) / 1e3, 2),
+                      "finish": round(float(t[3 + 2 * (P - 1)] - en[-1]) / 1e3, 2)}
+    return out
+
+
+def run_case(args):
+    """One fixed decode batch: SEQS sequences prefilled with CTX seeded tokens
+    on a model of LAYERS layers (fewer layers keep a profiler capture of one
+    layer's kernels to a few GB). Times `steps` greedy steps on the device,
+    then every kernel class with per-launch events. The timed steps (or, with
+    --window prefill, one more prefill) run between cudaProfilerStart/Stop,
+    so a profiler started with --profile-from-start off sees only them."""
+    import dataclasses
+
+    import torch
+
+    from zynfer_b200 import cuda as zc
+    from zynfer_b200 import workload
+
+    seqs, ctx, layers = (int(v) for v in args.case.split(","))
+    arch = dataclasses.replace(zc.QWEN3_0_6B, layers=layers)
+    B = seqs
+    total = args.warmup + 2 * args.steps + 2
+    gpu = zc.Gpu(0)
+    wk = zc.W_Q8 if args.weights == "q8" else zc.W_BF16
+    model = zc.Model(gpu, arch, wk, max_batch=B, max_seqs=B, max_seq_len=ctx + total + 16, max_prefill=ctx)
+    model.fill_synthetic(1, 0.02, 0.0)
+    gpu.set_linear_path(args.path)
+    gpu.set_decode_schedule(args.schedule)
+    first = [model.prefill(s, workload.prompt(s, ctx, 1), want_logits=False) for s in range(B)]
+    if args.window == "prefill":
+        gpu.sync()
+        torch.cuda.profiler.start()
+        first[0] = model.prefill(0, workload.prompt(0, ctx, 1), want_logits=False)
+        gpu.sync()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"prefill_tokens": ctx, "layers": layers, "weights": args.weights,
+                          "prefill_ms": round(gpu.last_step_ns / 1e6, 4), "path": gpu.last_path}), flush=True)
+        gpu.close()
+        return
+    slots = list(range(B))
+    out, _ = model.generate(slots, first, args.warmup)
+    nxt = out[-1].tolist()
+    gpu.sync()
+
+    torch.cuda.profiler.start()
+    out, ms = model.generate(slots, nxt, args.steps)
+    torch.cuda.profiler.stop()
+    path = gpu.last_path
+    nxt = out[-1].tolist()
+
+    ctxs = [model.seq_len(s) for s in slots]
+    gpu.set_timing(True)
+    model.generate(slots, nxt, args.steps)
+    times = {name: gpu.kernel_time(cls) for name, cls in
+             (("attention", zc.K_ATTN), ("linear", zc.K_LINEAR), ("lm_head", zc.K_LMHEAD), ("other", zc.K_OTHER))}
+    phases = phase_breakdown(gpu.phase_trace(), layers) if args.phases and args.schedule == "persistent" else None
+    gpu.set_timing(False)
+
+    kv_tok = sum(sum(c + 1 + s for c in ctxs) for s in range(args.steps)) / args.steps
+    attn_bytes = kv_tok * KV_BYTES_PER_TOKEN_HEAD * arch.n_kv + B * 2 * arch.n_q * arch.head_dim * 4
+    n_attn, ms_attn = times["attention"]
+    line = {
+        "seqs": B, "ctx": ctx, "layers": layers, "steps": args.steps, "path": path,
+        "ms_per_step": round(ms / args.steps, 4), "tok_s": round(B * args.steps / (ms / 1e3), 1),
+        "launches_per_step": gpu.step_launches,
+        "kernel_ms_per_step": {k: round(v[1] / args.steps, 4) for k, v in times.items()},
+        "launches": {k: v[0] for k, v in times.items()},
+        "attn_bytes_per_launch": int(attn_bytes),
+        "attn_gbs": round(attn_bytes / (ms_attn / max(1, n_attn) / 1e3) / 1e9, 1) if n_attn else None,
+    }
+    if phases:
+        line["phases_us"] = phases
+    print(json.dumps(line), flush=True)
     gpu.close()
 
 
@@ -406,6 +682,9 @@ def main():
     args = parse()
     if args.sweep == "gemv":
         run_gemv_sweep(args)
+        return
+    if args.case:
+        run_case(args)
         return
     if args.impl == "reference":
         run_reference(args)

@@ -1,5 +1,7 @@
-"""CPU checks of bench.py's int8 linear sweep mode (no GPU): the shapes it
-covers and its CPU leg (the oracle's matvecQ8 / matmulQ8, ops.zig:181-228)."""
+"""CPU checks of bench.py (no GPU): the int8 linear sweep mode (the shapes it
+covers and its CPU leg, the oracle's matvecQ8 / matmulQ8, ops.zig:181-228),
+the byte and FLOP counts behind the batch-1 and prefill roofline figures, and
+the --case arguments."""
 import sys
 
 import bench
@@ -32,3 +34,28 @@ def test_sweep_arguments(monkeypatch):
 def test_cpu_leg_times_one_and_eight_rows():
     assert 0.0 < bench.cpu_linear_us(1024, 1024, 1, budget_s=0.05)
     assert 0.0 < bench.cpu_linear_us(1024, 1024, 8, budget_s=0.05)
+
+
+def test_decode_bytes_per_token():
+    # 598.2 MB of int8 weights, scales and norms per token; KV 114,688 B per position
+    assert abs(bench.WEIGHT_BYTES_PER_TOKEN / 1e6 - 598.2) < 0.1
+    assert 28 * bench.KV_BYTES_PER_TOKEN_LAYER == 114688
+    # one sequence at context 2048 + 256 steps: mean 2176.5 positions -> 847.8 MB per token
+    mean_kv = bench.BATCH1_CTX + (bench.BATCH1_STEPS + 1) / 2.0
+    assert mean_kv == 2176.5
+    assert abs((bench.WEIGHT_BYTES_PER_TOKEN + mean_kv * 114688) / 1e6 - 847.8) < 0.1
+
+
+def test_prefill_flops_512():
+    # linears 2 x 440.4 M params x 512, causal attention 30.1 GFLOP, LM head on the last row
+    f = bench.prefill_flops(512)
+    assert abs(f / 1e9 - 481.4) < 0.5
+    assert 28 * bench.LINEAR_PARAMS_PER_LAYER == 440401920
+
+
+def test_case_arguments(monkeypatch):
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--case", "32,2048,2", "--steps", "2", "--warmup", "3",
+                                      "--schedule", "persistent", "--phases"])
+    a = bench.parse()
+    assert a.case == "32,2048,2" and a.steps == 2 and a.schedule == "persistent" and a.phases
+    assert tuple(int(v) for v in a.case.split(",")) == (32, 2048, 2)

@@ -50,9 +50,10 @@ def _worker(rank, world, port, q):
     mine = shard.assign_sequences(lens, world, 136)[rank]
     t = shard.max_over_ranks(10.0 + rank)
     s = shard.sum_over_ranks(float(len(mine)))
+    rows = shard.gather_over_ranks([float(rank), float(len(mine)), 0.5])
     dist.barrier()
     dist.destroy_process_group()
-    q.put((rank, mine, t, s))
+    q.put((rank, mine, t, s, rows))
 
 
 def test_two_rank_gloo_max_over_ranks():
@@ -70,3 +71,5 @@ def test_two_rank_gloo_max_over_ranks():
     assert res[0][2] == res[1][2] == 11.0       # slowest rank sets the time
     assert res[0][3] == res[1][3] == 64.0       # every sequence is somewhere
     assert sorted(res[0][1] + res[1][1]) == list(range(64))
+    for r in res:                                # per-rank rows reach every rank in rank order
+        assert r[4] == [[0.0, 32.0, 0.5], [1.0, 32.0, 0.5]]
