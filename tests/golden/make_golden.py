@@ -15,7 +15,7 @@ GPU machines do not have). Steps:
    final-normed row, the top-64 logits, 8192 strided logits and the logits'
    sum / sum of squares, from both tools.
 
-    python tests/golden/make_golden.py [--reference /root/reference] [--work /tmp/zg]
+    python tests/golden/make_golden.py --reference <reference checkout> [--work /tmp/zg]
 """
 from __future__ import annotations
 
@@ -93,7 +93,7 @@ def summarise(logits: np.ndarray):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, required=True, help="checkout of the Zynfer reference")
     ap.add_argument("--work", type=Path, default=Path("/tmp/zynfer_golden"))
     args = ap.parse_args()
     ck = args.work / "ckpt"
