@@ -131,6 +131,57 @@ ZYNFER_CU_API int zynfer_cu_fill_synthetic(ZynferCuCtx *ctx, uint64_t seed, floa
 ZYNFER_CU_API int zynfer_cu_download_q8(ZynferCuCtx *ctx, const char *name, int8_t *q, float *scale, uint64_t rows,
                           uint64_t cols);
 
+/* ---- .zynfer artifacts (src/model/artifact.zig) ----
+ * The reference's file format (artifact.zig:42-66: 88-byte header, 116-byte
+ * model record, 120-byte tensor entries, 64-byte-aligned payload, SHA-256 of
+ * the file) with one addition in format version 2: dtype 3 = int8, whose
+ * packRowQ8 row scales are the f32 tensor "<name>.scale" [rows]. Version-1
+ * files (f32 / f16 / bf16) load unchanged. */
+typedef struct ZynferCuArtifact ZynferCuArtifact;
+enum { ZYNFER_CU_DT_F32 = 0, ZYNFER_CU_DT_F16 = 1, ZYNFER_CU_DT_BF16 = 2, ZYNFER_CU_DT_I8 = 3 };
+typedef struct ZynferCuArtifactMeta {   /* Meta (artifact.zig:68-99) */
+    char model_id[64];
+    uint32_t format_version;
+    uint32_t vocab, hidden, inter, layers, n_q, n_kv, head_dim, max_pos, bos, eos;
+    float rope_theta, rms_norm_eps;
+    uint32_t tie_word_embeddings;
+    uint32_t tensor_count;
+    uint64_t file_bytes;
+} ZynferCuArtifactMeta;
+typedef struct ZynferCuTensorInfo {     /* TensorEntry (artifact.zig:124-150) */
+    char name[64];
+    uint32_t tensor_id, dtype, rank;
+    uint32_t shape[8];
+    uint64_t nbytes;
+    const void *data;                   /* inside the mapped file, valid until close */
+} ZynferCuTensorInfo;
+/* Artifact.loadFile (artifact.zig:394-433) + validate (artifact.zig:487-532):
+ * maps the file read-only and checks it in the reference's order. *out is set
+ * even on failure, to a handle whose zynfer_cu_artifact_error names the
+ * reference's error (InvalidMagic, UnsupportedVersion, BadEndian, BadHeader,
+ * BadAlignment, Truncated, ChecksumMismatch, InvalidRank, InvalidDtype,
+ * InvalidName, DuplicateTensorId, Overflow for files over 4 GiB); close it
+ * either way. Needs no GPU. */
+ZYNFER_CU_API int zynfer_cu_artifact_open(const char *path, ZynferCuArtifact **out);
+ZYNFER_CU_API void zynfer_cu_artifact_close(ZynferCuArtifact *art);
+ZYNFER_CU_API const char *zynfer_cu_artifact_error(const ZynferCuArtifact *art);
+ZYNFER_CU_API int zynfer_cu_artifact_meta(const ZynferCuArtifact *art, ZynferCuArtifactMeta *out);
+/* Directory entry `index` (0 .. tensor_count - 1). */
+ZYNFER_CU_API int zynfer_cu_artifact_tensor(const ZynferCuArtifact *art, uint32_t index, ZynferCuTensorInfo *out);
+/* Artifact.findById (artifact.zig:449-458) and findByName (:466-471). */
+ZYNFER_CU_API int zynfer_cu_artifact_find_id(const ZynferCuArtifact *art, uint32_t tensor_id, ZynferCuTensorInfo *out);
+ZYNFER_CU_API int zynfer_cu_artifact_find_name(const ZynferCuArtifact *art, const char *name, ZynferCuTensorInfo *out);
+/* Meta.toArch (artifact.zig:101-121): the architecture fields of a model
+ * descriptor (vocab .. theta); the runtime sizing fields are left as they are. */
+ZYNFER_CU_API int zynfer_cu_model_desc_from_artifact(const ZynferCuArtifact *art, ZynferCuModelDesc *desc);
+/* Weights.load (qwen_weights.zig:61-175) onto the device: every tensor of an
+ * initialised model of the artifact's architecture, by HF name, from the
+ * mapping (f32 and bf16 through zynfer_cu_upload_f32 / _bf16, int8 with its
+ * scales through zynfer_cu_upload_q8). A missing tensor is INVALID
+ * ("TensorNotFound: <name>"), f16 INVALID ("InvalidDtype"), an untied LM head
+ * UNSUPPORTED. */
+ZYNFER_CU_API int zynfer_cu_load_artifact(ZynferCuCtx *ctx, const ZynferCuArtifact *art);
+
 /* ---- sequences (KvCache.reset/used, kv_cache.zig:41-47) ---- */
 ZYNFER_CU_API int zynfer_cu_seq_reset(ZynferCuCtx *ctx, uint32_t seq);
 ZYNFER_CU_API int zynfer_cu_seq_len(const ZynferCuCtx *ctx, uint32_t seq, uint32_t *len);

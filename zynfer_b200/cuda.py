@@ -117,6 +117,15 @@ _SIGS = {
     "zynfer_cu_step_launches": (C.c_int, [VP]),
     "zynfer_cu_io_bytes": (C.c_int, [VP, C.POINTER(U64), C.POINTER(U64), C.c_int]),
     "zynfer_cu_alloc_events": (C.c_int, [VP, C.POINTER(U64), C.POINTER(U64)]),
+    "zynfer_cu_artifact_open": (C.c_int, [C.c_char_p, C.POINTER(VP)]),
+    "zynfer_cu_artifact_close": (None, [VP]),
+    "zynfer_cu_artifact_error": (C.c_char_p, [VP]),
+    "zynfer_cu_artifact_meta": (C.c_int, [VP, VP]),
+    "zynfer_cu_artifact_tensor": (C.c_int, [VP, U32, VP]),
+    "zynfer_cu_artifact_find_id": (C.c_int, [VP, U32, VP]),
+    "zynfer_cu_artifact_find_name": (C.c_int, [VP, C.c_char_p, VP]),
+    "zynfer_cu_model_desc_from_artifact": (C.c_int, [VP, C.POINTER(ModelDesc)]),
+    "zynfer_cu_load_artifact": (C.c_int, [VP, VP]),
 }
 EXPORTS = tuple(_SIGS)
 
@@ -329,6 +338,10 @@ class Model:
         gpu.check(lib().zynfer_cu_model_init(gpu.h, C.byref(self.desc)))
 
     # weights
+    def load_artifact(self, art):
+        """Every tensor of an open `.zynfer` artifact (zynfer_b200.artifact.Artifact) to the device."""
+        self.gpu.check(lib().zynfer_cu_load_artifact(self.gpu.h, art.h))
+
     def fill_synthetic(self, seed: int, w_std: float = 0.02, norm_std: float = 0.0):
         self.gpu.check(lib().zynfer_cu_fill_synthetic(self.gpu.h, seed, w_std, norm_std))
 
