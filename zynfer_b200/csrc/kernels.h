@@ -32,6 +32,7 @@ struct LinearArgs {
     const float* norm_w = nullptr; // optional RMSNorm applied to x rows first (GEMV only)
     float eps = 1e-6f;
     unsigned long long* argmax_keys = nullptr;  // [N] for kEpiArgmax
+    uint32_t* err = nullptr;       // device error word (bounded waits)
 };
 
 // synth.cu

@@ -385,7 +385,7 @@ int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtenso
     LinearArgs a;
     a.w = w; a.scale = s; a.wkind = wkind; a.M = M; a.K = K; a.x = x; a.ldx = K; a.N = N;
     a.y = y; a.ldy = epi == kEpiSwiGLU ? M / 2 : M; a.epi = epi; a.resid = resid; a.norm_w = norm_w;
-    a.eps = c->d.eps > 0.0f ? c->d.eps : 1e-6f; a.argmax_keys = keys;
+    a.eps = c->d.eps > 0.0f ? c->d.eps : 1e-6f; a.argmax_keys = keys; a.err = c->derr;
     int path = c->path_policy;
     // auto: one activation row -> GEMV (no plane kernel, one launch) except the
     // vocabulary-sized LM head; more rows -> tcgen05 (measured faster from 2 up)
@@ -663,6 +663,19 @@ void enqueue_prefill_layers(ZynferCuCtx* c, uint32_t seq, int T, uint32_t l0, ui
 }
 
 }  // namespace
+
+namespace zc {
+int ctx_fail(ZynferCuCtx* c, int code, const char* msg) { return fail(c, code, msg); }
+
+int ctx_check_arch(ZynferCuCtx* c, const ZynferCuModelDesc* w) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    const ZynferCuModelDesc& m = c->d;
+    if (m.vocab != w->vocab || m.hidden != w->hidden || m.inter != w->inter || m.layers != w->layers ||
+        m.n_q != w->n_q || m.n_kv != w->n_kv || m.head_dim != w->head_dim)
+        return fail(c, ZYNFER_CU_INVALID, "ShapeMismatch: the artifact's architecture is not the model's");
+    return ZYNFER_CU_OK;
+}
+}  // namespace zc
 
 // =================================================================== ABI
 
