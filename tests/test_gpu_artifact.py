@@ -101,3 +101,31 @@ def test_missing_tensor_and_wrong_architecture_are_reported(tmp_path):
         with pytest.raises(zc.InvalidArgument, match="ShapeMismatch"):
             other.load_artifact(art)
     os.remove(path)
+
+
+def test_cli_forward_golden_and_decode_bench(tmp_path, capsys):
+    """zynfer forward-golden / decode-bench --backend cuda (main.zig:412-505, 1150-1245)."""
+    import json
+
+    from zynfer_b200 import cli
+    path = str(tmp_path / "small_bf16.zynfer")
+    _write(path, A.DT_BF16, bf16_values=True)
+    ids = [int(t) for t in O.synth_tokens(9, SEED, 7, SMALL["vocab"])]
+    ref = O.Model(O.Arch(**SMALL), O.W_BF16, kv_bf16=False, seed=SEED, w_std=WSTD, norm_std=NSTD)
+    want = ref.session(16).prefill_last_logits(ids)
+    ref.close()
+    gold = str(tmp_path / "golden.f32")
+    want.astype("<f4").tofile(gold)
+    assert cli.main(["forward-golden", path, "--tokens", ",".join(map(str, ids)), "--golden", gold,
+                     "--backend", "cuda"]) == 0
+    out = capsys.readouterr().out
+    assert "golden OK" in out
+    top = out.split("top logits (last token):\n")[1].splitlines()[0]
+    assert top.strip().startswith(f"id={int(np.argmax(want))} ")
+    assert cli.main(["decode-bench", "--backend", "cuda", "--artifact", path, "--batch", "2",
+                     "--prefill-tokens", "32", "--decode-steps", "4", "--warmup", "1", "--iters", "2"]) == 0
+    out = capsys.readouterr().out
+    line = json.loads(out.split("json\n")[1].splitlines()[0])
+    assert line["backend"] == "cuda" and line["cuda_batch"] == 2
+    assert line["cuda_decode_ns_per_token"] > 0 and line["cuda_prefill_ns"] > 0
+    assert all(k in line for k in cli.BLOCK_BENCH_KEYS)
