@@ -19,7 +19,8 @@ namespace {
 // the grid takes an equal contiguous range of it (at least
 // kMinBlocksPerWarp), so each block of K/V is read exactly once and all
 // warps stream the same number of bytes whatever the context lengths. A warp
-// owns a private ring of kRing 8 KB slots (K then V of one block and head)
+// owns a private ring of kRing 8 KB slots (K then V of one block and head;
+// three slots, two for a one-row step)
 // filled by cp.async.bulk on per-slot mbarriers; there is no barrier between
 // warps in the main loop.
 //
@@ -56,36 +57,45 @@ using attn::fence_proxy_async_smem;
 using attn::pack_terms;
 constexpr int kDecWarps = 8, kDecThreads = kDecWarps * kWarp;
 static_assert(kDecWarps >= 4, "decode_max_segs assumes CTA spans of at least 4 warps");
-constexpr int kRing = 3;                                     // slots per warp
 constexpr int kMaxBatch = 1024;
-constexpr size_t kRingBytes = (size_t)kDecWarps * kRing * kSlotBytes;
 constexpr int kIdRing = 64;                                 // per-warp ring of block addresses (2 chunks of 32)
 constexpr size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
-constexpr size_t kScratchOff = align16(kRingBytes + kDecWarps * kRing * sizeof(uint64_t) + (kMaxBatch + 1) * sizeof(int) +
-                                       kDecWarps * kIdRing * sizeof(uint32_t));  // per warp: q (2 x 128 f32), new K/V row
-constexpr size_t kWarpScratch = kG * kD * 4 + 2 * kD * 2;
-constexpr size_t kRecOff = kScratchOff + kDecWarps * kWarpScratch;  // [2][kDecWarps] share records
-constexpr size_t kGidOff = kRecOff + (size_t)2 * kDecWarps * attn::kPartStride * 4;  // [2][kDecWarps] int
-constexpr size_t kDecodeSmem = kGidOff + 2 * kDecWarps * sizeof(int);
-static_assert(kDecodeSmem <= 232448, "decode attention shared memory");
-static_assert(kScratchOff % 16 == 0 && kWarpScratch % 16 == 0 && kRecOff % 16 == 0 &&
-                  (attn::kPartStride * 4) % 16 == 0,
-              "records are written and read as float2 / float4");
+constexpr size_t kWarpScratch = kG * kD * 4 + 2 * kD * 2;    // per warp: q (2 x 128 f32), new K/V row
+// Shared-memory layout for RING slots per warp. Three slots keep a block
+// loading while a warp computes on a pair (the rate at many rows); one row's
+// step gives every warp at most one pair (2 blocks), so two slots hold its
+// whole share, and the smaller footprint (~163 KB instead of ~227 KB) lets the
+// neighbouring one-row GEMV kernels' CTAs be resident on the same SM.
+template <int RING>
+struct DecLayout {
+    static constexpr size_t ring_bytes = (size_t)kDecWarps * RING * kSlotBytes;
+    static constexpr size_t scratch_off = align16(ring_bytes + kDecWarps * RING * sizeof(uint64_t) +
+                                                  (kMaxBatch + 1) * sizeof(int) + kDecWarps * kIdRing * sizeof(uint32_t));
+    static constexpr size_t rec_off = scratch_off + kDecWarps * kWarpScratch;  // [2][kDecWarps] share records
+    static constexpr size_t gid_off = rec_off + (size_t)2 * kDecWarps * attn::kPartStride * 4;  // [2][kDecWarps] int
+    static constexpr size_t smem = gid_off + 2 * kDecWarps * sizeof(int);
+    static_assert(smem <= 232448, "decode attention shared memory");
+    static_assert(scratch_off % 16 == 0 && kWarpScratch % 16 == 0 && rec_off % 16 == 0 &&
+                      (attn::kPartStride * 4) % 16 == 0,
+                  "records are written and read as float2 / float4");
+};
 
 struct BlockCursor {
     int b, head, blk, nblk;
 };
 
-__global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeArgs a) {
+template <int kRing>
+__device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
+    using Lay = DecLayout<kRing>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     unsigned char* ring = smem_raw + (size_t)warp * kRing * kSlotBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kRingBytes) + warp * kRing;
-    int* pref = reinterpret_cast<int*>(smem_raw + kRingBytes + kDecWarps * kRing * sizeof(uint64_t));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + Lay::ring_bytes) + warp * kRing;
+    int* pref = reinterpret_cast<int*>(smem_raw + Lay::ring_bytes + kDecWarps * kRing * sizeof(uint64_t));
     uint32_t* kidx = reinterpret_cast<uint32_t*>(pref + kMaxBatch + 1) + warp * kIdRing;
-    float* qb = reinterpret_cast<float*>(smem_raw + kScratchOff + warp * kWarpScratch);
-    float* recs = reinterpret_cast<float*>(smem_raw + kRecOff);  // record (warp, k) at (k * kDecWarps + warp)
-    int (*rec_gid)[kDecWarps] = reinterpret_cast<int (*)[kDecWarps]>(smem_raw + kGidOff);  // (row, kv head) of each record
+    float* qb = reinterpret_cast<float*>(smem_raw + Lay::scratch_off + warp * kWarpScratch);
+    float* recs = reinterpret_cast<float*>(smem_raw + Lay::rec_off);  // record (warp, k) at (k * kDecWarps + warp)
+    int (*rec_gid)[kDecWarps] = reinterpret_cast<int (*)[kDecWarps]>(smem_raw + Lay::gid_off);  // (row, kv head) of each record
     uint16_t* kvnew = reinterpret_cast<uint16_t*>(qb + kG * kD);
     constexpr unsigned kAll = 0xFFFFFFFFu;
 
@@ -450,6 +460,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeA
     }
 }
 
+// The decode kernels: three ring slots for many rows (the register file is
+// the kernel's own); two slots and at most 192 registers per thread for a
+// one-row step, so a one-row GEMV CTA (256 threads, <= 64 registers, <= 48 KB
+// of shared memory) fits on the same SM beside it.
+__global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeArgs a) { attn_decode_body<3>(a); }
+__global__ void __maxnreg__(192) attn_decode_row_kernel(AttnDecodeArgs a) { attn_decode_body<2>(a); }
+
 // ------------------------------------------------------------ prefill
 //
 // Causal GQA prefill attention on the tensor cores (mma.sync m16n8k16, bf16
@@ -651,12 +668,14 @@ __global__ void __launch_bounds__(PTHREADS, 1) attn_prefill_kernel(AttnPrefillAr
 }  // namespace
 
 void prepare_attn_kernels() {
-    configure_kernel((const void*)attn_decode_kernel, kDecodeSmem);
+    configure_kernel((const void*)attn_decode_kernel, DecLayout<3>::smem);
+    configure_kernel((const void*)attn_decode_row_kernel, DecLayout<2>::smem);
     configure_kernel((const void*)attn_prefill_kernel, kPrefillSmem);
 }
 
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st) {
-    launch_pdl(attn_decode_kernel, device_sm_count(), kDecThreads, kDecodeSmem, st, a);
+    if (a.B == 1) launch_pdl(attn_decode_row_kernel, device_sm_count(), kDecThreads, DecLayout<2>::smem, st, a);
+    else launch_pdl(attn_decode_kernel, device_sm_count(), kDecThreads, DecLayout<3>::smem, st, a);
 }
 
 void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st) {
