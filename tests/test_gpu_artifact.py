@@ -19,6 +19,9 @@ pytestmark = pytest.mark.gpu
 SMALL = dict(vocab=4096, hidden=512, inter=1024, layers=2, n_q=4, n_kv=2, head_dim=128, max_pos=4096, eps=1e-6,
              theta=1_000_000.0)
 SEED, WSTD, NSTD = 11, 0.05, 0.1
+# the device generator derives its scale from the f32 std the C ABI receives;
+# the host generator gets the same f32 value, so both produce identical weights
+WSTD32, NSTD32 = float(np.float32(WSTD)), float(np.float32(NSTD))
 
 
 def _meta():
@@ -31,7 +34,7 @@ def _meta():
 
 def _write(path, dtype, bf16_values):
     ts = []
-    for name, w in synth_np.synth_weights(O.Arch(**SMALL), SEED, w_std=WSTD, norm_std=NSTD, bf16=bf16_values):
+    for name, w in synth_np.synth_weights(O.Arch(**SMALL), SEED, w_std=WSTD32, norm_std=NSTD32, bf16=bf16_values):
         if dtype == A.DT_BF16:
             ts.append(A.Tensor(name, A.DT_BF16, list(w.shape), synth_np.bf16_bits(w).tobytes()))
         elif dtype == A.DT_I8 and w.ndim == 2:
@@ -86,7 +89,7 @@ def test_bf16_model_from_artifact_equals_device_fill(tmp_path):
 def test_missing_tensor_and_wrong_architecture_are_reported(tmp_path):
     path = str(tmp_path / "partial.zynfer")
     ts = [A.Tensor(n, A.DT_F32, list(w.shape), np.ascontiguousarray(w, np.float32).tobytes())
-          for n, w in synth_np.synth_weights(O.Arch(**SMALL), SEED, w_std=WSTD, norm_std=NSTD)
+          for n, w in synth_np.synth_weights(O.Arch(**SMALL), SEED, w_std=WSTD32, norm_std=NSTD32)
           if n != "model.layers.1.self_attn.k_norm.weight"]
     with open(path, "wb") as f:
         f.write(A.build(_meta(), ts))
