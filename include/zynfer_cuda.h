@@ -214,6 +214,28 @@ ZYNFER_CU_API int zynfer_cu_decode_step(ZynferCuCtx *ctx, const uint32_t *seqs, 
  * CUDA-event time of the steps on the context stream. */
 ZYNFER_CU_API int zynfer_cu_generate(ZynferCuCtx *ctx, const uint32_t *seqs, const uint32_t *first,
                        uint32_t batch, uint32_t steps, uint32_t *out_ids, float *device_ms);
+/* Next-token rule of zynfer_cu_decode_step, zynfer_cu_generate and the token
+ * zynfer_cu_prefill returns (no counterpart in the reference, which decodes
+ * greedily with topK, qwen_forward.zig:177-193; its roadmap's Stage 12,
+ * docs/roadmap.md:29, names sampling without specifying it).
+ * temperature 0 (the default): greedy, the argmax. temperature > 0: temperature
+ * only (top_k 0, top_p 1) draws from softmax(logits / temperature) exactly
+ * (Gumbel-max); otherwise the top_k (1..64; 0 = 64) largest logits, their
+ * softmax at that temperature summed in descending order, cut to the shortest
+ * prefix whose sum reaches top_p (0 < top_p <= 1) of the total, and one draw
+ * from that prefix. Draws come from the counter generator of synth_rng.h keyed
+ * by (seed, sequence slot) at the position of the step's input token, so a
+ * sequence's tokens do not depend on its batch neighbours. Logits are
+ * written to device memory whenever sampling is on; the persistent schedule
+ * is not used while it is. Rebuilds the decode graphs on the next step. */
+ZYNFER_CU_API int zynfer_cu_set_sampling(ZynferCuCtx *ctx, float temperature, uint32_t top_k, float top_p,
+                                         uint64_t seed);
+/* The same rule on caller-owned device logits [rows][vocab] (rows <= the
+ * model's max_batch): slots[i] and positions[i] (host) key row i's draws;
+ * out_ids (host) receives one id per row. temperature > 0. Synchronises. */
+ZYNFER_CU_API int zynfer_cu_sample(ZynferCuCtx *ctx, const float *logits, uint32_t rows, uint32_t vocab,
+                                   const uint32_t *slots, const uint32_t *positions, float temperature,
+                                   uint32_t top_k, float top_p, uint64_t seed, uint32_t *out_ids);
 /* One transformer block (qwen_block.forward, qwen_block.zig:161-235) of layer
  * `layer` on host hidden states x [t][hidden] at pos0 = the sequence's length;
  * out [t][hidden]. Appends to the sequence's cache for that layer. */

@@ -79,6 +79,9 @@ def lib():
     L.zo_expect_close.argtypes = [F32P, F32P, SZ, C.c_float, C.c_float]
     L.zo_expect_close.restype = C.c_int
     L.zo_top_k.argtypes = [F32P, SZ, SZ, U32P, F32P]
+    L.zo_sample_row.argtypes = [F32P, SZ, C.c_float, C.c_uint32, C.c_float, C.c_uint64, C.c_uint32, C.c_uint32,
+                                C.POINTER(C.c_uint32)]
+    L.zo_sample_row.restype = C.c_int
     L.zo_synth_normal.argtypes = [F32P, SZ, C.c_uint64, C.c_uint64, C.c_float]
     L.zo_synth_tokens.argtypes = [U32P, SZ, C.c_uint64, C.c_uint64, C.c_uint32]
     L.zo_model_create.argtypes = [C.POINTER(ZoArch), C.c_int, C.c_int, C.c_int]
@@ -252,6 +255,15 @@ def top_k(logits, k):
     vals = np.empty(k, np.float32)
     lib().zo_top_k(logits, logits.size, k, ids, vals)
     return ids, vals
+
+
+def sample_row(logits, temperature, top_k, top_p, seed, slot, pos):
+    """Extension: one sampled token id (zo_sample_row); inv_t = 1/temperature in f32."""
+    logits = f32(logits)
+    out = C.c_uint32()
+    inv_t = float(np.float32(1.0) / np.float32(temperature))
+    lib().zo_sample_row(logits, logits.size, inv_t, top_k, top_p, seed, slot, pos, C.byref(out))
+    return int(out.value)
 
 
 def synth_normal(n, seed, stream, std):

@@ -358,6 +358,77 @@ void zo_top_k(const float *logits, size_t n, size_t k, uint32_t *ids, float *val
     }
 }
 
+/* Extension (sampling: the reference has greedy topK only; its roadmap
+ * Stage 12, docs/roadmap.md:29, is not started). One row of logits:
+ * - temperature only (top_k == 0, top_p >= 1): the Gumbel-max draw
+ *   argmax_v (l_v * inv_t + g_v), g_v = -log(-log(u_v)), first maximum on ties
+ *   (topK's rule, qwen_forward.zig:177-193);
+ * - otherwise the K = top_k (64 when 0, at most 64) largest logits in topK's
+ *   order, p_i = exp((l_i - l_0) * inv_t) summed in that order, the shortest
+ *   prefix m whose sum reaches top_p times the total (all K when top_p >= 1),
+ *   and the first i < m whose running sum exceeds u times the prefix sum
+ *   (m - 1 if rounding leaves none).
+ * Draws: zs_uniform01 of ZS_SAMPLE_STREAM(slot) at pos * (vocab + 1) + v, and
+ * + vocab for the row's draw. Every f32 step is a single rounded operation. */
+int zo_sample_row(const float *logits, size_t V, float inv_t, uint32_t top_k, float top_p, uint64_t seed,
+                  uint32_t slot, uint32_t pos, uint32_t *out) {
+    const uint64_t key = zs_key(seed, ZS_SAMPLE_STREAM(slot));
+    const uint64_t base = (uint64_t)pos * (V + 1);
+    if (top_k == 0 && !(top_p < 1.0f)) {
+        uint32_t best = 0;
+        float best_s = -INFINITY;
+        for (size_t v = 0; v < V; v++) {
+            const float u = zs_uniform01(key, base + v);
+            const float g = -logf(-logf(u));
+            const float sv = logits[v] * inv_t + g;
+            if (sv > best_s) {
+                best_s = sv;
+                best = (uint32_t)v;
+            }
+        }
+        *out = best;
+        return ZO_OK;
+    }
+    const size_t K = top_k == 0 || top_k > 64 ? 64 : top_k;
+    uint32_t ids[64];
+    float vals[64], p[64];
+    zo_top_k(logits, V, K, ids, vals);
+    size_t n = 0;
+    while (n < K && vals[n] != -INFINITY) n++;
+    if (n == 0) {
+        *out = 0;
+        return ZO_OK;
+    }
+    float z = 0.0f;
+    for (size_t i = 0; i < n; i++) {
+        p[i] = expf((vals[i] - vals[0]) * inv_t);
+        z += p[i];
+    }
+    size_t m = n;
+    if (top_p < 1.0f) {
+        const float target = top_p * z;
+        float c = 0.0f;
+        for (m = 0; m < n;) {
+            c += p[m++];
+            if (c >= target) break;
+        }
+    }
+    float zm = 0.0f;
+    for (size_t i = 0; i < m; i++) zm += p[i];
+    const float r = zs_uniform01(key, base + V) * zm;
+    float c = 0.0f;
+    size_t pick = m - 1;
+    for (size_t i = 0; i < m; i++) {
+        c += p[i];
+        if (c > r) {
+            pick = i;
+            break;
+        }
+    }
+    *out = ids[pick];
+    return ZO_OK;
+}
+
 void zo_synth_normal(float *out, size_t n, uint64_t seed, uint64_t stream, float std_dev) {
     const uint64_t key = zs_key(seed, stream);
     const float k = (float)((double)std_dev / ZS_IH4_SIGMA);

@@ -64,6 +64,11 @@ void zo_diff_f32(const float *expected, const float *actual, size_t n, ZoDiff *o
 int zo_expect_close(const float *expected, const float *actual, size_t n, float atol, float rtol);
 void zo_top_k(const float *logits, size_t n, size_t k, uint32_t *ids, float *vals);
 
+/* Extension: temperature / top-k / top-p sampling of one row of logits (see
+ * zynfer_oracle.c for the exact rule and the draws). */
+int zo_sample_row(const float *logits, size_t V, float inv_t, uint32_t top_k, float top_p, uint64_t seed,
+                  uint32_t slot, uint32_t pos, uint32_t *out);
+
 /* ---- synthetic data (same generator as the CUDA library) ---- */
 void zo_synth_normal(float *out, size_t n, uint64_t seed, uint64_t stream, float std_dev);
 void zo_synth_tokens(uint32_t *out, size_t n, uint64_t seed, uint64_t stream, uint32_t vocab);

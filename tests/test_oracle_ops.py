@@ -171,3 +171,24 @@ def test_synth_generator_c_matches_numpy():
     assert np.array_equal(t_c, t_n)
     big = synth_np.normal(1 << 20, 5, 1, 1.0)
     assert abs(float(big.mean())) < 5e-3 and abs(float(big.std()) - 1.0) < 5e-3
+
+
+def test_sampler_rule():  # extension: temperature / top-k / top-p sampling (zo_sample_row)
+    rng = np.random.default_rng(1)
+    logits = (rng.standard_normal(1000) * 3).astype(np.float32)
+    top = int(np.argmax(logits))
+    assert O.sample_row(logits, 1e-4, 0, 1.0, 5, 0, 0) == top      # a cold temperature is the argmax
+    assert O.sample_row(logits, 1.0, 1, 1.0, 5, 0, 0) == top       # top-1 is the argmax
+    assert O.sample_row(logits, 1.0, 0, 1e-6, 5, 0, 0) == top      # a tiny nucleus keeps only the top
+    # the draws are keyed by (seed, slot, position): repeatable, and independent across slots
+    assert O.sample_row(logits, 1.0, 0, 1.0, 9, 3, 7) == O.sample_row(logits, 1.0, 0, 1.0, 9, 3, 7)
+    p = np.exp(logits.astype(np.float64) - logits.max())
+    p /= p.sum()
+    n = 3000
+    full = np.bincount([O.sample_row(logits, 1.0, 0, 1.0, s, 0, 0) for s in range(n)], minlength=1000) / n
+    best = np.argsort(-p)[:3]
+    assert np.all(np.abs(full[best] - p[best]) < 4 * np.sqrt(p[best] / n) + 1e-3)
+    k5 = np.bincount([O.sample_row(logits, 1.0, 5, 1.0, s, 1, 0) for s in range(n)], minlength=1000) / n
+    assert set(np.nonzero(k5)[0]) <= set(np.argsort(-logits, kind="stable")[:5].tolist())
+    q = np.sort(p)[::-1][:5] / np.sort(p)[::-1][:5].sum()
+    assert np.all(np.abs(np.sort(k5[k5 > 0])[::-1][:len(q)] - q[:np.count_nonzero(k5)]) < 0.05)

@@ -108,6 +108,23 @@ void launch_bf16_to_f32(const uint16_t* src, size_t n, float* dst, cudaStream_t 
 void launch_silu_mul(const float* g, const float* u, size_t n, float* o, cudaStream_t st);
 void launch_finalize(const FinalizeArgs& a, cudaStream_t st);
 
+// sample.cu: temperature / top-k / top-p sampling of `rows` rows of logits
+struct SampleArgs {
+    const float* logits;   // [rows][V]
+    int V, rows;
+    float inv_t;           // 1 / temperature (> 0)
+    int top_k;             // 0 = off (top-p then looks at the 64 largest), else 1..64
+    float top_p;           // >= 1 = off
+    uint64_t seed;
+    const int* seq_of;     // [rows] sequence slot per row (nullable: seq0)
+    const int* positions;  // [rows] position of the row's input token (nullable: pos0)
+    int seq0, pos0;
+    unsigned long long* keys_out;  // nullable [rows]: the id in the argmax-key encoding
+    uint32_t* ids_out;             // nullable [rows]
+};
+void prepare_sample_kernels();
+void launch_sample(const SampleArgs& a, cudaStream_t st);
+
 // gemv.cu (N <= 8)
 void launch_gemv(const LinearArgs& a, cudaStream_t st);
 // gemm_simt.cu (any N)

@@ -144,6 +144,12 @@ struct ZynferCuCtx {
     size_t simt_xn_elems = 0;
     int path_policy = kPathAuto;
     int schedule = kSchedAuto;
+    // next-token rule of decode, generate and prefill: greedy (temperature 0)
+    // or sampling (sample.cu)
+    float samp_temp = 0.0f;
+    uint32_t samp_top_k = 0;
+    float samp_top_p = 1.0f;
+    uint64_t samp_seed = 0;
     bool persistent_ok = false;          // model shape and device allow the persistent (dataflow) decode kernel
     PersistentLayer* dlayers = nullptr;  // [layers] weight pointers for it
     unsigned* psync = nullptr;           // [3] its unused / finished-CTA / abort words
@@ -432,7 +438,19 @@ int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtenso
 // dataflow kernel (whose linear phases run on CUDA cores) at every batch size,
 // batch 1 included.
 bool use_persistent(const ZynferCuCtx* c, int B) {
-    return B <= kPersistentMaxBatch && c->persistent_ok && c->schedule == kSchedPersistent;
+    return B <= kPersistentMaxBatch && c->persistent_ok && c->schedule == kSchedPersistent && c->samp_temp <= 0.0f;
+}
+
+// Replace the argmax keys of `rows` rows by sampled ids (sampling on only;
+// the LM head has written the logits).
+void enqueue_sample(ZynferCuCtx* c, int rows, const int* seq_of, const int* positions, int seq0, int pos0) {
+    SampleArgs sa{};
+    sa.logits = c->dlogits; sa.V = (int)c->d.vocab; sa.rows = rows;
+    sa.inv_t = 1.0f / c->samp_temp; sa.top_k = (int)c->samp_top_k; sa.top_p = c->samp_top_p; sa.seed = c->samp_seed;
+    sa.seq_of = seq_of; sa.positions = positions; sa.seq0 = seq0; sa.pos0 = pos0;
+    sa.keys_out = c->dkeys; sa.ids_out = nullptr;
+    launch_sample(sa, c->stream);
+    c->step_launches += 1;
 }
 
 void enqueue_decode_persistent(ZynferCuCtx* c, int B, bool want_logits) {
@@ -526,8 +544,10 @@ void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
         linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, &Ld.tm_d, H, I, c->dh, B, c->dx, kEpiResid, c->dx1, nullptr,
                nullptr);
     }
+    const bool sampling = c->samp_temp > 0.0f;
     linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, &c->tm_embed, m.vocab, H, c->dx, B,
-           want_logits ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
+           want_logits || sampling ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
+    if (sampling) enqueue_sample(c, B, c->dseq, c->dpos, 0, 0);
     FinalizeArgs fa{};
     fa.keys = c->dkeys; fa.ids_out = c->dids; fa.next_tokens = c->dtok; fa.positions = c->dpos;
     fa.history = c->dhist; fa.step = c->dstep; fa.B = B;
@@ -1265,8 +1285,10 @@ int zynfer_cu_prefill(ZynferCuCtx* c, uint32_t seq, const uint32_t* tokens, uint
     c->step_paths = 0;
     launch_embed(c->embed, c->sembed, c->wkind, c->ptok, n, m.hidden, m.vocab, c->px, c->derr, c->stream);
     enqueue_prefill_layers(c, seq, (int)n, 0, m.layers);
+    const bool sampling = c->samp_temp > 0.0f;
     linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, &c->tm_embed, m.vocab, m.hidden, c->px + (size_t)(n - 1) * m.hidden, 1,
-           last_logits ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
+           last_logits || sampling ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
+    if (sampling) enqueue_sample(c, 1, nullptr, nullptr, (int)seq, (int)n - 1);
     FinalizeArgs fa{};
     fa.keys = c->dkeys; fa.ids_out = c->dids; fa.B = 1;
     launch_finalize(fa, c->stream);
@@ -1464,6 +1486,51 @@ int zynfer_cu_linear(ZynferCuCtx* c, int wkind, const void* w, const float* scal
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "linear launch");
     set_path(c, "linear", 1u << p, nullptr);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_set_sampling(ZynferCuCtx* c, float temperature, uint32_t top_k, float top_p, uint64_t seed) {
+    if (!c) return ZYNFER_CU_INVALID;
+    if (!(temperature >= 0.0f) || temperature > 1e6f || top_k > 64 || !(top_p > 0.0f) || top_p > 1.0f)
+        return fail(c, ZYNFER_CU_INVALID, "sampling: temperature >= 0, top_k <= 64, 0 < top_p <= 1");
+    c->samp_temp = temperature;
+    c->samp_top_k = top_k;
+    c->samp_top_p = top_p;
+    c->samp_seed = seed;
+    for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second.exec);  // graphs bake the rule
+    c->graphs.clear();
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_sample(ZynferCuCtx* c, const float* logits, uint32_t rows, uint32_t vocab, const uint32_t* slots,
+                     const uint32_t* positions, float temperature, uint32_t top_k, float top_p, uint64_t seed,
+                     uint32_t* out_ids) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    if (!logits || !slots || !positions || !out_ids || rows == 0 || vocab == 0)
+        return fail(c, ZYNFER_CU_INVALID, "bad sample arguments");
+    if (rows > c->d.max_batch) return fail(c, ZYNFER_CU_INVALID, "rows > max_batch");
+    if (!(temperature > 0.0f) || top_k > 64 || !(top_p > 0.0f) || top_p > 1.0f)
+        return fail(c, ZYNFER_CU_INVALID, "sampling: temperature > 0, top_k <= 64, 0 < top_p <= 1");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    for (uint32_t i = 0; i < rows; ++i) {
+        c->hio[i] = slots[i];
+        c->hio[rows + i] = positions[i];
+    }
+    ZC_CHECK(c, cudaMemcpyAsync(c->dio, c->hio, (size_t)2 * rows * 4, cudaMemcpyHostToDevice, c->stream), "stage");
+    SampleArgs sa{};
+    sa.logits = logits; sa.V = (int)vocab; sa.rows = (int)rows; sa.inv_t = 1.0f / temperature;
+    sa.top_k = (int)top_k; sa.top_p = top_p; sa.seed = seed;
+    sa.seq_of = reinterpret_cast<const int*>(c->dio); sa.positions = reinterpret_cast<const int*>(c->dio + rows);
+    sa.keys_out = nullptr; sa.ids_out = c->dids;
+    launch_sample(sa, c->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "sample launch");
+    ZC_CHECK(c, cudaMemcpyAsync(c->hids, c->dids, (size_t)rows * 4, cudaMemcpyDeviceToHost, c->stream), "ids");
+    int rc = check_device_error(c);
+    if (rc) return rc;
+    for (uint32_t i = 0; i < rows; ++i) out_ids[i] = c->hids[i];
+    set_path(c, "sample", 0, nullptr);
     return ZYNFER_CU_OK;
 }
 

@@ -50,6 +50,7 @@ void prepare_all_kernels() {
     prepare_attn_kernels();
     prepare_flow_kernels();
     prepare_tc_kernels();
+    prepare_sample_kernels();
 }
 
 int device_sm_count() {

@@ -83,6 +83,20 @@ ZS_HD float zs_normal(uint64_t key, uint64_t index, float k) {
 #endif
 }
 
+/* Sampling draws of one sequence slot: stream ZS_SAMPLE_STREAM(slot); the
+ * token at position pos uses indices pos * (vocab + 1) + v (one draw per
+ * vocabulary entry) and pos * (vocab + 1) + vocab (the row's single draw). */
+#define ZS_SAMPLE_STREAM(slot) (0x5A5A000000000000ull | (uint64_t)(slot))
+
+/* Uniform in (0, 1) from 23 random bits: (u + 1/2) 2^-23, every step exact in f32. */
+ZS_HD float zs_uniform01(uint64_t key, uint64_t index) {
+#if defined(__CUDA_ARCH__)
+    return __fmul_rn(__fadd_rn((float)(zs_bits(key, index) >> 41), 0.5f), 1.1920928955078125e-07f);
+#else
+    return ((float)(zs_bits(key, index) >> 41) + 0.5f) * 1.1920928955078125e-07f;
+#endif
+}
+
 /* Uniform integer in [0, n). */
 ZS_HD uint32_t zs_uniform_u32(uint64_t key, uint64_t index, uint32_t n) {
     return (uint32_t)(zs_bits(key, index) % (uint64_t)n);

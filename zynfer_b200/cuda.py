@@ -102,6 +102,8 @@ _SIGS = {
     "zynfer_cu_block_forward": (C.c_int, [VP, U32, U32, VP, U32, VP]),
     "zynfer_cu_linear": (C.c_int, [VP, C.c_int, VP, VP, VP, U32, U32, U32, VP]),
     "zynfer_cu_set_linear_path": (C.c_int, [VP, C.c_char_p]),
+    "zynfer_cu_set_sampling": (C.c_int, [VP, C.c_float, U32, C.c_float, U64]),
+    "zynfer_cu_sample": (C.c_int, [VP, VP, U32, U32, VP, VP, C.c_float, U32, C.c_float, U64, VP]),
     "zynfer_cu_set_decode_schedule": (C.c_int, [VP, C.c_char_p]),
     "zynfer_cu_phase_trace": (C.c_int, [VP, VP, C.c_int]),
     "zynfer_cu_linear_q8_static": (C.c_int, [VP, VP, VP, U32, U32, U32, VP, VP]),
@@ -260,6 +262,20 @@ class Gpu:
     def set_linear_path(self, path: str):
         """"auto" | "gemv" | "tcgen05" | "simt"."""
         self.check(lib().zynfer_cu_set_linear_path(self.h, path.encode()))
+
+    def set_sampling(self, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0, seed: int = 0):
+        """Next-token rule of decode / generate / prefill: temperature 0 = greedy."""
+        self.check(lib().zynfer_cu_set_sampling(self.h, temperature, top_k, top_p, seed))
+
+    def sample(self, logits, rows: int, vocab: int, slots, positions, temperature: float, top_k: int = 0,
+               top_p: float = 1.0, seed: int = 0):
+        """The sampling rule on device logits [rows][vocab]; returns one id per row."""
+        s = np.ascontiguousarray(slots, np.uint32)
+        p = np.ascontiguousarray(positions, np.uint32)
+        out = np.empty(rows, np.uint32)
+        self.check(lib().zynfer_cu_sample(self.h, _ptr(logits), rows, vocab, _ptr(s), _ptr(p), temperature, top_k,
+                                          top_p, seed, _ptr(out)))
+        return out
 
     def phase_trace(self):
         """Phase timestamps (ns) of the last persistent decode step run with timing on."""
