@@ -196,6 +196,23 @@ ZYNFER_CU_API int zynfer_cu_kv_read(ZynferCuCtx *ctx, uint32_t seq, uint32_t lay
  * the same way holds bit-identical K/V. */
 ZYNFER_CU_API int zynfer_cu_kv_fill_synthetic(ZynferCuCtx *ctx, uint32_t seq, uint32_t n, uint64_t seed);
 
+/* Prefix reuse over the paged pool (no counterpart in the reference; its
+ * roadmap's Stage 22, docs/roadmap.md:39, names it): `dst` (reset first)
+ * becomes a sequence of the first n positions of `src`. Whole 16-token
+ * blocks are shared, counted per block and returned to the pool when the last
+ * sequence holding them is reset; only a partly filled last block is copied,
+ * because it is the one `dst` appends into next. Appends only ever write
+ * positions at or past a sequence's length, so no shared block is written
+ * again. n <= the length of src. */
+ZYNFER_CU_API int zynfer_cu_seq_fork(ZynferCuCtx *ctx, uint32_t dst, uint32_t src, uint32_t n);
+/* Append n tokens to `seq` (decode steps of one row, from position = its
+ * length): what follows a shared prefix. last_logits [vocab] (of the last
+ * token) and argmax may be NULL. */
+ZYNFER_CU_API int zynfer_cu_extend(ZynferCuCtx *ctx, uint32_t seq, const uint32_t *tokens, uint32_t n,
+                                   float *last_logits, uint32_t *argmax);
+/* Free pool blocks and blocks held by more than one sequence. */
+ZYNFER_CU_API int zynfer_cu_pool_stats(const ZynferCuCtx *ctx, uint32_t *free_blocks, uint32_t *shared_blocks);
+
 /* ---- forward ---- */
 /* Session.prefillLastLogits (qwen_forward.zig:89-160): resets `seq`, runs the
  * n prompt tokens through all layers, then the final norm and tied LM head on

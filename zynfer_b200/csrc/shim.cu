@@ -103,6 +103,7 @@ struct ZynferCuCtx {
     size_t kv_layer_elems = 0;
     int max_blocks = 0, n_blocks = 0;
     std::vector<int> free_blocks;
+    std::vector<uint32_t> block_refs;  // sequences holding each pool block (shared prefixes hold one block several times)
     std::vector<std::vector<int>> seq_blocks;
     std::vector<uint32_t> seq_len;
     std::vector<char> table_dirty;  // host row changed since its last upload
@@ -563,6 +564,7 @@ int ensure_blocks(ZynferCuCtx* c, uint32_t seq, uint32_t upto_len) {
         if (c->free_blocks.empty()) return fail(c, ZYNFER_CU_OOM, "KV block pool exhausted");
         const int b = c->free_blocks.back();
         c->free_blocks.pop_back();
+        c->block_refs[b] = 1;
         c->table_host[(size_t)seq * c->max_blocks + bl.size()] = b;
         if (bl.size() == bl.capacity()) c->host_alloc_events += 1;  // reserved to max_blocks at init
         bl.push_back(b);
@@ -572,7 +574,8 @@ int ensure_blocks(ZynferCuCtx* c, uint32_t seq, uint32_t upto_len) {
 }
 
 void release_seq(ZynferCuCtx* c, uint32_t seq) {
-    for (int b : c->seq_blocks[seq]) c->free_blocks.push_back(b);
+    for (int b : c->seq_blocks[seq])
+        if (--c->block_refs[b] == 0) c->free_blocks.push_back(b);
     c->seq_blocks[seq].clear();
     c->seq_len[seq] = 0;
     std::fill(c->table_host + (size_t)seq * c->max_blocks, c->table_host + (size_t)(seq + 1) * c->max_blocks, -1);
@@ -877,6 +880,7 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     ALLOC(c->kv, c->kv_layer_elems * m.layers);
     c->free_blocks.clear();
     c->free_blocks.reserve(c->n_blocks);
+    c->block_refs.assign(c->n_blocks, 0);
     for (int b = c->n_blocks - 1; b >= 0; --b) c->free_blocks.push_back(b);
     c->seq_blocks.assign(m.max_seqs, {});
     for (auto& bl : c->seq_blocks) bl.reserve(c->max_blocks);  // decode never grows a block list
@@ -1179,6 +1183,71 @@ int zynfer_cu_kv_fill_synthetic(ZynferCuCtx* c, uint32_t seq, uint32_t n, uint64
     if ((rc = check_device_error(c))) return rc;
     c->seq_len[seq] = n;
     set_path(c, "kv_fill", 0, nullptr);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_seq_fork(ZynferCuCtx* c, uint32_t dst, uint32_t src, uint32_t n) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    if (dst >= c->d.max_seqs || src >= c->d.max_seqs || dst == src)
+        return fail(c, ZYNFER_CU_INVALID, "fork: two different sequence slots");
+    if (n > c->seq_len[src]) return fail(c, ZYNFER_CU_INVALID, "fork: n is longer than the source sequence");
+    if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
+    cudaSetDevice(c->device);
+    release_seq(c, dst);
+    const uint32_t full = n / kKvBlock, rest = n % kKvBlock;
+    std::vector<int>& sb = c->seq_blocks[src];
+    std::vector<int>& db = c->seq_blocks[dst];
+    for (uint32_t i = 0; i < full; ++i) {  // whole blocks are shared: no sequence ever writes a full block again
+        const int b = sb[i];
+        c->block_refs[b] += 1;
+        c->table_host[(size_t)dst * c->max_blocks + i] = b;
+        db.push_back(b);
+    }
+    c->table_dirty[dst] = 1;
+    if (rest) {
+        // the partly filled block is the one dst appends into next: dst gets its own copy
+        int rc = ensure_blocks(c, dst, n);
+        if (rc) return rc;
+        const int from = sb[full], to = db[full];
+        const size_t hd = c->d.head_dim, blk_elems = (size_t)2 * kKvBlock * hd;  // K then V of one head
+        for (uint32_t l = 0; l < c->d.layers; ++l) {
+            uint16_t* base = c->kv + l * c->kv_layer_elems;
+            ZC_CHECK(c, cudaMemcpy2DAsync(base + (size_t)to * blk_elems, (size_t)c->n_blocks * blk_elems * 2,
+                                          base + (size_t)from * blk_elems, (size_t)c->n_blocks * blk_elems * 2,
+                                          blk_elems * 2, c->d.n_kv, cudaMemcpyDeviceToDevice, c->stream),
+                     "fork: copy the partial block");
+        }
+    }
+    int rc = upload_table_rows(c, &dst, 1);
+    if (rc) return rc;
+    ZC_CHECK(c, cudaStreamSynchronize(c->stream), "fork");
+    c->seq_len[dst] = n;
+    set_path(c, "seq_fork", 0, nullptr);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_extend(ZynferCuCtx* c, uint32_t seq, const uint32_t* tokens, uint32_t n, float* last_logits,
+                     uint32_t* argmax) {
+    if (!c || !c->ready) return c ? fail(c, ZYNFER_CU_INVALID, "model not initialised") : ZYNFER_CU_INVALID;
+    if (!tokens || n == 0) return fail(c, ZYNFER_CU_INVALID, "extend: no tokens");
+    if (seq >= c->d.max_seqs) return fail(c, ZYNFER_CU_INVALID, "sequence id out of range");
+    if ((uint64_t)c->seq_len[seq] + n > c->d.max_seq_len) return fail(c, ZYNFER_CU_INVALID, "KV cache full");
+    uint32_t id = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        int rc = zynfer_cu_decode_step(c, &seq, tokens + i, 1, &id, i + 1 == n ? last_logits : nullptr);
+        if (rc) return rc;
+    }
+    if (argmax) *argmax = id;
+    set_path(c, "extend", 0, nullptr);
+    return ZYNFER_CU_OK;
+}
+
+int zynfer_cu_pool_stats(const ZynferCuCtx* c, uint32_t* free_blocks, uint32_t* shared_blocks) {
+    if (!c || !c->ready || !free_blocks || !shared_blocks) return ZYNFER_CU_INVALID;
+    uint32_t shared = 0;
+    for (uint32_t r : c->block_refs) shared += r > 1 ? 1u : 0u;
+    *free_blocks = (uint32_t)c->free_blocks.size();
+    *shared_blocks = shared;
     return ZYNFER_CU_OK;
 }
 

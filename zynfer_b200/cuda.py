@@ -96,6 +96,9 @@ _SIGS = {
     "zynfer_cu_seq_len": (C.c_int, [VP, U32, C.POINTER(U32)]),
     "zynfer_cu_kv_read": (C.c_int, [VP, U32, U32, C.c_int, VP]),
     "zynfer_cu_kv_fill_synthetic": (C.c_int, [VP, U32, U32, U64]),
+    "zynfer_cu_seq_fork": (C.c_int, [VP, U32, U32, U32]),
+    "zynfer_cu_extend": (C.c_int, [VP, U32, VP, U32, VP, VP]),
+    "zynfer_cu_pool_stats": (C.c_int, [VP, C.POINTER(U32), C.POINTER(U32)]),
     "zynfer_cu_prefill": (C.c_int, [VP, U32, VP, U32, VP, VP]),
     "zynfer_cu_decode_step": (C.c_int, [VP, VP, VP, U32, VP, VP]),
     "zynfer_cu_generate": (C.c_int, [VP, VP, VP, U32, U32, VP, C.POINTER(C.c_float)]),
@@ -390,6 +393,23 @@ class Model:
         n = U32()
         self.gpu.check(lib().zynfer_cu_seq_len(self.gpu.h, seq, C.byref(n)))
         return int(n.value)
+
+    def seq_fork(self, dst: int, src: int, n: int):
+        """`dst` becomes the first n positions of `src` (whole blocks shared, the partial one copied)."""
+        self.gpu.check(lib().zynfer_cu_seq_fork(self.gpu.h, dst, src, n))
+
+    def extend(self, seq: int, tokens, want_logits: bool = True):
+        """Append tokens to a sequence; the last token's logits and argmax."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        logits = np.empty(self.arch.vocab, np.float32) if want_logits else None
+        am = np.zeros(1, np.uint32)
+        self.gpu.check(lib().zynfer_cu_extend(self.gpu.h, seq, _ptr(t), t.size, _ptr(logits), _ptr(am)))
+        return (logits, int(am[0])) if want_logits else int(am[0])
+
+    def pool_stats(self):
+        free, shared = U32(), U32()
+        self.gpu.check(lib().zynfer_cu_pool_stats(self.gpu.h, C.byref(free), C.byref(shared)))
+        return int(free.value), int(shared.value)
 
     def kv_fill_synthetic(self, seq: int, n: int, seed: int):
         """Reset `seq` and fill positions [0, n) of every layer with the seeded stand-in K/V."""
