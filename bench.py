@@ -31,7 +31,7 @@ device pointers. Each call reads another of R weight copies (R x m x k above
 twice the L2), CUDA events around every call on the library's stream give
 its time, and achieved GB/s = (m k + 4 m + 4 B k + 4 B m) / time.
 
-At one GPU the line also carries two more workloads of the same model:
+At one GPU the line also carries three more workloads of the same model:
 * "batch1" (one sequence, context 2048, 256 greedy tokens on the device):
   ms/token, tok/s and the fraction of the HBM roofline (weights + KV bytes
   per token / measured peak), with the argmax agreement of every timed token
@@ -43,6 +43,9 @@ At one GPU the line also carries two more workloads of the same model:
   accumulate): ms per prefill from CUDA events, TFLOP/s of the algorithmic
   FLOPs against the measured bf16 peak, and the last-token logits of the
   reference tools' golden fixture prompt on the same kind of model.
+* "linears" (the sweep's six shapes at 1 and 8 rows on the default kernel
+  choice, 100 calls each): microseconds and GB/s per isolated call, and the
+  oracle's single-thread time per call.
 
     python bench.py --case SEQS,CTX,LAYERS [--steps K] [--warmup W] [--schedule S]
                     [--path P] [--weights q8|bf16] [--window decode|prefill] [--phases]
@@ -104,10 +107,11 @@ def parse():
     ap.add_argument("--sweep-shape", default=None, help="one shape of the sweep, as MxK")
     ap.add_argument("--no-batch1", action="store_true", help="skip the one-sequence context-2048 workload")
     ap.add_argument("--no-prefill", action="store_true", help="skip the 512-token bf16 prefill workload")
+    ap.add_argument("--no-linears", action="store_true", help="skip the int8 linear sweep at 1 and 8 rows")
     ap.add_argument("--batch1-steps", type=int, default=BATCH1_STEPS)
     ap.add_argument("--case", default=None, help="SEQS,CTX,LAYERS: one fixed decode batch (profiling case)")
     ap.add_argument("--schedule", default="auto", help="--case: decode schedule (auto, kernels, persistent)")
-    ap.add_argument("--path", default="auto", help="--case: linear kernel family (auto, gemv, tcgen05, simt)")
+    ap.add_argument("--path", default="auto", help="--case: linear kernel family (auto, gemv, mma, tcgen05, simt)")
     ap.add_argument("--weights", default="q8", choices=["q8", "bf16"], help="--case: weight storage")
     ap.add_argument("--window", default="decode", choices=["decode", "prefill"],
                     help="--case: what runs between cudaProfilerStart/Stop")
@@ -457,6 +461,7 @@ def run_ours(args):
         oracle.close()
     if rank == 0 and world == 1 and not args.no_prefill:
         prefill = run_prefill(local)
+    linears = run_linears(gpu) if rank == 0 and world == 1 and not args.no_linears else None
 
     if rank == 0:
         mean_ctx = sum(ctx_before) / len(ctx_before)
@@ -497,6 +502,8 @@ def run_ours(args):
             line["batch1"] = batch1
         if prefill is not None:
             line["prefill"] = prefill
+        if linears is not None:
+            line["linears"] = linears
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -626,17 +633,15 @@ def cpu_linear_us(m: int, k: int, batch: int, budget_s: float = 1.0) -> float:
             return dt / calls * 1e6
 
 
-def run_gemv_sweep(args):
+def linear_sweep(gpu, calls: int, shapes, paths_b8=("auto", "gemv", "mma", "tcgen05"), cpu_budget_s: float = 1.0):
+    """Yield one record per (shape, rows, linear path) of the int8 linear sweep
+    on an open context (device pointers through zynfer_cu_linear)."""
     import torch
     from zynfer_b200 import cuda as zc
     peak, peak_kind = measured_peaks()
-    gpu = zc.Gpu(0)
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
     g.manual_seed(SEED)
-    shapes = GEMV_SHAPES
-    if args.sweep_shape:
-        shapes = [tuple(int(v) for v in args.sweep_shape.lower().split("x"))]
     for (m, k) in shapes:
         copies = max(2, -(-2 * L2_BYTES // (m * k)))
         w = torch.randint(-127, 128, (copies, m, k), dtype=torch.int8, device=dev, generator=g)
@@ -646,7 +651,7 @@ def run_gemv_sweep(args):
             x = torch.randn((batch, k), device=dev, generator=g)
             y = torch.empty((batch, m), device=dev)
             ref = (x @ w[0].float().t()) * sc[0]
-            for path in (("auto",) if batch == 1 else ("auto", "gemv")):
+            for path in (("auto",) if batch == 1 else paths_b8):
                 gpu.set_linear_path(path)
                 for i in range(copies):  # warm-up: tensor maps, scratch
                     gpu.linear(zc.W_Q8, w[i], sc[i], x, batch, m, k, y)
@@ -654,9 +659,9 @@ def run_gemv_sweep(args):
                 gpu.linear(zc.W_Q8, w[0], sc[0], x, batch, m, k, y)
                 gpu.sync()
                 err = float(((y - ref).abs().max() / ref.abs().max().clamp_min(1e-30)).item())
-                calls = max(args.sweep_calls, 2 * copies)
+                n_calls = max(calls, 2 * copies)
                 gpu.set_timing(True)
-                for i in range(calls):
+                for i in range(n_calls):
                     gpu.linear(zc.W_Q8, w[i % copies], sc[i % copies], x, batch, m, k, y)
                 n, ms = gpu.kernel_time(zc.K_LINEAR)
                 gpu.set_timing(False)
@@ -664,17 +669,42 @@ def run_gemv_sweep(args):
                 nbytes = m * k + 4 * m + 4 * batch * k + 4 * batch * m
                 gbs = nbytes / (us * 1e-6) / 1e9
                 if batch not in cpu_us:
-                    cpu_us[batch] = cpu_linear_us(m, k, batch)
-                print(json.dumps({
+                    cpu_us[batch] = cpu_linear_us(m, k, batch, cpu_budget_s)
+                yield {
                     "sweep": "gemv", "m": m, "k": k, "batch": batch, "path": path, "kernel_path": gpu.last_path,
                     "us_per_call": round(us, 3), "bytes_per_call": nbytes, "achieved_gbs": round(gbs, 1),
                     "peak_gbs": peak, "peak_kind": peak_kind, "frac": round(gbs / peak, 4),
                     "rotation_copies": copies, "calls": n, "max_rel_err_vs_torch_f32": err,
                     "cpu_us_per_call": round(cpu_us[batch], 1), "cpu_threads": 1,
-                    "cpu_kind": "port (oracle matvecQ8 / matmulQ8)"}), flush=True)
+                    "cpu_kind": "port (oracle matvecQ8 / matmulQ8)"}
         del w, sc
         torch.cuda.empty_cache()
     gpu.set_linear_path("auto")
+
+
+def run_linears(gpu) -> dict:
+    """The int8 linear sweep's shapes at 1 and 8 rows on the default kernel
+    choice, compactly, for the benchmark line."""
+    cases = []
+    for r in linear_sweep(gpu, 100, GEMV_SHAPES, paths_b8=("auto",), cpu_budget_s=0.5):
+        cases.append({"m": r["m"], "k": r["k"], "rows": r["batch"], "kernel_path": r["kernel_path"],
+                      "us_per_call": r["us_per_call"], "achieved_gbs": r["achieved_gbs"], "frac": r["frac"],
+                      "max_rel_err_vs_torch_f32": r["max_rel_err_vs_torch_f32"],
+                      "cpu_us_per_call": r["cpu_us_per_call"]})
+    return {"workload": "matvecQ8 / matmulQ8 shapes of the model at 1 and 8 activation rows, one isolated call "
+                        "each, weights rotated over copies larger than twice the L2",
+            "bytes_per_call": "m k + 4 m + 4 rows k + 4 rows m", "cpu": "oracle, 1 host thread",
+            "cases": cases}
+
+
+def run_gemv_sweep(args):
+    from zynfer_b200 import cuda as zc
+    gpu = zc.Gpu(0)
+    shapes = GEMV_SHAPES
+    if args.sweep_shape:
+        shapes = [tuple(int(v) for v in args.sweep_shape.lower().split("x"))]
+    for rec in linear_sweep(gpu, args.sweep_calls, shapes):
+        print(json.dumps(rec), flush=True)
     gpu.close()
 
 

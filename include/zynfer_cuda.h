@@ -261,13 +261,15 @@ ZYNFER_CU_API int zynfer_cu_block_forward(ZynferCuCtx *ctx, uint32_t layer, uint
 
 /* ---- op level (device pointers; run on the context stream) ---- */
 /* matvecQ8 / matmul over `batch` rows (ops.zig:181-197): y[b][m] = (W[m,:] . x[b,:]) * scale[m].
- * x must be 16-byte aligned and y 8-byte aligned. */
+ * w and x must be 16-byte aligned and y 8-byte aligned. */
 ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, const float *scale,
                      const float *x, uint32_t batch, uint32_t m, uint32_t k, float *y);
-/* Kernel family for linear layers: "auto" (model schedules: CUDA-core GEMV for
- * one activation row except the LM head, tcgen05 tensor cores otherwise;
- * zynfer_cu_linear likewise: the GEMV for one row of at most 16384 outputs), "gemv",
- * "tcgen05", or "simt" (the CUDA-core tiled GEMM, kept for comparisons).
+/* Kernel family for linear layers: "auto" (model schedules and zynfer_cu_linear:
+ * the CUDA-core GEMV for one activation row, the few-row integer-MMA kernel for
+ * 2..6 int8 rows, each up to 16384 outputs; tcgen05 tensor cores otherwise),
+ * "gemv", "mma" (int8, 2..8 rows of k <= 3072 or 9..16 rows of k <= 1024; its
+ * results equal the tcgen05 path's bit for bit), "tcgen05", or "simt" (the CUDA-core tiled GEMM, kept for
+ * comparisons). A family that cannot take a call falls back to tcgen05.
  * Applies to later calls of this context. */
 ZYNFER_CU_API int zynfer_cu_set_linear_path(ZynferCuCtx *ctx, const char *path);
 /* Decode schedule for zynfer_cu_decode_step / zynfer_cu_generate: "kernels"

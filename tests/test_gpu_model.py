@@ -93,22 +93,59 @@ def test_decode_teacher_forced_matches_oracle(small, oracle_small):
     assert small.seq_len(2) == 30 + 12
 
 
-def test_batched_decode_each_row_matches_oracle(small, oracle_small):
-    for batch in (3, 12):  # gemv path (<= 8 rows) and tiled-GEMM path
-        lens = [5 + 13 * i for i in range(batch)]
-        seqs = list(range(batch))
-        sessions = []
-        for sq, n in zip(seqs, lens):
-            ids = O.synth_tokens(n, SEED + sq, 3, SMALL["vocab"])
-            small.prefill(sq, ids, want_logits=False)
-            ses = oracle_small.session(256)
-            ses.forward(ids, want_logits=False)
-            sessions.append(ses)
-        for step in range(3):
-            toks = O.synth_tokens(batch, 100 + step, 3, SMALL["vocab"])
-            am, logits = small.decode_step(seqs, toks, want_logits=True)
-            for r in range(batch):
-                check_logits(sessions[r].forward([toks[r]]), logits[r], f"B={batch} row {r} step {step}")
+@pytest.mark.parametrize("path", ["auto", "gemv", "mma", "tcgen05"])
+def test_batched_decode_each_row_matches_oracle(gpu, small, oracle_small, path):
+    # every linear family at a few rows (norm prologue, residual, SwiGLU and
+    # argmax epilogues), past the GEMV's 8 rows, and at the few-row kernel's 16
+    gpu.set_linear_path(path)
+    try:
+        for batch in (3, 8, 12, 16):
+            lens = [5 + 13 * i for i in range(batch)]
+            seqs = list(range(batch))
+            sessions = []
+            for sq, n in zip(seqs, lens):
+                ids = O.synth_tokens(n, SEED + sq, 3, SMALL["vocab"])
+                small.prefill(sq, ids, want_logits=False)
+                ses = oracle_small.session(256)
+                ses.forward(ids, want_logits=False)
+                sessions.append(ses)
+            for step in range(3):
+                toks = O.synth_tokens(batch, 100 + step, 3, SMALL["vocab"])
+                am, logits = small.decode_step(seqs, toks, want_logits=True)
+                if path != "auto" and batch <= (8 if path == "gemv" else 16):
+                    assert f"{path}" in gpu.last_path, gpu.last_path
+                for r in range(batch):
+                    check_logits(sessions[r].forward([toks[r]]), logits[r],
+                                 f"{path} B={batch} row {r} step {step}")
+                    assert int(am[r]) == int(np.argmax(logits[r]))
+            for ses in sessions:
+                ses.close()
+    finally:
+        gpu.set_linear_path("auto")
+
+
+def test_few_row_decode_equals_tcgen05_decode(gpu, small):
+    # the few-row MMA linears reproduce the tcgen05 linears bit for bit, so a
+    # whole decode step (norms, residuals, SwiGLU, attention, LM head) does too
+    logits = {}
+    for path in ("mma", "tcgen05"):
+        gpu.set_linear_path(path)
+        try:
+            for batch in (2, 7, 16):
+                seqs = list(range(batch))
+                for sq in seqs:
+                    small.prefill(sq, O.synth_tokens(9 + 5 * sq, SEED + sq, 4, SMALL["vocab"]), want_logits=False)
+                for step in range(2):
+                    toks = O.synth_tokens(batch, 200 + step, 3, SMALL["vocab"])
+                    _, lg = small.decode_step(seqs, toks, want_logits=True)
+                    logits[(path, batch, step)] = lg.copy()
+                if path == "mma":
+                    assert "mma" in gpu.last_path, gpu.last_path
+        finally:
+            gpu.set_linear_path("auto")
+    for (path, batch, step), lg in logits.items():
+        if path == "mma":
+            assert np.array_equal(lg, logits[("tcgen05", batch, step)]), (batch, step)
 
 
 def test_generate_graph_equals_stepwise(small):

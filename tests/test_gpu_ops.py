@@ -112,9 +112,13 @@ def test_linear_q8_each_path(gpu, path, m, k, batch):  # ops.zig:181-197 on ever
 
 
 @pytest.mark.parametrize("m,k,batch,expect", [(4096, 1024, 1, "linear:gemv"), (1024, 3072, 1, "linear:gemv"),
-                                              (4096, 1024, 2, "linear:tcgen05"), (16512, 1024, 1, "linear:tcgen05")])
+                                              (4096, 1024, 2, "linear:mma"), (1024, 3072, 6, "linear:mma"),
+                                              (1024, 1024, 7, "linear:tcgen05"), (1024, 1024, 16, "linear:tcgen05"),
+                                              (4096, 1024, 17, "linear:tcgen05"), (16512, 1024, 1, "linear:tcgen05"),
+                                              (16512, 1024, 4, "linear:tcgen05")])
 def test_linear_q8_auto_reports_the_kernel_it_ran(gpu, m, k, batch, expect):  # ops.zig:181-197
-    # auto: the GEMV for one activation row of at most 16384 outputs, tcgen05 otherwise
+    # auto: the GEMV for one activation row, the few-row MMA kernel for 2..6
+    # rows, each for at most 16384 outputs; tcgen05 otherwise
     w = O.synth_normal(m * k, 33, m + k, 0.02).reshape(m, k)
     q, s = O.pack_row_q8(w)
     x = O.synth_normal(batch * k, 34, batch, 1.0).reshape(batch, k)
@@ -127,6 +131,56 @@ def test_linear_q8_auto_reports_the_kernel_it_ran(gpu, m, k, batch, expect):  # 
     for b in range(batch):
         ref = O.matvec_q8(q, s, x[b])
         assert O.expect_close(ref, got[b], 2e-4, 2e-4), (b, O.diff(ref, got[b]).max_abs)
+
+
+@pytest.mark.parametrize("m,k", [(4096, 1024), (6144, 1024), (1024, 2048), (1024, 3072), (3072, 1024), (512, 4096)])
+@pytest.mark.parametrize("batch", [2, 5, 8, 9, 16])
+def test_linear_q8_few_rows_equals_tcgen05_and_oracle(gpu, m, k, batch):  # ops.zig:200-228
+    # the few-row MMA kernel builds the plane kernel's digits itself and sums
+    # them exactly: its outputs equal the tcgen05 path's bit for bit
+    w = O.synth_normal(m * k, 41, m + k, 0.02).reshape(m, k)
+    q, s = O.pack_row_q8(w)
+    x = O.synth_normal(batch * k, 42, batch, 1.0).reshape(batch, k)
+    x[-1, :5] *= 80.0  # one row with a larger fixed-point exponent
+    x[0, :] = 0.0      # and an all-zero row
+    fits = k <= (3072 if batch <= 8 else 1024)  # the activation rows it holds in registers
+    got = {}
+    for path in ("mma", "tcgen05"):
+        y = torch.full((batch, m), float("nan"), dtype=torch.float32, device="cuda")
+        gpu.set_linear_path(path)
+        try:
+            gpu.linear(zc.W_Q8, dev(q), dev(s), dev(x), batch, m, k, y)
+            gpu.sync()
+            assert gpu.last_path == f"linear:{path if fits else 'tcgen05'}"
+        finally:
+            gpu.set_linear_path("auto")
+        got[path] = host(y)
+    assert np.array_equal(got["mma"], got["tcgen05"])
+    for b in range(batch):
+        ref = O.matvec_q8(q, s, x[b])
+        d = O.diff(ref, got["mma"][b])
+        assert O.expect_close(ref, got["mma"][b], 2e-4, 2e-4), (b, d.max_abs, d.failing_index)
+
+
+@pytest.mark.parametrize("k,batch", [(1024, 17), (1024, 24), (2048, 9), (4096, 2)])
+def test_linear_q8_few_rows_falls_back_where_it_cannot_run(gpu, k, batch):
+    # more than 16 rows, or more activation values than it holds in registers:
+    # the tcgen05 path runs instead
+    m = 1024
+    w = O.synth_normal(m * k, 43, 1, 0.02).reshape(m, k)
+    q, s = O.pack_row_q8(w)
+    x = O.synth_normal(batch * k, 44, batch, 1.0).reshape(batch, k)
+    y = torch.empty((batch, m), dtype=torch.float32, device="cuda")
+    gpu.set_linear_path("mma")
+    try:
+        gpu.linear(zc.W_Q8, dev(q), dev(s), dev(x), batch, m, k, y)
+        gpu.sync()
+        assert gpu.last_path == "linear:tcgen05"
+    finally:
+        gpu.set_linear_path("auto")
+    got = host(y)
+    for b in range(batch):
+        assert O.expect_close(O.matvec_q8(q, s, x[b]), got[b], 2e-4, 2e-4), b
 
 
 @pytest.mark.parametrize("path", ["tcgen05", "simt"])

@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libzynfer_cuda.so")
 OBJ = os.path.join(HERE, "_build")
-SOURCES = ["synth.cu", "norm.cu", "gemv.cu", "gemm_simt.cu", "attn.cu", "decode_flow.cu", "tc_gemm.cu", "static_linear.cu", "artifact.cu", "sample.cu", "shim.cu"]
+SOURCES = ["synth.cu", "norm.cu", "gemv.cu", "fewrow.cu", "gemm_simt.cu", "attn.cu", "decode_flow.cu", "tc_gemm.cu", "static_linear.cu", "artifact.cu", "sample.cu", "shim.cu"]
 HEADERS = ["attn_common.cuh", "common.cuh", "kernels.h", "synth_rng.h", "tc_gemm.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",

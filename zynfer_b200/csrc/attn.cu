@@ -99,7 +99,6 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
     uint16_t* kvnew = reinterpret_cast<uint16_t*>(qb + kG * kD);
     constexpr unsigned kAll = 0xFFFFFFFFu;
 
-    pdl_launch_dependents();
     const int B = a.B;
     const int max_len = a.max_blocks * kKvBlock;
     // Row-major prefix of KV block counts. Positions and block tables are
@@ -213,6 +212,7 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
     int pos = n > 0 ? a.positions[cc.b] : 0;  // the first piece's position and RoPE row, before the wait
     attn::ShareAux aux = attn::share_aux(src, pos);
     pdl_wait();
+    pdl_launch_dependents();  // after the wait: the next linear's early weight loads do not delay this one's start
 
     const int g = lane >> 2, t = lane & 3;
     const int mi = lane >> 3, ri = lane & 7;

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "kernels.h"
+
 namespace zc {
 
 constexpr int kWarp = 32;
@@ -69,6 +71,31 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
     return v;
+}
+
+// The int8 digit planes of four activation values f (|f| < 2^e, 2^e a row's
+// power-of-two scale): q = rint(f 2^(22-e)),
+// |q| <= 2^22, written q = d0 2^16 + d1 2^8 + d2 with d1, d2 in [-128, 127].
+// 2^(22-e) is a float whenever 22 - e <= 127, and then f * 2^(22-e) is the
+// same correctly rounded product ldexpf returns; with u = q + 0x8080, d2 and
+// d1 are bytes 0 and 1 of u minus 128 (the unique such digits) and d0 is
+// u >> 16, whose low byte is byte 2 of u. d0, d1, d2 receive the four
+// values' digits as packed int8.
+__device__ __forceinline__ void digits4(const float (&f)[4], int e, uint32_t& d0, uint32_t& d1, uint32_t& d2) {
+    uint32_t u[4];
+    if (22 - e <= 127) {
+        const float p2 = __int_as_float((22 - e + 127) << 23);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) u[j] = (uint32_t)(__float2int_rn(__fmul_rn(f[j], p2)) + 0x8080);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) u[j] = (uint32_t)(__float2int_rn(ldexpf(f[j], 22 - e)) + 0x8080);
+    }
+    const uint32_t lo01 = __byte_perm(u[0], u[1], 0x5140), lo23 = __byte_perm(u[2], u[3], 0x5140);
+    const uint32_t hi01 = __byte_perm(u[0], u[1], 0x7362), hi23 = __byte_perm(u[2], u[3], 0x7362);
+    d2 = __byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u;
+    d1 = __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u;
+    d0 = __byte_perm(hi01, hi23, 0x5410);
 }
 
 // Orderable key for a (logit, index) pair: a larger key is a larger logit,
@@ -182,6 +209,22 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 // L2 prefetch of one cache line (weights that do not depend on a predecessor).
 __device__ __forceinline__ void prefetch_l2(const void* p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// Every thread of the grid prefetches its share of the ranges' 128-byte lines
+// into L2 with the evict-last priority, so they survive the KV streaming of an
+// attention launch in between. Weights never depend on an earlier kernel, so
+// this runs before griddepcontrol.wait.
+__device__ __forceinline__ void prefetch_l2_ranges(const L2Range (&r)[2]) {
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    const size_t step = (size_t)gridDim.x * blockDim.x * 128;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        if (!r[i].p) continue;
+        const char* base = static_cast<const char*>(r[i].p);
+        for (size_t off = tid * 128; off < r[i].bytes; off += step)
+            asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(base + off));
+    }
 }
 
 }  // namespace zc

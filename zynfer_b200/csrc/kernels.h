@@ -9,6 +9,12 @@ namespace zc {
 
 enum WKind : int { kWQ8 = 0, kWBF16 = 1 };
 
+// A byte range of a later kernel's weights to bring into L2 (p null: none).
+struct L2Range {
+    const void* p;
+    uint32_t bytes;
+};
+
 // Linear-layer epilogues.
 enum Epi : int {
     kEpiNone = 0,     // y = acc * scale
@@ -33,6 +39,7 @@ struct LinearArgs {
     float eps = 1e-6f;
     unsigned long long* argmax_keys = nullptr;  // [N] for kEpiArgmax
     uint32_t* err = nullptr;       // device error word (bounded waits)
+    L2Range pf[2] = {};            // the next linear's weights and scales, prefetched into L2
 };
 
 // synth.cu
@@ -127,6 +134,14 @@ void launch_sample(const SampleArgs& a, cudaStream_t st);
 
 // gemv.cu (N <= 8)
 void launch_gemv(const LinearArgs& a, cudaStream_t st);
+// The GEMV stages its N activation rows of K values in shared memory: true
+// when they fit.
+bool gemv_fits(int N, int K);
+// fewrow.cu: int8 weights, 2..16 rows, RMSNorm prologue and none / residual /
+// SwiGLU epilogues in one launch (results equal the tcgen05 path's)
+bool fewrow_fits(const LinearArgs& a);
+void prepare_fewrow_kernels();
+void launch_fewrow(const LinearArgs& a, cudaStream_t st);
 // gemm_simt.cu (any N)
 void launch_gemm_simt(const LinearArgs& a, cudaStream_t st);
 

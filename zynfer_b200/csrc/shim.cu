@@ -29,11 +29,14 @@ namespace {
 
 // Which kernel runs a linear layer: the CUDA-core GEMV (few rows), the
 // tensor-core tcgen05 path, or the CUDA-core tiled GEMM (kept for A/B checks).
-enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3 };
+enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3, kPathMma = 4 };
 // Decode schedule: separate kernels per op (graph-captured; what auto takes),
 // or one persistent dataflow kernel per step for small int8 batches (on request).
 enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2 };
 constexpr int kGemvMaxM = 16384;  // model auto policy: largest matrix (output rows) for the batch-1 GEMV
+// auto policy: most activation rows for the few-row MMA kernel (measured in a
+// decode step: 10 % faster than tcgen05 at 4 rows, level at 6, 13 % slower at 8)
+constexpr int kFewRowAutoMax = 6;
 
 struct LayerDev {
     void* wqkv = nullptr;
@@ -139,6 +142,7 @@ struct ZynferCuCtx {
     uint8_t* planes = nullptr;
     float* exps = nullptr;  // per-row 2^(e-22) of the int8 digit planes
     int tc_tpad = 0, tc_kmax = 0;
+    L2Range pf_next[2] = {};  // prefetch ranges the next linear() passes to its kernel, then clears
     std::map<uint64_t, CUtensorMap> bmaps;
     std::map<std::pair<const void*, uint64_t>, CUtensorMap> amaps;  // op-level weights
     float* simt_xn = nullptr;  // normalised rows for the CUDA-core GEMM path
@@ -250,8 +254,8 @@ bool take_launch_fault(ZynferCuCtx* c) {
 // fixed buffer (no allocation): e.g. "decode:gemv+tcgen05:graph".
 void set_path(ZynferCuCtx* c, const char* call, unsigned paths, const char* mode) {
     char fam[48] = "";
-    const char* names[4] = {"auto", "gemv", "simt", "tcgen05"};
-    for (int b = 1; b < 4; ++b)
+    const char* names[5] = {"auto", "gemv", "simt", "tcgen05", "mma"};
+    for (int b = 1; b < 5; ++b)
         if (paths & (1u << b)) {
             if (fam[0]) strncat(fam, "+", sizeof(fam) - strlen(fam) - 1);
             strncat(fam, names[b], sizeof(fam) - strlen(fam) - 1);
@@ -383,8 +387,9 @@ const CUtensorMap* b_map(ZynferCuCtx* c, int wkind, int K, int nt) {
 }
 
 // y = linear(norm_w ? rmsnorm(x) : x) with the epilogue `epi`, on the path the
-// policy picks: GEMV (x staged in shared memory) for a few rows, tcgen05 for more.
-// Returns the kernel family it launched (kPathGemv, kPathTc or kPathSimt).
+// policy picks: GEMV (x staged in shared memory) for one row, the few-row
+// integer-MMA kernel for 2..16 int8 rows, tcgen05 for more.
+// Returns the kernel family it launched (kPathGemv, kPathMma, kPathTc or kPathSimt).
 int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtensorMap* tmA, int M, int K,
            const float* x, int N, float* y, int epi, const float* resid, const float* norm_w,
            unsigned long long* keys, int wkind = -1) {
@@ -393,17 +398,28 @@ int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtenso
     a.w = w; a.scale = s; a.wkind = wkind; a.M = M; a.K = K; a.x = x; a.ldx = K; a.N = N;
     a.y = y; a.ldy = epi == kEpiSwiGLU ? M / 2 : M; a.epi = epi; a.resid = resid; a.norm_w = norm_w;
     a.eps = c->d.eps > 0.0f ? c->d.eps : 1e-6f; a.argmax_keys = keys; a.err = c->derr;
+    a.pf[0] = c->pf_next[0]; a.pf[1] = c->pf_next[1];
+    c->pf_next[0] = c->pf_next[1] = L2Range{nullptr, 0};
     int path = c->path_policy;
     // auto: one activation row -> GEMV (no plane kernel, one launch) except the
-    // vocabulary-sized LM head; more rows -> tcgen05 (measured faster from 2 up)
-    if (path == kPathAuto) path = (N == 1 && M <= kGemvMaxM) ? kPathGemv : kPathTc;
-    if (path == kPathGemv && N > 8) path = kPathTc;
+    // vocabulary-sized LM head; 2..6 int8 rows -> the few-row kernel (one
+    // launch, no plane kernel) up to the same size; more rows -> tcgen05
+    if (path == kPathAuto) {
+        if (N == 1 && M <= kGemvMaxM) path = kPathGemv;
+        else if (N > 1 && N <= kFewRowAutoMax && M <= kGemvMaxM && fewrow_fits(a)) path = kPathMma;
+        else path = kPathTc;
+    }
+    if (path == kPathGemv && !gemv_fits(N, K)) path = kPathTc;
+    if (path == kPathMma && !fewrow_fits(a)) path = kPathTc;
     if (path == kPathTc && (!tmA || N > c->tc_tpad || K > c->tc_kmax || K > kPlanesMaxK)) path = kPathSimt;
     TimedEvent* te;
     tbegin(c, cls, &te);
     c->step_paths |= 1u << path;
     if (path == kPathGemv) {
         launch_gemv(a, c->stream);
+        c->step_launches += 1;
+    } else if (path == kPathMma) {
+        launch_fewrow(a, c->stream);
         c->step_launches += 1;
     } else if (path == kPathSimt) {
         if (norm_w) {
@@ -418,7 +434,8 @@ int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtenso
         const int nt = tc_tile_tokens(wkind, N);
         TcLaunch L;
         L.tmA = tmA;
-        L.args = TcArgs{M, K, N, c->tc_tpad, wkind, epi, s, c->exps, y, a.ldy, resid, keys, c->derr};
+        L.args = TcArgs{M, K, N, c->tc_tpad, wkind, epi, s, c->exps, y, a.ldy, resid, keys, c->derr, 0,
+                        {a.pf[0], a.pf[1]}};
         L.sms = c->caps.sm_count > 0 ? c->caps.sm_count : 148;
         const int S = tc_cluster_size(M, N, K, wkind, epi, L.sms);
         PlanesArgs pa{x, K, N, K, c->tc_tpad, wkind, norm_w, a.eps, c->planes, c->exps};
@@ -508,6 +525,14 @@ void enqueue_decode_persistent(ZynferCuCtx* c, int B, bool want_logits) {
     }
 }
 
+// The next linear() call prefetches into L2 the weights and row scales of the
+// linear that follows it in the step (rows x cols), so that one reads them
+// from L2 instead of HBM.
+void set_prefetch(ZynferCuCtx* c, const void* w, const float* s, size_t rows, size_t cols) {
+    c->pf_next[0] = L2Range{w, (uint32_t)(rows * cols * (c->wkind == kWQ8 ? 1 : 2))};
+    c->pf_next[1] = L2Range{s, s ? (uint32_t)(rows * sizeof(float)) : 0u};
+}
+
 void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
     if (use_persistent(c, B)) {
         enqueue_decode_persistent(c, B, want_logits);
@@ -523,6 +548,7 @@ void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
     c->step_launches += 1;
     for (uint32_t l = 0; l < m.layers; ++l) {
         const LayerDev& Ld = c->L[l];
+        set_prefetch(c, Ld.wo, Ld.so, H, c->qd);
         linear(c, ZYNFER_CU_K_LINEAR, Ld.wqkv, Ld.sqkv, &Ld.tm_qkv, c->qkv_rows, H, c->dx, B, c->dqkv, kEpiNone,
                nullptr, Ld.input_ln, nullptr);
         // per-head RMSNorm + RoPE and the K/V append run inside the attention kernel
@@ -538,14 +564,19 @@ void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
         launch_attn_decode(aa, c->stream);
         tend(c, te);
         c->step_launches += 1;
+        set_prefetch(c, Ld.wgu, Ld.sgu, 2 * I, H);
         linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, &Ld.tm_o, H, c->qd, c->dattn, B, c->dx1, kEpiResid, c->dx,
                nullptr, nullptr);
+        set_prefetch(c, Ld.wd, Ld.sd, H, I);
         linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, &Ld.tm_gu, 2 * I, H, c->dx1, B, c->dh, kEpiSwiGLU, nullptr,
                Ld.post_ln, nullptr);
+        if (l + 1 < m.layers) set_prefetch(c, c->L[l + 1].wqkv, c->L[l + 1].sqkv, c->qkv_rows, H);
         linear(c, ZYNFER_CU_K_LINEAR, Ld.wd, Ld.sd, &Ld.tm_d, H, I, c->dh, B, c->dx, kEpiResid, c->dx1, nullptr,
                nullptr);
     }
     const bool sampling = c->samp_temp > 0.0f;
+    // the LM head prefetches the next step's first linear
+    if (m.layers > 0) set_prefetch(c, c->L[0].wqkv, c->L[0].sqkv, c->qkv_rows, H);
     linear(c, ZYNFER_CU_K_LMHEAD, c->embed, c->sembed, &c->tm_embed, m.vocab, H, c->dx, B,
            want_logits || sampling ? c->dlogits : nullptr, kEpiArgmax, nullptr, c->final_norm, c->dkeys);
     if (sampling) enqueue_sample(c, B, c->dseq, c->dpos, 0, 0);
@@ -1530,8 +1561,8 @@ int zynfer_cu_linear(ZynferCuCtx* c, int wkind, const void* w, const float* scal
     if (wkind != ZYNFER_CU_W_Q8 && wkind != ZYNFER_CU_W_BF16) return fail(c, ZYNFER_CU_INVALID, "unknown weight kind");
     if (wkind == ZYNFER_CU_W_Q8 && !scale) return fail(c, ZYNFER_CU_INVALID, "int8 weights need scales");
     if (k % 512) return fail(c, ZYNFER_CU_UNSUPPORTED, "k must be a multiple of 512");
-    if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 8)
-        return fail(c, ZYNFER_CU_INVALID, "x must be 16-byte and y 8-byte aligned");
+    if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 8)
+        return fail(c, ZYNFER_CU_INVALID, "w and x must be 16-byte and y 8-byte aligned");
     if (m % 128) return fail(c, ZYNFER_CU_UNSUPPORTED, "m must be a multiple of 128");
     if (take_launch_fault(c)) return ZYNFER_CU_LAUNCH;
     cudaSetDevice(c->device);
@@ -1609,6 +1640,7 @@ int zynfer_cu_set_linear_path(ZynferCuCtx* c, const char* path) {
     else if (!strcmp(path, "gemv")) c->path_policy = kPathGemv;
     else if (!strcmp(path, "simt")) c->path_policy = kPathSimt;
     else if (!strcmp(path, "tcgen05")) c->path_policy = kPathTc;
+    else if (!strcmp(path, "mma")) c->path_policy = kPathMma;
     else return fail(c, ZYNFER_CU_INVALID, std::string("unknown linear path ") + path);
     for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second.exec);  // graphs bake the old choice
     c->graphs.clear();

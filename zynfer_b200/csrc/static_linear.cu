@@ -99,7 +99,7 @@ extern "C" int zynfer_cu_linear_q8_static(const int8_t* w, const float* scale, c
     L.tmA = &tmA;
     L.tmB = &tmB;
     L.args = zc::TcArgs{(int)m, (int)k, (int)batch, kPadRows, zc::kWQ8, zc::kEpiNone, scale, d->xscale, y, (int)m,
-                        nullptr, nullptr, d->err, g_stall_next.exchange(false) ? 1 : 0};
+                        nullptr, nullptr, d->err, g_stall_next.exchange(false) ? 1 : 0, {}};
     L.sms = d->sms;
     zc::launch_prep_planes(pa, st);
     zc::launch_tc_gemm(L, st);

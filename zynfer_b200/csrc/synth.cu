@@ -51,6 +51,7 @@ void prepare_all_kernels() {
     prepare_flow_kernels();
     prepare_tc_kernels();
     prepare_sample_kernels();
+    prepare_fewrow_kernels();
 }
 
 int device_sm_count() {

@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
 
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     pdl_launch_dependents();
+    prefetch_l2_ranges(a.pf);
     const int m_tiles = a.M / kBM;
     const int n_tiles = (a.T + NT - 1) / NT;
     const int units = m_tiles * n_tiles;
@@ -512,6 +513,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_cluster_kernel(const __grid_
 
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     pdl_launch_dependents();
+    prefetch_l2_ranges(a.pf);
     const int S = (int)cluster_size(), rank = (int)cluster_rank();
     const int m_tiles = a.M / kBM;
     const int tile = blockIdx.x / S;
@@ -693,24 +695,11 @@ __global__ void __launch_bounds__(kPrepThreads) prep_planes_kernel(PlanesArgs a)
             const int k = 4 * (threadIdx.x + i * kPrepThreads);
             if (k >= K) break;
             const float f[4] = {val(w[i].x, v[i].x), val(w[i].y, v[i].y), val(w[i].z, v[i].z), val(w[i].w, v[i].w)};
-            char4 d0, d1, d2;
-            int8_t* o0 = &d0.x;
-            int8_t* o1 = &d1.x;
-            int8_t* o2 = &d2.x;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int q = __float2int_rn(ldexpf(f[j], 22 - e));  // |q| <= 2^22
-                const int q2 = (int)(int8_t)(q & 0xFF);
-                const int q1v = (q - q2) >> 8;
-                const int q1 = (int)(int8_t)(q1v & 0xFF);
-                const int q0 = (q1v - q1) >> 8;  // |q0| <= 64
-                o0[j] = (int8_t)q0;
-                o1[j] = (int8_t)q1;
-                o2[j] = (int8_t)q2;
-            }
-            *reinterpret_cast<char4*>(p0 + k) = d0;
-            *reinterpret_cast<char4*>(p0 + plane + k) = d1;
-            *reinterpret_cast<char4*>(p0 + 2 * plane + k) = d2;
+            uint32_t d0, d1, d2;
+            digits4(f, e, d0, d1, d2);
+            *reinterpret_cast<uint32_t*>(p0 + k) = d0;
+            *reinterpret_cast<uint32_t*>(p0 + plane + k) = d1;
+            *reinterpret_cast<uint32_t*>(p0 + 2 * plane + k) = d2;
         }
     } else {
         uint16_t* p0 = reinterpret_cast<uint16_t*>(a.planes) + (size_t)t * K;

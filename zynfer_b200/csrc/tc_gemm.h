@@ -36,6 +36,7 @@ struct TcArgs {
     unsigned long long* argmax_keys;
     uint32_t* err;
     int stall;  // fault injection: 1 = no CTA loads its first stage, so the MMA warp's bounded wait runs out
+    L2Range pf[2];  // the next linear's weights and scales, prefetched into L2
 };
 
 struct TcLaunch {

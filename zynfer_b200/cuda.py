@@ -263,7 +263,7 @@ class Gpu:
         self.check(lib().zynfer_cu_linear(self.h, wkind, _ptr(w), _ptr(scale), _ptr(x), batch, m, k, _ptr(y)))
 
     def set_linear_path(self, path: str):
-        """"auto" | "gemv" | "tcgen05" | "simt"."""
+        """"auto" | "gemv" | "mma" | "tcgen05" | "simt"."""
         self.check(lib().zynfer_cu_set_linear_path(self.h, path.encode()))
 
     def set_sampling(self, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0, seed: int = 0):
