@@ -470,40 +470,62 @@ __global__ void __maxnreg__(192) attn_decode_row_kernel(AttnDecodeArgs a) { attn
 // ------------------------------------------------------------ prefill
 //
 // Causal GQA prefill attention on the tensor cores (mma.sync m16n8k16, bf16
-// in, f32 accumulate), flash-attention style. CTA = (32-query tile, kv
-// head): warps 0-1 take rows 16w.. of query head 2 kvh, warps 2-3 of head
-// 2 kvh + 1, so both heads share each staged K/V tile. Every f32 operand is
+// in, f32 accumulate), flash-attention style. CTA = (32-query tile, kv head),
+// 8 warps: warp w takes query head 2 kvh + (w >> 2), rows 16 ((w >> 1) & 1)
+// of the tile, and the key half (w & 1) of every 64-key tile, so both heads
+// share each staged K/V tile and a tile's MMAs are spread over twice the
+// warps; the two halves' softmax states merge once at the end. f32 q is
 // split into two bf16 terms (x = hi + lo to 2^-18 relative) and each product
-// is taken as hi*hi + hi*lo + lo*hi (three MMAs), so S and P V carry f32-grade
-// accuracy; the K/V tiles are staged as hi and lo bf16 copies (64 keys x 128
-// dims, rows chunk-swizzled for conflict-free ldmatrix). Keys after the query
-// or past T are masked (kv_len == q_len == T, ops.zig:322).
-constexpr int PQ = 32, PK = 64, PTHREADS = 128;
-constexpr int kTileElems = PK * kD;                     // one bf16 copy of a K or V tile
-constexpr size_t kPrefillSmem = (size_t)4 * kTileElems * 2;  // K hi, K lo, V hi, V lo
+// is taken as q_hi k_hi + q_hi k_lo + q_lo k_hi (likewise P V), so S and P V
+// carry f32-grade accuracy; when K and V are exact bf16 (the cache's
+// values) their lo terms are zero and skipped. K and V arrive from qkv_post
+// already split into bf16 planes, and each 64-key tile is copied with
+// cp.async into a double buffer (16-byte chunks of each row XOR-swizzled by
+// row for conflict-free ldmatrix) while the previous tile is computed. Keys
+// after the query or past T are masked (kv_len == q_len == T, ops.zig:322).
+constexpr int PQ = 32, PK = 64, PTHREADS = 256;
+constexpr int kTileBytes = PK * kD * 2;  // one bf16 plane of a K or V tile
+constexpr size_t kPrefillSmem = (size_t)2 * 4 * kTileBytes;  // two stages of K hi, K lo, V hi, V lo
 
-// element (row, dim) of a staged 64 x 128 bf16 tile, 16-byte chunks XOR-swizzled by row
-__device__ __forceinline__ int tile_swz(int r, int e) { return r * kD + ((((e >> 3) ^ (r & 7)) << 3) | (e & 7)); }
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 __global__ void __launch_bounds__(PTHREADS, 1) attn_prefill_kernel(AttnPrefillArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    uint16_t* khi = reinterpret_cast<uint16_t*>(smem_raw);
-    uint16_t* klo = khi + kTileElems;
-    uint16_t* vhi = klo + kTileElems;
-    uint16_t* vlo = vhi + kTileElems;
     constexpr unsigned kAll = 0xFFFFFFFFu;
-
-    pdl_launch_dependents();
     pdl_wait();
+    pdl_launch_dependents();
     const int qt = gridDim.x - 1 - blockIdx.x, kvh = blockIdx.y;  // longest (causal) tiles first
     const int T = a.T;
     const int q0 = qt * PQ;
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-    const int h = kvh * kG + (warp >> 1);       // query head of this warp
-    const int r0 = q0 + (warp & 1) * 16;         // first query row of this warp
+    const int hs = warp >> 2, kh = warp & 1;
+    const int h = kvh * kG + hs;                 // query head of this warp
+    const int r0 = q0 + ((warp >> 1) & 1) * 16;  // first query row of this warp
     const int g = lane >> 2, t = lane & 3;
     const int mi = lane >> 3, ri = lane & 7;
     const float scale = 1.0f / sqrtf((float)kD);
+    const bool lo = a.lo_terms != 0;
+    const int nplanes = lo ? 4 : 2;  // staged planes: K hi, (K lo), V hi, (V lo)
+    const int stage_bytes = nplanes * kTileBytes;
+    const size_t plane = (size_t)a.n_kv * T * kD;
+
+    // copy the 64-key tile starting at k0 into stage s (keys past T as zeros)
+    auto issue = [&](int k0, int s) {
+        const uint32_t base = smem_addr(smem_raw) + (uint32_t)(s * stage_bytes);
+        const int chunks = nplanes * PK * (kD / 8);
+        for (int i = threadIdx.x; i < chunks; i += PTHREADS) {
+            const int c = i % (kD / 8), r = (i / (kD / 8)) % PK, sp = i / (PK * (kD / 8));
+            const int p = lo ? sp : 2 * sp;  // source plane
+            const bool valid = k0 + r < T;
+            const uint16_t* src = a.kv_planes + (size_t)p * plane + ((size_t)kvh * T + (valid ? k0 + r : 0)) * kD + 8 * c;
+            cp_async16(base + (uint32_t)(sp * kTileBytes + r * kD * 2 + ((c ^ (r & 7)) << 4)), src, valid);
+        }
+    };
 
     // Q fragments (A operand, 16 rows x 16 dims per k-step), hi and lo terms
     uint32_t qa[8][4], qb[8][4];
@@ -533,135 +555,155 @@ __global__ void __launch_bounds__(PTHREADS, 1) attn_prefill_kernel(AttnPrefillAr
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // rows g and g + 8
 
     const int last_key = min(q0 + PQ, T);  // keys [0, last_key)
-    const float* kg = a.k + (size_t)kvh * T * kD;
-    const float* vg = a.v + (size_t)kvh * T * kD;
-    for (int k0 = 0; k0 < last_key; k0 += PK) {
-        __syncthreads();  // previous tile fully consumed
-        // stage K and V (f32 -> bf16 hi / lo), keys past T as zeros
-        for (int i = threadIdx.x; i < PK * kD / 4; i += PTHREADS) {
-            const int r = i / (kD / 4), e = 4 * (i % (kD / 4));
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (k0 + r < T) {
-                kv = *reinterpret_cast<const float4*>(kg + (size_t)(k0 + r) * kD + e);
-                vv = *reinterpret_cast<const float4*>(vg + (size_t)(k0 + r) * kD + e);
-            }
-            const int off = tile_swz(r, e);
-            *reinterpret_cast<uint2*>(khi + off) = make_uint2(attn::pack_terms(kv.x, kv.y, false), attn::pack_terms(kv.z, kv.w, false));
-            *reinterpret_cast<uint2*>(klo + off) = make_uint2(attn::pack_terms(kv.x, kv.y, true), attn::pack_terms(kv.z, kv.w, true));
-            *reinterpret_cast<uint2*>(vhi + off) = make_uint2(attn::pack_terms(vv.x, vv.y, false), attn::pack_terms(vv.z, vv.w, false));
-            *reinterpret_cast<uint2*>(vlo + off) = make_uint2(attn::pack_terms(vv.x, vv.y, true), attn::pack_terms(vv.z, vv.w, true));
-        }
+    const int ntiles = (last_key + PK - 1) / PK;
+    issue(0, 0);
+    cp_async_commit();
+    for (int it = 0; it < ntiles; ++it) {
+        const int k0 = it * PK;
+        if (it + 1 < ntiles) issue(k0 + PK, (it + 1) & 1);
+        cp_async_commit();
+        cp_async_wait_1();  // this tile's group is complete
         __syncthreads();
-        if (k0 > r0 + 15) continue;  // every key of this tile is after every query of this warp
-
-        // S = Q K^T over 64 keys: 8 n-tiles of 8 keys; ldmatrix.x4 yields two n-tiles
-        float sacc[8][4];
+        const int kb = k0 + 32 * kh;  // first key of this warp's half
+        if (kb <= r0 + 15) {
+            const uint32_t st = smem_addr(smem_raw) + (uint32_t)((it & 1) * stage_bytes);
+            const uint32_t khi_s = st, klo_s = st + kTileBytes;
+            const uint32_t vhi_s = st + (lo ? 2 : 1) * kTileBytes, vlo_s = st + 3 * kTileBytes;
+            // S = Q K^T over this warp's 32 keys: 4 n-tiles of 8 keys; ldmatrix.x4 yields two
+            float sacc[4][4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
-        const uint32_t khi_s = smem_addr(khi), klo_s = smem_addr(klo);
+            for (int j = 0; j < 4; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
+            for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
-            for (int jp = 0; jp < 4; ++jp) {
-                // matrices: (keys 16jp + 0..7, dims 16ks..+7), (same keys, +8), (keys +8, dims), (keys +8, +8)
-                const int key = 16 * jp + ri + ((mi >> 1) << 3);
-                const int ch = 2 * ks + (mi & 1);
-                const uint32_t off = (uint32_t)(key * kD * 2 + ((ch ^ (key & 7)) << 4));
-                uint32_t h0, h1, h2, h3, l0b, l1b, l2b, l3b;
-                attn::ldsm_x4(khi_s + off, h0, h1, h2, h3);
-                attn::ldsm_x4(klo_s + off, l0b, l1b, l2b, l3b);
-                // n-tile 2jp: (h0, h1), n-tile 2jp + 1: (h2, h3)
-                attn::mma_bf16(sacc[2 * jp], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], h0, h1);
-                attn::mma_bf16(sacc[2 * jp], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], l0b, l1b);
-                attn::mma_bf16(sacc[2 * jp], qb[ks][0], qb[ks][1], qb[ks][2], qb[ks][3], h0, h1);
-                attn::mma_bf16(sacc[2 * jp + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], h2, h3);
-                attn::mma_bf16(sacc[2 * jp + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], l2b, l3b);
-                attn::mma_bf16(sacc[2 * jp + 1], qb[ks][0], qb[ks][1], qb[ks][2], qb[ks][3], h2, h3);
+                for (int jp = 0; jp < 2; ++jp) {
+                    // matrices: (keys 16jp + 0..7, dims 16ks..+7), (same keys, +8), (keys +8, dims), (keys +8, +8)
+                    const int key = 32 * kh + 16 * jp + ri + ((mi >> 1) << 3);
+                    const int ch = 2 * ks + (mi & 1);
+                    const uint32_t off = (uint32_t)(key * kD * 2 + ((ch ^ (key & 7)) << 4));
+                    uint32_t h0, h1, h2, h3;
+                    attn::ldsm_x4(khi_s + off, h0, h1, h2, h3);
+                    attn::mma_bf16(sacc[2 * jp], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], h0, h1);
+                    attn::mma_bf16(sacc[2 * jp], qb[ks][0], qb[ks][1], qb[ks][2], qb[ks][3], h0, h1);
+                    attn::mma_bf16(sacc[2 * jp + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], h2, h3);
+                    attn::mma_bf16(sacc[2 * jp + 1], qb[ks][0], qb[ks][1], qb[ks][2], qb[ks][3], h2, h3);
+                    if (lo) {
+                        uint32_t l0b, l1b, l2b, l3b;
+                        attn::ldsm_x4(klo_s + off, l0b, l1b, l2b, l3b);
+                        attn::mma_bf16(sacc[2 * jp], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], l0b, l1b);
+                        attn::mma_bf16(sacc[2 * jp + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], l2b, l3b);
+                    }
+                }
+            }
+            // scale, causal mask, online softmax (rows g and g + 8 of the warp's 16)
+            const int qa_row = r0 + g, qb_row = r0 + g + 8;
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int key = kb + 8 * j + 2 * t;
+                sacc[j][0] = (key <= qa_row && key < T) ? sacc[j][0] * scale : -INFINITY;
+                sacc[j][1] = (key + 1 <= qa_row && key + 1 < T) ? sacc[j][1] * scale : -INFINITY;
+                sacc[j][2] = (key <= qb_row && key < T) ? sacc[j][2] * scale : -INFINITY;
+                sacc[j][3] = (key + 1 <= qb_row && key + 1 < T) ? sacc[j][3] * scale : -INFINITY;
+                mx0 = fmaxf(mx0, fmaxf(sacc[j][0], sacc[j][1]));
+                mx1 = fmaxf(mx1, fmaxf(sacc[j][2], sacc[j][3]));
+            }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(kAll, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(kAll, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(kAll, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(kAll, mx1, 2));
+            const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+            // a row with no visible key yet keeps max -inf; its terms stay 0
+            const float c0 = n0 == -INFINITY ? 1.0f : expf(m0 - n0);
+            const float c1 = n1 == -INFINITY ? 1.0f : expf(m1 - n1);
+            m0 = n0;
+            m1 = n1;
+            l0 *= c0;
+            l1 *= c1;
+#pragma unroll
+            for (int nt = 0; nt < 16; ++nt) {
+                o[nt][0] *= c0;
+                o[nt][1] *= c0;
+                o[nt][2] *= c1;
+                o[nt][3] *= c1;
+            }
+            uint32_t pa[2][4], pb[2][4];  // P as the A operand of 2 k-steps of 16 keys, hi and lo
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p0 = n0 == -INFINITY ? 0.0f : expf(sacc[j][0] - n0);
+                const float p1 = n0 == -INFINITY ? 0.0f : expf(sacc[j][1] - n0);
+                const float p2 = n1 == -INFINITY ? 0.0f : expf(sacc[j][2] - n1);
+                const float p3 = n1 == -INFINITY ? 0.0f : expf(sacc[j][3] - n1);
+                l0 += p0 + p1;
+                l1 += p2 + p3;
+                // n-tile j = keys 8j..: k-step j / 2, registers (0, 1) for even j, (2, 3) for odd j
+                const int kk = j >> 1, hi2 = (j & 1) * 2;
+                pa[kk][hi2 + 0] = attn::pack_terms(p0, p1, false);
+                pa[kk][hi2 + 1] = attn::pack_terms(p2, p3, false);
+                pb[kk][hi2 + 0] = attn::pack_terms(p0, p1, true);
+                pb[kk][hi2 + 1] = attn::pack_terms(p2, p3, true);
+            }
+            // O += P V: 2 k-steps of 16 keys x 16 n-tiles of 8 dims (ldmatrix.trans: two n-tiles each)
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+#pragma unroll
+                for (int np = 0; np < 8; ++np) {
+                    const int key = 32 * kh + 16 * kk + ri + ((mi & 1) << 3);
+                    const int ch = 2 * np + (mi >> 1);
+                    const uint32_t off = (uint32_t)(key * kD * 2 + ((ch ^ (key & 7)) << 4));
+                    uint32_t h0, h1, h2, h3;
+                    attn::ldsm_x4_trans(vhi_s + off, h0, h1, h2, h3);
+                    attn::mma_bf16(o[2 * np], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], h0, h1);
+                    attn::mma_bf16(o[2 * np], pb[kk][0], pb[kk][1], pb[kk][2], pb[kk][3], h0, h1);
+                    attn::mma_bf16(o[2 * np + 1], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], h2, h3);
+                    attn::mma_bf16(o[2 * np + 1], pb[kk][0], pb[kk][1], pb[kk][2], pb[kk][3], h2, h3);
+                    if (lo) {
+                        uint32_t l0b, l1b, l2b, l3b;
+                        attn::ldsm_x4_trans(vlo_s + off, l0b, l1b, l2b, l3b);
+                        attn::mma_bf16(o[2 * np], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], l0b, l1b);
+                        attn::mma_bf16(o[2 * np + 1], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], l2b, l3b);
+                    }
+                }
             }
         }
-        // scale, causal mask, online softmax (rows g and g + 8 of the warp's 16)
-        const int qa_row = r0 + g, qb_row = r0 + g + 8;
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int key = k0 + 8 * j + 2 * t;
-            sacc[j][0] = (key <= qa_row && key < T) ? sacc[j][0] * scale : -INFINITY;
-            sacc[j][1] = (key + 1 <= qa_row && key + 1 < T) ? sacc[j][1] * scale : -INFINITY;
-            sacc[j][2] = (key <= qb_row && key < T) ? sacc[j][2] * scale : -INFINITY;
-            sacc[j][3] = (key + 1 <= qb_row && key + 1 < T) ? sacc[j][3] * scale : -INFINITY;
-            mx0 = fmaxf(mx0, fmaxf(sacc[j][0], sacc[j][1]));
-            mx1 = fmaxf(mx1, fmaxf(sacc[j][2], sacc[j][3]));
-        }
-        mx0 = fmaxf(mx0, __shfl_xor_sync(kAll, mx0, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(kAll, mx0, 2));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(kAll, mx1, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(kAll, mx1, 2));
-        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-        // a row with no visible key yet keeps max -inf; its terms stay 0
-        const float c0 = n0 == -INFINITY ? 1.0f : expf(m0 - n0);
-        const float c1 = n1 == -INFINITY ? 1.0f : expf(m1 - n1);
-        m0 = n0;
-        m1 = n1;
-        l0 *= c0;
-        l1 *= c1;
-#pragma unroll
-        for (int nt = 0; nt < 16; ++nt) {
-            o[nt][0] *= c0;
-            o[nt][1] *= c0;
-            o[nt][2] *= c1;
-            o[nt][3] *= c1;
-        }
-        uint32_t pa[4][4], pb[4][4];  // P as the A operand of 4 k-steps of 16 keys, hi and lo
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float p0 = n0 == -INFINITY ? 0.0f : expf(sacc[j][0] - n0);
-            const float p1 = n0 == -INFINITY ? 0.0f : expf(sacc[j][1] - n0);
-            const float p2 = n1 == -INFINITY ? 0.0f : expf(sacc[j][2] - n1);
-            const float p3 = n1 == -INFINITY ? 0.0f : expf(sacc[j][3] - n1);
-            l0 += p0 + p1;
-            l1 += p2 + p3;
-            // n-tile j = keys 8j..: k-step j / 2, registers (0, 1) for even j, (2, 3) for odd j
-            const int kk = j >> 1, hi2 = (j & 1) * 2;
-            pa[kk][hi2 + 0] = attn::pack_terms(p0, p1, false);
-            pa[kk][hi2 + 1] = attn::pack_terms(p2, p3, false);
-            pb[kk][hi2 + 0] = attn::pack_terms(p0, p1, true);
-            pb[kk][hi2 + 1] = attn::pack_terms(p2, p3, true);
-        }
-        // O += P V: 4 k-steps of 16 keys x 16 n-tiles of 8 dims (ldmatrix.trans: two n-tiles each)
-        const uint32_t vhi_s = smem_addr(vhi), vlo_s = smem_addr(vlo);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-            for (int np = 0; np < 8; ++np) {
-                const int key = 16 * kk + ri + ((mi & 1) << 3);
-                const int ch = 2 * np + (mi >> 1);
-                const uint32_t off = (uint32_t)(key * kD * 2 + ((ch ^ (key & 7)) << 4));
-                uint32_t h0, h1, h2, h3, l0b, l1b, l2b, l3b;
-                attn::ldsm_x4_trans(vhi_s + off, h0, h1, h2, h3);
-                attn::ldsm_x4_trans(vlo_s + off, l0b, l1b, l2b, l3b);
-                attn::mma_bf16(o[2 * np], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], h0, h1);
-                attn::mma_bf16(o[2 * np], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], l0b, l1b);
-                attn::mma_bf16(o[2 * np], pb[kk][0], pb[kk][1], pb[kk][2], pb[kk][3], h0, h1);
-                attn::mma_bf16(o[2 * np + 1], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], h2, h3);
-                attn::mma_bf16(o[2 * np + 1], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], l2b, l3b);
-                attn::mma_bf16(o[2 * np + 1], pb[kk][0], pb[kk][1], pb[kk][2], pb[kk][3], h2, h3);
-            }
-        }
+        __syncthreads();  // the stage is rewritten by the copy issued in the next iteration
     }
-    // normalise and store rows g, g + 8: out [T][n_q][d]
+
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // (only empty groups can remain)
+    // merge the two key halves of each (head, row group): half 1 hands its
+    // state (quad-summed l, m, o in fragment order) to half 0 through shared
+    // memory (the staging buffers are free now)
     l0 += __shfl_xor_sync(kAll, l0, 1);
     l0 += __shfl_xor_sync(kAll, l0, 2);
     l1 += __shfl_xor_sync(kAll, l1, 1);
     l1 += __shfl_xor_sync(kAll, l1, 2);
-    const float i0 = l0 > 0.0f ? 1.0f / l0 : 0.0f, i1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
+    float* xch = reinterpret_cast<float*>(smem_raw) + (size_t)(warp >> 1) * kWarp * 68 + lane * 68;
+    if (kh == 1) {
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt)
+            *reinterpret_cast<float4*>(xch + 4 * nt) = make_float4(o[nt][0], o[nt][1], o[nt][2], o[nt][3]);
+        *reinterpret_cast<float4*>(xch + 64) = make_float4(m0, m1, l0, l1);
+    }
+    __syncthreads();
+    if (kh == 1) return;
+    const float4 ml = *reinterpret_cast<const float4*>(xch + 64);
+    const float M0 = fmaxf(m0, ml.x), M1 = fmaxf(m1, ml.y);
+    const float ca0 = m0 == -INFINITY ? 0.0f : expf(m0 - M0), cb0 = ml.x == -INFINITY ? 0.0f : expf(ml.x - M0);
+    const float ca1 = m1 == -INFINITY ? 0.0f : expf(m1 - M1), cb1 = ml.y == -INFINITY ? 0.0f : expf(ml.y - M1);
+    const float L0 = l0 * ca0 + ml.z * cb0, L1 = l1 * ca1 + ml.w * cb1;
+    const float i0 = L0 > 0.0f ? 1.0f / L0 : 0.0f, i1 = L1 > 0.0f ? 1.0f / L1 : 0.0f;
+    // normalise and store rows g, g + 8: out [T][n_q][d]
     const int ra = r0 + g, rb = r0 + g + 8;
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) {
+        const float4 po = *reinterpret_cast<const float4*>(xch + 4 * nt);
         const int d = 8 * nt + 2 * t;
         if (ra < T)
-            *reinterpret_cast<float2*>(a.out + ((size_t)ra * a.n_q + h) * kD + d) = make_float2(o[nt][0] * i0, o[nt][1] * i0);
+            *reinterpret_cast<float2*>(a.out + ((size_t)ra * a.n_q + h) * kD + d) =
+                make_float2((o[nt][0] * ca0 + po.x * cb0) * i0, (o[nt][1] * ca0 + po.y * cb0) * i0);
         if (rb < T)
-            *reinterpret_cast<float2*>(a.out + ((size_t)rb * a.n_q + h) * kD + d) = make_float2(o[nt][2] * i1, o[nt][3] * i1);
+            *reinterpret_cast<float2*>(a.out + ((size_t)rb * a.n_q + h) * kD + d) =
+                make_float2((o[nt][2] * ca1 + po.z * cb1) * i1, (o[nt][3] * ca1 + po.w * cb1) * i1);
     }
 }
 
@@ -680,7 +722,8 @@ void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st) {
 
 void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st) {
     dim3 grid((a.T + PQ - 1) / PQ, a.n_kv);
-    launch_pdl(attn_prefill_kernel, grid, PTHREADS, kPrefillSmem, st, a);
+    const size_t smem = a.lo_terms ? kPrefillSmem : kPrefillSmem / 2;
+    launch_pdl(attn_prefill_kernel, grid, PTHREADS, smem, st, a);
 }
 
 }  // namespace zc

@@ -96,9 +96,13 @@ struct QkvArgs {
     // outputs
     float* q_out;          // decode: [T][n_q][d]; prefill: heads-major [n_q][T][d]
     int q_heads_major;
-    float* k_stage;        // prefill only (nullable): [n_kv][T][d]
+    float* k_stage;        // nullable: [n_kv][T][d] f32 (the op-level entry point)
     float* v_stage;
     int stage_round_bf16;  // staged K/V rounded to bf16 (the values the cache holds)
+    // prefill (nullable): K and V as bf16 terms for the tensor-core attention,
+    // [4][n_kv][T][d] = K hi, K lo, V hi, V lo with x = hi + lo to 2^-18
+    // relative (lo is zero when stage_round_bf16)
+    uint16_t* kv_planes;
     uint32_t* err;
 };
 void launch_qkv_post(const QkvArgs& a, cudaStream_t st);
@@ -231,11 +235,11 @@ bool flow_supported(int device);
 size_t flow_record_words(int ctas);
 cudaError_t launch_decode_flow(const PersistentArgs& a, cudaStream_t st);
 struct AttnPrefillArgs {
-    const float* q;   // [n_q][T][d]
-    const float* k;   // [n_kv][T][d]
-    const float* v;
+    const float* q;             // [n_q][T][d]
+    const uint16_t* kv_planes;  // [4][n_kv][T][d]: K hi, K lo, V hi, V lo (qkv_post)
+    int lo_terms;               // 0: K and V are exact bf16 (the lo planes are zero and skipped)
     int T, n_q, n_kv, d;
-    float* out;       // [T][n_q][d]
+    float* out;                 // [T][n_q][d]
 };
 void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st);
 

@@ -147,6 +147,17 @@ __global__ void qkv_post_kernel(QkvArgs a) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = a.stage_round_bf16 ? bf16_round(v[j]) : v[j];
     }
+    if (a.kv_planes) {
+        const size_t plane = (size_t)a.n_kv * a.T * d;
+        uint16_t* hi = a.kv_planes + (size_t)(2 * which) * plane + ((size_t)kvh * a.T + t) * d;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float x = a.stage_round_bf16 ? bf16_round(v[j]) : v[j];
+            const uint16_t h = f32_to_bf16_rne(x);
+            hi[lane + 32 * j] = h;
+            hi[plane + lane + 32 * j] = f32_to_bf16_rne(x - __uint_as_float((uint32_t)h << 16));
+        }
+    }
 }
 
 // siluMul (ops.zig:36-42): o = silu(g) * u, elementwise.

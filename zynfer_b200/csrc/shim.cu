@@ -128,7 +128,8 @@ struct ZynferCuCtx {
     size_t hist_cap = 0;  // entries
     // prefill scratch (max_prefill rows)
     float *px = nullptr, *px1 = nullptr, *pqkv = nullptr, *pq = nullptr,
-          *pk = nullptr, *pv = nullptr, *pattn = nullptr, *ph = nullptr;
+          *pattn = nullptr, *ph = nullptr;
+    uint16_t* pkvp = nullptr;  // K and V of a prefill as bf16 terms [4][n_kv][T][d]
     uint32_t* ptok = nullptr;
     // device error word and pinned host staging
     uint32_t* derr = nullptr;
@@ -700,12 +701,13 @@ void enqueue_prefill_layers(ZynferCuCtx* c, uint32_t seq, int T, uint32_t l0, ui
         qa.row_pos = nullptr; qa.pos0 = 0; qa.row_seq = nullptr; qa.seq0 = (int)seq;
         qa.kv_layer = c->kv + l * c->kv_layer_elems; qa.block_table = c->table_dev;
         qa.max_blocks = c->max_blocks; qa.n_pool_blocks = c->n_blocks;
-        qa.q_out = c->pq; qa.q_heads_major = 1; qa.k_stage = c->pk; qa.v_stage = c->pv;
+        qa.q_out = c->pq; qa.q_heads_major = 1; qa.k_stage = nullptr; qa.v_stage = nullptr;
+        qa.kv_planes = c->pkvp;
         qa.stage_round_bf16 = m.prefill_kv_f32 ? 0 : 1; qa.err = c->derr;
         launch_qkv_post(qa, c->stream);
         AttnPrefillArgs pa{};
-        pa.q = c->pq; pa.k = c->pk; pa.v = c->pv; pa.T = T; pa.n_q = m.n_q; pa.n_kv = m.n_kv;
-        pa.d = m.head_dim; pa.out = c->pattn;
+        pa.q = c->pq; pa.kv_planes = c->pkvp; pa.lo_terms = m.prefill_kv_f32 ? 1 : 0; pa.T = T; pa.n_q = m.n_q;
+        pa.n_kv = m.n_kv; pa.d = m.head_dim; pa.out = c->pattn;
         launch_attn_prefill(pa, c->stream);
         linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, &Ld.tm_o, H, c->qd, c->pattn, T, c->px1, kEpiResid, c->px,
                nullptr, nullptr);
@@ -944,8 +946,7 @@ int zynfer_cu_model_init(ZynferCuCtx* c, const ZynferCuModelDesc* desc) {
     ALLOC(c->px1, P * H);
     ALLOC(c->pqkv, P * c->qkv_rows);
     ALLOC(c->pq, P * c->qd);
-    ALLOC(c->pk, P * c->kvd);
-    ALLOC(c->pv, P * c->kvd);
+    ALLOC(c->pkvp, 4 * P * c->kvd);
     ALLOC(c->pattn, P * c->qd);
     ALLOC(c->ph, P * I);
     ALLOC(c->ptok, P);
