@@ -432,7 +432,7 @@ int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtenso
         launch_gemm_simt(a, c->stream);
         c->step_launches += 1;
     } else {
-        const int nt = tc_tile_tokens(wkind, N);
+        const int nt = tc_tile_tokens(wkind, M, N);
         TcLaunch L;
         L.tmA = tmA;
         L.args = TcArgs{M, K, N, c->tc_tpad, wkind, epi, s, c->exps, y, a.ldy, resid, keys, c->derr, 0,

@@ -91,7 +91,7 @@ extern "C" int zynfer_cu_linear_q8_static(const int8_t* w, const float* scale, c
     // that are never stored, so nothing has to start at zero.
     zc::PlanesArgs pa{x, (int)k, (int)batch, (int)k, kPadRows, zc::kWQ8, nullptr, 1e-6f, d->planes, d->xscale};
     CUtensorMap tmA, tmB;
-    const int nt = zc::tc_tile_tokens(zc::kWQ8, (int)batch);
+    const int nt = zc::tc_tile_tokens(zc::kWQ8, (int)m, (int)batch);
     if (!zc::make_tmap_k_major(&tmA, w, zc::kWQ8, k, m, 128) ||
         !zc::make_tmap_k_major(&tmB, d->planes, zc::kWQ8, k, (uint64_t)3 * kPadRows, (uint32_t)nt))
         return ZYNFER_CU_INTERNAL;

@@ -799,10 +799,14 @@ void launch_epi(const TcLaunch& L, cudaStream_t st) {
 
 }  // namespace
 
-int tc_tile_tokens(int wkind, int T) {
+int tc_tile_tokens(int wkind, int M, int T) {
     if (T <= 16) return 16;
     if (T <= 32) return 32;
-    return (wkind == kWQ8 || T <= 64) ? 64 : 128;
+    if (wkind == kWQ8 || T <= 64) return 64;
+    // bf16 with many tokens: 128-token tiles, unless they would leave more
+    // than half the SMs idle (a 1024-row projection of 512 tokens: 32 tiles);
+    // then 64-token tiles, which tc_cluster_size can also split along K
+    return 2 * (M / kBM) * ((T + 127) / 128) <= device_sm_count() ? 64 : 128;
 }
 
 void prepare_tc_kernels() {
@@ -820,7 +824,7 @@ void launch_prep_planes(const PlanesArgs& a, cudaStream_t st) {
 }
 
 void launch_tc_gemm(const TcLaunch& L, cudaStream_t st) {
-    const int nt = tc_tile_tokens(L.args.wkind, L.args.T);
+    const int nt = tc_tile_tokens(L.args.wkind, L.args.M, L.args.T);
     if (L.args.wkind == kWQ8) {
         switch (nt) {
             case 16: launch_epi<kWQ8, 16>(L, st); break;
@@ -838,7 +842,7 @@ void launch_tc_gemm(const TcLaunch& L, cudaStream_t st) {
 }
 
 int tc_cluster_size(int M, int T, int K, int wkind, int epi, int sms) {
-    const int nt = tc_tile_tokens(wkind, T);
+    const int nt = tc_tile_tokens(wkind, M, T);
     if (nt > 64 || epi == kEpiArgmax) return 1;
     const int tiles = (M / kBM) * ((T + nt - 1) / nt);
     if (2 * tiles > sms) return 1;  // enough tiles to fill the GPU without splitting K
@@ -850,7 +854,7 @@ int tc_cluster_size(int M, int T, int K, int wkind, int epi, int sms) {
 }
 
 void launch_tc_cluster(const TcLaunch& L, int S, cudaStream_t st) {
-    const int nt = tc_tile_tokens(L.args.wkind, L.args.T);
+    const int nt = tc_tile_tokens(L.args.wkind, L.args.M, L.args.T);
     if (L.args.wkind == kWQ8) {
         switch (nt) {
             case 16: launch_cluster_epi<kWQ8, 16>(L, S, st); break;

@@ -46,13 +46,14 @@ struct TcLaunch {
     int sms;  // persistent grid size
 };
 
-int tc_tile_tokens(int wkind, int T);  // NT: tokens per N tile
+int tc_tile_tokens(int wkind, int M, int T);  // NT: tokens per N tile of an M x K by T linear
 bool make_tmap_k_major(CUtensorMap* map, const void* base, int wkind, uint64_t k_elems, uint64_t rows,
                        uint32_t box_rows);
 void launch_prep_planes(const PlanesArgs& a, cudaStream_t st);
 void launch_tc_gemm(const TcLaunch& L, cudaStream_t st);
-// Cluster split-K variant for narrow problems: CTAs per cluster along K
-// (1 = use launch_tc_gemm), and its launcher (no argmax epilogue, T <= 64).
+// Cluster split-K variant for problems with too few (M, N) tiles to fill the
+// GPU: CTAs per cluster along K (1 = use launch_tc_gemm), and its launcher
+// (one tile per cluster, tiles of at most 64 tokens, no argmax epilogue).
 int tc_cluster_size(int M, int T, int K, int wkind, int epi, int sms);
 void launch_tc_cluster(const TcLaunch& L, int S, cudaStream_t st);
 // The next allocation-free linear call launches with TcArgs::stall set.
