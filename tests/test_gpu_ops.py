@@ -162,6 +162,31 @@ def test_linear_q8_few_rows_equals_tcgen05_and_oracle(gpu, m, k, batch):  # ops.
         assert O.expect_close(ref, got["mma"][b], 2e-4, 2e-4), (b, d.max_abs, d.failing_index)
 
 
+@pytest.mark.parametrize("m,k", [(4096, 1024), (6144, 1024), (1024, 2048), (1024, 3072)])
+def test_linear_q8_tile_shapes_agree(gpu, m, k):  # ops.zig:200-228
+    # 9, 16, 24 and 40 rows run 16-, 32- and 64-token tiles with different
+    # cluster splits of K; each output row depends only on its own activation
+    # row and the sums are exact, so the shared rows agree bit for bit
+    w = O.synth_normal(m * k, 51, m + k, 0.02).reshape(m, k)
+    q, s = O.pack_row_q8(w)
+    x = O.synth_normal(40 * k, 52, 40, 1.0).reshape(40, k)
+    x[3, :9] *= 60.0
+    got = {}
+    gpu.set_linear_path("tcgen05")
+    try:
+        for batch in (40, 24, 16, 9):
+            y = torch.full((batch, m), float("nan"), dtype=torch.float32, device="cuda")
+            gpu.linear(zc.W_Q8, dev(q), dev(s), dev(x[:batch]), batch, m, k, y)
+            gpu.sync()
+            got[batch] = host(y)
+    finally:
+        gpu.set_linear_path("auto")
+    for batch in (24, 16, 9):
+        assert np.array_equal(got[batch], got[40][:batch]), batch
+    for b in range(0, 40, 7):
+        assert O.expect_close(O.matvec_q8(q, s, x[b]), got[40][b], 2e-4, 2e-4), b
+
+
 @pytest.mark.parametrize("k,batch", [(1024, 17), (1024, 24), (2048, 9), (4096, 2)])
 def test_linear_q8_few_rows_falls_back_where_it_cannot_run(gpu, k, batch):
     # more than 16 rows, or more activation values than it holds in registers:

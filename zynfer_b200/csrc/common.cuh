@@ -98,6 +98,16 @@ __device__ __forceinline__ void digits4(const float (&f)[4], int e, uint32_t& d0
     d0 = __byte_perm(hi01, hi23, 0x5410);
 }
 
+// RMSNorm sum of squares in the order every kernel that digitises activation
+// rows uses, so their row scales agree bit for bit however they split K:
+// within each 128-value block, lane l of a warp takes values 4l .. 4l + 3
+// (sq4: rounded fused multiply-adds in that order) and the warp adds the 32
+// lanes with the xor butterfly of warp_sum; the blocks' sums are then added
+// one after another in k order.
+__device__ __forceinline__ float sq4(const float4 v) {
+    return __fmaf_rn(v.w, v.w, __fmaf_rn(v.z, v.z, __fmaf_rn(v.y, v.y, __fmul_rn(v.x, v.x))));
+}
+
 // Orderable key for a (logit, index) pair: a larger key is a larger logit,
 // and among equal logits the lower index (the reference's topK keeps the
 // first maximum, qwen_forward.zig:177-193). topK starts from (id 0, -inf) and

@@ -13,8 +13,8 @@
 // integer tensor-core path:
 //
 // * Each CTA stages the activation rows itself, with the arithmetic of the
-//   plane kernel of tc_gemm.cu, operation for operation (same per-thread
-//   partial sums, same warp and block reduction order): RMSNorm scale, a
+//   plane kernel of tc_gemm.cu, operation for operation (the block order of
+//   sq4 for the sum of squares, order-free maxima): RMSNorm scale, a
 //   per-row power of two 2^e >= max|x|, and the 22-bit fixed-point value
 //   split into three signed int8 digits v = d0 2^16 + d1 2^8 + d2. The
 //   digits, and so every integer sum below, equal the tcgen05 path's, and the
@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(kFrThreads, TN == 2 ? 2 : 1) fewrow_q8_kernel(
     constexpr int ROWS = WT * 8 * TN;       // weight rows per CTA
     constexpr int kMaxBlk = 8 / TN;         // 64-byte blocks per lane and tile held in registers
     extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ float red_ss[kFrWarps][NBP], red_mx[kFrWarps][NBP];
+    __shared__ float red_bs[NBP][kFrMaxK / 128], red_mx[kFrWarps][NBP];
     __shared__ float xscale_s[NBP], inv_s[NBP];
     __shared__ int e_s[NBP];
 
@@ -106,10 +106,9 @@ __global__ void __launch_bounds__(kFrThreads, TN == 2 ? 2 : 1) fewrow_q8_kernel(
     pdl_wait();
 
     // ---- activation rows -> digit planes, with the plane kernel's thread
-    // mapping (thread i holds k = 4 (i + 256 j) of every row) and operation
-    // order: per-thread partial sums, warp butterflies, the ordered sum over
-    // the eight warps. Every row's values are loaded at once and stay in
-    // registers for both passes (NBP * KV <= kFrHeld float4).
+    // mapping (thread i holds k = 4 (i + 256 j) of every row) and the
+    // sum-of-squares order of sq4. Every row's values are loaded at once and
+    // stay in registers for both passes (NBP * KV <= kFrHeld float4).
     float4 wn[KV];
     float4 xv[NBP][KV];
 #pragma unroll
@@ -124,35 +123,28 @@ __global__ void __launch_bounds__(kFrThreads, TN == 2 ? 2 : 1) fewrow_q8_kernel(
     }
 #pragma unroll
     for (int b = 0; b < NBP; ++b) {
-        float ss = 0.0f, mx = 0.0f;
+        float mx = 0.0f;
 #pragma unroll
         for (int i = 0; i < KV; ++i) {
             const float4 x4 = xv[b][i];
-            ss += x4.x * x4.x;
-            ss += x4.y * x4.y;
-            ss += x4.z * x4.z;
-            ss += x4.w * x4.w;
+            // (warp, lane) holds values 4 lane .. 4 lane + 3 of the 128-value block warp + 8 i
+            const float bs = warp_sum(sq4(x4));
+            if (lane == 0 && 4 * (threadIdx.x + i * kFrThreads) < K) red_bs[b][warp + kFrWarps * i] = bs;
             const float4 p = a.norm_w ? make_float4(__fmul_rn(wn[i].x, x4.x), __fmul_rn(wn[i].y, x4.y),
                                                     __fmul_rn(wn[i].z, x4.z), __fmul_rn(wn[i].w, x4.w))
                                       : x4;
             mx = fmaxf(mx, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
         }
-        ss = warp_sum(ss);
         mx = warp_max(mx);
-        if (lane == 0) {
-            red_ss[warp][b] = ss;
-            red_mx[warp][b] = mx;
-        }
+        if (lane == 0) red_mx[warp][b] = mx;
     }
     __syncthreads();
     if (threadIdx.x < N) {
         const int b = threadIdx.x;
         float ss = 0.0f, mx = 0.0f;
+        for (int kb = 0; kb < K / 128; ++kb) ss = __fadd_rn(ss, red_bs[b][kb]);  // blocks in k order
 #pragma unroll
-        for (int i = 0; i < kFrWarps; ++i) {
-            ss += red_ss[i][b];
-            mx = fmaxf(mx, red_mx[i][b]);
-        }
+        for (int i = 0; i < kFrWarps; ++i) mx = fmaxf(mx, red_mx[i][b]);
         float inv = 1.0f;
         if (a.norm_w) {
             inv = 1.0f / sqrtf(ss / (float)K + a.eps);

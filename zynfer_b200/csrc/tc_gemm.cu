@@ -624,7 +624,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_cluster_kernel(const __grid_
 // --------------------------------------------------- activation planes
 
 // One CTA per activation row, every value loaded once into registers
-// (K <= kPrepMaxK): one block reduction gives sum(x^2) and max|w x| (the
+// (K <= kPrepMaxK): warp reductions give sum(x^2) (in the block order of sq4)
+// and max|w x| (the
 // RMSNorm scale is a positive constant and rounding keeps the order, so
 // max |(w x) inv| = max|w x| * inv exactly), then the planes are written from
 // the registers. RMSNorm as ops.zig:49-67: (w * x) * 1/sqrt(mean(x^2) + eps).
@@ -635,13 +636,13 @@ template <int WK>
 __global__ void __launch_bounds__(kPrepThreads) prep_planes_kernel(PlanesArgs a) {
     pdl_launch_dependents();
     pdl_wait();
-    __shared__ float red_ss[kPrepThreads / kWarp], red_mx[kPrepThreads / kWarp];
+    __shared__ float red_bs[kPrepMaxK / 128], red_mx[kPrepThreads / kWarp];
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     const int t = blockIdx.x;
     const int K = a.K;  // multiple of 128, <= kPrepMaxK
     const float* xr = a.x + (size_t)t * a.ldx;
     float4 v[kPrepVec], w[kPrepVec];
-    float ss = 0.0f, mx = 0.0f;
+    float mx = 0.0f;
 #pragma unroll
     for (int i = 0; i < kPrepVec; ++i) {
         const int k = 4 * (threadIdx.x + i * kPrepThreads);
@@ -655,29 +656,22 @@ __global__ void __launch_bounds__(kPrepThreads) prep_planes_kernel(PlanesArgs a)
     }
 #pragma unroll
     for (int i = 0; i < kPrepVec; ++i) {
-        ss += v[i].x * v[i].x;
-        ss += v[i].y * v[i].y;
-        ss += v[i].z * v[i].z;
-        ss += v[i].w * v[i].w;
+        // thread (warp, lane) holds values 4 lane .. 4 lane + 3 of the 128-value block warp + 8 i
+        const float bs = warp_sum(sq4(v[i]));
+        if (lane == 0 && 4 * (threadIdx.x + i * kPrepThreads) < K) red_bs[warp + (kPrepThreads / kWarp) * i] = bs;
         const float4 p = a.norm_w ? make_float4(__fmul_rn(w[i].x, v[i].x), __fmul_rn(w[i].y, v[i].y),
                                                 __fmul_rn(w[i].z, v[i].z), __fmul_rn(w[i].w, v[i].w))
                                   : v[i];
         mx = fmaxf(mx, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
     }
-    ss = warp_sum(ss);
     mx = warp_max(mx);
-    if (lane == 0) {
-        red_ss[warp] = ss;
-        red_mx[warp] = mx;
-    }
+    if (lane == 0) red_mx[warp] = mx;
     __syncthreads();
-    ss = 0.0f;
+    float ss = 0.0f;
+    for (int kb = 0; kb < K / 128; ++kb) ss = __fadd_rn(ss, red_bs[kb]);  // blocks in k order
     mx = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kPrepThreads / kWarp; ++i) {
-        ss += red_ss[i];
-        mx = fmaxf(mx, red_mx[i]);
-    }
+    for (int i = 0; i < kPrepThreads / kWarp; ++i) mx = fmaxf(mx, red_mx[i]);
     float inv = 1.0f;
     if (a.norm_w) {
         inv = 1.0f / sqrtf(ss / (float)K + a.eps);
