@@ -495,7 +495,7 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 __global__ void __launch_bounds__(PTHREADS, 1) attn_prefill_kernel(AttnPrefillArgs a) {
-    extern __shared__ __align__(128) unsigned char smem_raw[];
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
     constexpr unsigned kAll = 0xFFFFFFFFu;
     pdl_wait();
     pdl_launch_dependents();
@@ -694,16 +694,30 @@ __global__ void __launch_bounds__(PTHREADS, 1) attn_prefill_kernel(AttnPrefillAr
     const float i0 = L0 > 0.0f ? 1.0f / L0 : 0.0f, i1 = L1 > 0.0f ? 1.0f / L1 : 0.0f;
     // normalise and store rows g, g + 8: out [T][n_q][d]
     const int ra = r0 + g, rb = r0 + g + 8;
+    const size_t K = (size_t)a.n_q * kD, out_plane = (size_t)a.t_pad * K;
+    // the plane kernel's bf16 hi / lo split of two consecutive outputs
+    auto store_planes = [&](int r, int d, float v0, float v1) {
+        const uint16_t h0 = f32_to_bf16_rne(v0), h1 = f32_to_bf16_rne(v1);
+        const uint16_t l0 = f32_to_bf16_rne(__fsub_rn(v0, __uint_as_float((uint32_t)h0 << 16)));
+        const uint16_t l1 = f32_to_bf16_rne(__fsub_rn(v1, __uint_as_float((uint32_t)h1 << 16)));
+        uint16_t* p = a.planes + (size_t)r * K + (size_t)h * kD + d;
+        *reinterpret_cast<uint32_t*>(p) = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        *reinterpret_cast<uint32_t*>(p + out_plane) = (uint32_t)l0 | ((uint32_t)l1 << 16);
+    };
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) {
         const float4 po = *reinterpret_cast<const float4*>(xch + 4 * nt);
         const int d = 8 * nt + 2 * t;
-        if (ra < T)
-            *reinterpret_cast<float2*>(a.out + ((size_t)ra * a.n_q + h) * kD + d) =
-                make_float2((o[nt][0] * ca0 + po.x * cb0) * i0, (o[nt][1] * ca0 + po.y * cb0) * i0);
-        if (rb < T)
-            *reinterpret_cast<float2*>(a.out + ((size_t)rb * a.n_q + h) * kD + d) =
-                make_float2((o[nt][2] * ca1 + po.z * cb1) * i1, (o[nt][3] * ca1 + po.w * cb1) * i1);
+        if (ra < T) {
+            const float v0 = (o[nt][0] * ca0 + po.x * cb0) * i0, v1 = (o[nt][1] * ca0 + po.y * cb0) * i0;
+            *reinterpret_cast<float2*>(a.out + ((size_t)ra * a.n_q + h) * kD + d) = make_float2(v0, v1);
+            if (a.planes) store_planes(ra, d, v0, v1);
+        }
+        if (rb < T) {
+            const float v0 = (o[nt][2] * ca1 + po.z * cb1) * i1, v1 = (o[nt][3] * ca1 + po.w * cb1) * i1;
+            *reinterpret_cast<float2*>(a.out + ((size_t)rb * a.n_q + h) * kD + d) = make_float2(v0, v1);
+            if (a.planes) store_planes(rb, d, v0, v1);
+        }
     }
 }
 

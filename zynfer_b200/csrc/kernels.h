@@ -240,6 +240,10 @@ struct AttnPrefillArgs {
     int lo_terms;               // 0: K and V are exact bf16 (the lo planes are zero and skipped)
     int T, n_q, n_kv, d;
     float* out;                 // [T][n_q][d]
+    // nullable: the output also as the bf16 hi / lo activation planes of the
+    // next linear, [2][t_pad][n_q d] (what the plane kernel would write)
+    uint16_t* planes;
+    int t_pad;
 };
 void launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st);
 

@@ -141,6 +141,11 @@ struct ZynferCuCtx {
     // tcgen05 linear scratch: activation planes and per-row exponents, plus
     // B-operand descriptors per (kind, K, NT)
     uint8_t* planes = nullptr;
+    // bf16 activation planes that the prefill attention wrote for the O
+    // projection, so that linear skips its plane kernel (a buffer of their own:
+    // `planes` may still be read by the linear before)
+    uint8_t* planes2 = nullptr;
+    bool planes_in2 = false;  // set before linear(): x's planes are in planes2
     float* exps = nullptr;  // per-row 2^(e-22) of the int8 digit planes
     int tc_tpad = 0, tc_kmax = 0;
     L2Range pf_next[2] = {};  // prefetch ranges the next linear() passes to its kernel, then clears
@@ -370,6 +375,7 @@ int ensure_tc_scratch(ZynferCuCtx* c, int t, int kmax, int mmax) {
     const int nt = std::max(tpad, c->tc_tpad), nk = std::max(kmax, c->tc_kmax);
     // superseded buffers stay in c->allocs until destroy (scratch only grows)
     if ((rc = dalloc(c, &c->planes, (size_t)4 * nt * nk))) return rc;  // 3 int8 or 2 bf16 planes
+    if ((rc = dalloc(c, &c->planes2, (size_t)4 * nt * nk))) return rc;
     if ((rc = dalloc(c, &c->exps, (size_t)nt))) return rc;
     c->tc_tpad = nt;
     c->tc_kmax = nk;
@@ -377,13 +383,15 @@ int ensure_tc_scratch(ZynferCuCtx* c, int t, int kmax, int mmax) {
     return ZYNFER_CU_OK;
 }
 
-const CUtensorMap* b_map(ZynferCuCtx* c, int wkind, int K, int nt) {
-    const uint64_t key = ((uint64_t)wkind << 48) | ((uint64_t)K << 16) | (uint64_t)nt;
+const CUtensorMap* b_map(ZynferCuCtx* c, int wkind, int K, int nt, int second = 0) {
+    const uint64_t key = ((uint64_t)second << 56) | ((uint64_t)wkind << 48) | ((uint64_t)K << 16) | (uint64_t)nt;
     auto it = c->bmaps.find(key);
     if (it != c->bmaps.end()) return &it->second;
     CUtensorMap m;
     const int P = wkind == kWQ8 ? 3 : 2;
-    if (!make_tmap_k_major(&m, c->planes, wkind, (uint64_t)K, (uint64_t)P * c->tc_tpad, (uint32_t)nt)) return nullptr;
+    if (!make_tmap_k_major(&m, second ? c->planes2 : c->planes, wkind, (uint64_t)K, (uint64_t)P * c->tc_tpad,
+                           (uint32_t)nt))
+        return nullptr;
     return &(c->bmaps[key] = m);
 }
 
@@ -401,6 +409,8 @@ int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtenso
     a.eps = c->d.eps > 0.0f ? c->d.eps : 1e-6f; a.argmax_keys = keys; a.err = c->derr;
     a.pf[0] = c->pf_next[0]; a.pf[1] = c->pf_next[1];
     c->pf_next[0] = c->pf_next[1] = L2Range{nullptr, 0};
+    const bool planes_in2 = c->planes_in2 && wkind == kWBF16;
+    c->planes_in2 = false;
     int path = c->path_policy;
     // auto: one activation row -> GEMV (no plane kernel, one launch) except the
     // vocabulary-sized LM head; 2..6 int8 rows -> the few-row kernel (one
@@ -439,14 +449,17 @@ int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtenso
                         {a.pf[0], a.pf[1]}};
         L.sms = c->caps.sm_count > 0 ? c->caps.sm_count : 148;
         const int S = tc_cluster_size(M, N, K, wkind, epi, L.sms);
-        PlanesArgs pa{x, K, N, K, c->tc_tpad, wkind, norm_w, a.eps, c->planes, c->exps};
-        launch_prep_planes(pa, c->stream);
-        L.tmB = b_map(c, wkind, K, nt);
+        if (!planes_in2) {
+            PlanesArgs pa{x, K, N, K, c->tc_tpad, wkind, norm_w, a.eps, c->planes, c->exps};
+            launch_prep_planes(pa, c->stream);
+            c->step_launches += 1;
+        }
+        L.tmB = b_map(c, wkind, K, nt, planes_in2 ? 1 : 0);
         if (L.tmB) {
             if (S > 1) launch_tc_cluster(L, S, c->stream);
             else launch_tc_gemm(L, c->stream);
         }
-        c->step_launches += 2;
+        c->step_launches += 1;
     }
     tend(c, te);
     return path;
@@ -705,10 +718,17 @@ void enqueue_prefill_layers(ZynferCuCtx* c, uint32_t seq, int T, uint32_t l0, ui
         qa.kv_planes = c->pkvp;
         qa.stage_round_bf16 = m.prefill_kv_f32 ? 0 : 1; qa.err = c->derr;
         launch_qkv_post(qa, c->stream);
+        // bf16 weights: the attention also writes the O projection's activation
+        // planes, so O needs no plane kernel (the same from the gate/up epilogue
+        // for down measured slower: its scattered 2-byte stores cost more than
+        // the launch)
+        const bool bf16 = c->wkind == kWBF16 && T <= c->tc_tpad;
         AttnPrefillArgs pa{};
         pa.q = c->pq; pa.kv_planes = c->pkvp; pa.lo_terms = m.prefill_kv_f32 ? 1 : 0; pa.T = T; pa.n_q = m.n_q;
         pa.n_kv = m.n_kv; pa.d = m.head_dim; pa.out = c->pattn;
+        pa.planes = bf16 ? reinterpret_cast<uint16_t*>(c->planes2) : nullptr; pa.t_pad = c->tc_tpad;
         launch_attn_prefill(pa, c->stream);
+        c->planes_in2 = bf16;
         linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, &Ld.tm_o, H, c->qd, c->pattn, T, c->px1, kEpiResid, c->px,
                nullptr, nullptr);
         linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, &Ld.tm_gu, 2 * I, H, c->px1, T, c->ph, kEpiSwiGLU, nullptr,
