@@ -145,55 +145,91 @@ def measured_peak_tflops():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+    """SM clocks and clock-event (throttle) reasons sampled while the timed
+    region runs: NVML polled every 2 ms from a host thread (so even a
+    30 ms region yields samples), nvidia-smi as the fallback. Read-only."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_id: str):
         self.gpu_id = gpu_id
+        self.samples: list[tuple[float, float, set]] = []
+        self.nvml = None
         self.proc = None
-        self.lines: list[str] = []
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(gpu_id)
+            self.max_sm = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.nvml = pynvml
+        except Exception:
+            self.nvml = None
+
+    def _poll_nvml(self):
+        p = self.nvml
+        bits = [(name, getattr(p, attr, 0)) for name, attr in self.REASONS]
+        while not self._stop.is_set():
+            try:
+                sm = float(p.nvmlDeviceGetClockInfo(self.handle, p.NVML_CLOCK_SM))
+                r = p.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((sm, self.max_sm, {name for name, b in bits if b and r & b}))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def _read_smi(self):
+        names = [n for n, _ in self.REASONS]
+        for ln in self.proc.stdout:
+            f = [x.strip() for x in ln.strip().split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                self.samples.append((float(f[1]), float(f[2]),
+                                     {n for n, v in zip(names, f[5:9]) if v.lower() == "active"}))
+            except ValueError:
+                continue
 
     def start(self):
+        if self.nvml:
+            self._t = threading.Thread(target=self._poll_nvml, daemon=True)
+            self._t.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t = threading.Thread(target=self._read_smi, daemon=True)
             self._t.start()
         except Exception:
             self.proc = None
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self._t.join(timeout=2)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
+        if self.nvml:
+            self._stop.set()
+            self._t.join(timeout=2)
+            source = "nvml"
+        elif self.proc:
+            self.proc.terminate()
             try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self._t.join(timeout=2)
+            source = "nvidia-smi"
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"], "samples": 0}
+        sm = [x[0] for x in self.samples]
+        reasons = set().union(*[x[2] for x in self.samples]) if self.samples else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(x[1] for x in self.samples) if self.samples else None,
+                "reasons": sorted(reasons), "samples": len(sm), "source": source}
 
 
 def oracle_model(threads: int):
@@ -390,7 +426,6 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     clocks.start()
-    time.sleep(0.2)
     torch.cuda.profiler.start()  # a profiler run with --profile-from-start off sees the timed steps only
     out, dev_ms = model.generate(slots, nxt, args.steps)
     torch.cuda.synchronize()
