@@ -266,7 +266,8 @@ ZYNFER_CU_API int zynfer_cu_linear(ZynferCuCtx *ctx, int wkind, const void *w, c
                      const float *x, uint32_t batch, uint32_t m, uint32_t k, float *y);
 /* Kernel family for linear layers: "auto" (model schedules and zynfer_cu_linear:
  * the CUDA-core GEMV for one activation row, the few-row integer-MMA kernel for
- * 2..6 int8 rows, each up to 16384 outputs; tcgen05 tensor cores otherwise),
+ * 2..6 int8 rows (2..8 when k <= 1024), each up to 16384 outputs; tcgen05
+ * tensor cores otherwise),
  * "gemv", "mma" (int8, 2..8 rows of k <= 3072 or 9..16 rows of k <= 1024; its
  * results equal the tcgen05 path's bit for bit), "tcgen05", or "simt" (the CUDA-core tiled GEMM, kept for
  * comparisons). A family that cannot take a call falls back to tcgen05.

@@ -113,12 +113,13 @@ def test_linear_q8_each_path(gpu, path, m, k, batch):  # ops.zig:181-197 on ever
 
 @pytest.mark.parametrize("m,k,batch,expect", [(4096, 1024, 1, "linear:gemv"), (1024, 3072, 1, "linear:gemv"),
                                               (4096, 1024, 2, "linear:mma"), (1024, 3072, 6, "linear:mma"),
-                                              (1024, 1024, 7, "linear:tcgen05"), (1024, 1024, 16, "linear:tcgen05"),
+                                              (1024, 1024, 7, "linear:mma"), (1024, 2048, 7, "linear:tcgen05"),
+                                              (1024, 1024, 9, "linear:tcgen05"), (1024, 1024, 16, "linear:tcgen05"),
                                               (4096, 1024, 17, "linear:tcgen05"), (16512, 1024, 1, "linear:tcgen05"),
                                               (16512, 1024, 4, "linear:tcgen05")])
 def test_linear_q8_auto_reports_the_kernel_it_ran(gpu, m, k, batch, expect):  # ops.zig:181-197
     # auto: the GEMV for one activation row, the few-row MMA kernel for 2..6
-    # rows, each for at most 16384 outputs; tcgen05 otherwise
+    # rows (2..8 when k <= 1024), each for at most 16384 outputs; tcgen05 otherwise
     w = O.synth_normal(m * k, 33, m + k, 0.02).reshape(m, k)
     q, s = O.pack_row_q8(w)
     x = O.synth_normal(batch * k, 34, batch, 1.0).reshape(batch, k)

@@ -35,8 +35,12 @@ enum LinPath { kPathAuto = 0, kPathGemv = 1, kPathSimt = 2, kPathTc = 3, kPathMm
 enum Schedule { kSchedAuto = 0, kSchedKernels = 1, kSchedPersistent = 2 };
 constexpr int kGemvMaxM = 16384;  // model auto policy: largest matrix (output rows) for the batch-1 GEMV
 // auto policy: most activation rows for the few-row MMA kernel (measured in a
-// decode step: 10 % faster than tcgen05 at 4 rows, level at 6, 13 % slower at 8)
+// decode step: 10 % faster than tcgen05 at 4 rows, level at 6, 13 % slower at 8
+// for every linear), and up to 8 rows for the K = 1024 linears alone, whose
+// rows it stages fastest (batch 8: 1.45 -> 1.42 ms; slower from 12 rows)
 constexpr int kFewRowAutoMax = 6;
+constexpr int kFewRowAutoMaxNarrow = 8;
+constexpr int kFewRowNarrowK = 1024;
 
 struct LayerDev {
     void* wqkv = nullptr;
@@ -417,7 +421,9 @@ int linear(ZynferCuCtx* c, int cls, const void* w, const float* s, const CUtenso
     // launch, no plane kernel) up to the same size; more rows -> tcgen05
     if (path == kPathAuto) {
         if (N == 1 && M <= kGemvMaxM) path = kPathGemv;
-        else if (N > 1 && N <= kFewRowAutoMax && M <= kGemvMaxM && fewrow_fits(a)) path = kPathMma;
+        else if (N > 1 && (N <= kFewRowAutoMax || (N <= kFewRowAutoMaxNarrow && K <= kFewRowNarrowK)) &&
+                 M <= kGemvMaxM && fewrow_fits(a))
+            path = kPathMma;
         else path = kPathTc;
     }
     if (path == kPathGemv && !gemv_fits(N, K)) path = kPathTc;
