@@ -231,6 +231,25 @@ def test_bf16_model_prefill_matches_f32_oracle():
     check_logits(ref_model.session(128).prefill_last_logits(ids), logits, "bf16 prefill", F32_PATH)
 
 
+@pytest.mark.parametrize("T", [1, 31, 100, 200])
+def test_bf16_prefill_ragged_lengths_match_f32_oracle(T):  # qwen_forward.zig:89-160
+    # f32 K/V (hi and lo terms), key tiles cut short by T, the attention also
+    # writing the O projection's activation planes (the GEMV takes O at T = 1)
+    gpu = zc.Gpu(0)
+    try:
+        m = zc.Model(gpu, zc.Arch(**SMALL), zc.W_BF16, max_batch=2, max_seqs=2, max_seq_len=256,
+                     max_prefill=256, prefill_kv_f32=True)
+        m.fill_synthetic(SEED, WSTD, NSTD)
+        ref_model = O.Model(O.Arch(**SMALL), O.W_BF16, kv_bf16=False, seed=SEED, w_std=WSTD, norm_std=NSTD)
+        ids = O.synth_tokens(T, SEED, 52 + T, SMALL["vocab"])
+        logits, am = m.prefill(0, ids)
+        check_logits(ref_model.session(256).prefill_last_logits(ids), logits, f"bf16 prefill T={T}", F32_PATH)
+        assert int(am) == int(np.argmax(logits))
+        ref_model.close()
+    finally:
+        gpu.close()
+
+
 def test_block_forward_matches_oracle_block():  # qwen_block.zig:161-235, one layer
     arch = dict(SMALL, layers=1)
     gpu = zc.Gpu(0)
