@@ -195,7 +195,10 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
         const uint16_t* kp = block_k(j);
         unsigned char* dst = ring + s * kSlotBytes;
         mbar_arrive_expect_tx(&full[s], kSlotBytes);
-        bulk_g2s(dst, kp, kSlotBytes, &full[s]);  // K then V of the block: one contiguous 8 KB
+        // K then V of the block: one contiguous 8 KB, read once per step, so
+        // evict-first in L2: the next linears' prefetched weights (evict-last)
+        // stay (batch 16 / 64: 3.3 / 1.6 % faster per step)
+        bulk_g2s_hint(dst, kp, kSlotBytes, &full[s], l2_evict_first_policy());  // K then V of the block: one contiguous 8 KB
     };
 
     // Fill the ring. The cache holds every earlier token (this step's row is
