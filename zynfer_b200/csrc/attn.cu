@@ -198,7 +198,7 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
         // K then V of the block: one contiguous 8 KB, read once per step, so
         // evict-first in L2: the next linears' prefetched weights (evict-last)
         // stay (batch 16 / 64: 3.3 / 1.6 % faster per step)
-        bulk_g2s_hint(dst, kp, kSlotBytes, &full[s], l2_evict_first_policy());  // K then V of the block: one contiguous 8 KB
+        bulk_g2s_hint(dst, kp, kSlotBytes, &full[s], l2_evict_first_policy());
     };
 
     // Fill the ring. The cache holds every earlier token (this step's row is
