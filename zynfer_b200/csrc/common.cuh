@@ -131,6 +131,16 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
                  : "l"(p));
     return r;
 }
+// The same, evict-first in L2 (data read once per step).
+__device__ __forceinline__ uint4 ldg_stream_first(const void* p) {
+    uint4 r;
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p), "l"(pol));
+    return r;
+}
 
 // ------------------------------------------------------ mbarrier + bulk copy
 

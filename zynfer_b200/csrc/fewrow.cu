@@ -98,7 +98,9 @@ __global__ void __launch_bounds__(kFrThreads, TN == 2 ? 2 : 1) fewrow_q8_kernel(
 #pragma unroll
             for (int tn = 0; tn < TN; ++tn) {
                 const int row = row0 + (wt * TN + tn) * 8 + g;
-                wv[blk][tn] = ldg_stream(wq + (size_t)row * K + ks * KW + blk * 64 + 16 * t);
+                // evict-first: read once per step (batch 2 / 4: 1.0 / 1.4 % per step;
+                // the batch-1 GEMV measured slower with it)
+                wv[blk][tn] = ldg_stream_first(wq + (size_t)row * K + ks * KW + blk * 64 + 16 * t);
             }
         }
     }
