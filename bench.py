@@ -115,6 +115,8 @@ def parse():
     ap.add_argument("--weights", default="q8", choices=["q8", "bf16"], help="--case: weight storage")
     ap.add_argument("--window", default="decode", choices=["decode", "prefill"],
                     help="--case: what runs between cudaProfilerStart/Stop")
+    ap.add_argument("--kv-f32", action="store_true",
+                    help="--case: prefill attention over f32 K/V (the benchmark's prefill), not the cache's bf16 values")
     ap.add_argument("--phases", action="store_true",
                     help="--case with the persistent schedule: per-phase times from CTA 0's phase trace")
     return ap.parse_args()
@@ -591,7 +593,8 @@ def run_case(args):
     total = args.warmup + 2 * args.steps + 2
     gpu = zc.Gpu(0)
     wk = zc.W_Q8 if args.weights == "q8" else zc.W_BF16
-    model = zc.Model(gpu, arch, wk, max_batch=B, max_seqs=B, max_seq_len=ctx + total + 16, max_prefill=ctx)
+    model = zc.Model(gpu, arch, wk, max_batch=B, max_seqs=B, max_seq_len=ctx + total + 16, max_prefill=ctx,
+                     prefill_kv_f32=args.kv_f32)
     model.fill_synthetic(1, 0.02, 0.0)
     gpu.set_linear_path(args.path)
     gpu.set_decode_schedule(args.schedule)
