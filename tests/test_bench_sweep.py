@@ -59,3 +59,33 @@ def test_case_arguments(monkeypatch):
     a = bench.parse()
     assert a.case == "32,2048,2" and a.steps == 2 and a.schedule == "persistent" and a.phases
     assert tuple(int(v) for v in a.case.split(",")) == (32, 2048, 2)
+
+
+def test_clock_sampler_reports_missing_sources():
+    # without NVML and without nvidia-smi the line says so instead of inventing clocks
+    s = bench.ClockSampler("GPU-00000000-0000-0000-0000-000000000000")
+    s.nvml = None
+    import subprocess
+    orig = subprocess.Popen
+
+    def no_smi(*a, **k):
+        raise FileNotFoundError("nvidia-smi")
+    subprocess.Popen = no_smi
+    try:
+        s.start()
+        out = s.stop()
+    finally:
+        subprocess.Popen = orig
+    assert out["samples"] == 0 and out["sm_mhz"] is None and out["reasons"] == ["no clock source"]
+
+
+def test_clock_sampler_summarises_samples():
+    s = bench.ClockSampler("GPU-00000000-0000-0000-0000-000000000000")
+    s.nvml = None
+    s.proc = None
+    s.samples = [(1965.0, 1965.0, set()), (1800.0, 1965.0, {"sw_power_cap"}), (1965.0, 1965.0, set())]
+    s.nvml = object()  # take the NVML branch of stop(): no thread to join
+    s._t = type("T", (), {"join": lambda self, timeout=None: None})()
+    out = s.stop()
+    assert out["sm_mhz"] == 1965.0 and out["sm_max_mhz"] == 1965.0
+    assert out["reasons"] == ["sw_power_cap"] and out["samples"] == 3
