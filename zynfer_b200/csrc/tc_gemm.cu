@@ -442,6 +442,11 @@ __device__ __forceinline__ void cluster_reduce_items(const TcArgs& a, long long*
     const int items = pairs * NT;
     for (int base = e; base < items; base += 256 * U) {
         long long x0[U][SMAX], x1[U][SMAX];
+        // every load of the U items (remote partials, row scales, activation
+        // scales, residuals) is issued before any store: the output may alias
+        // the residual, so a load after a store could not be moved ahead of it
+        float xs_u[U], sc_u[U][2];
+        float2 rs_u[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int idx = min(base + 256 * u, items - 1);
@@ -450,6 +455,14 @@ __device__ __forceinline__ void cluster_reduce_items(const TcArgs& a, long long*
 #pragma unroll
             for (int s2 = 0; s2 < SMAX; ++s2)
                 if (s2 < S) ld_cluster_s64x2(rb[s2] + off, x0[u][s2], x1[u][s2]);
+            const int tt = min(n0 + t, a.T - 1);
+            if constexpr (WK == kWQ8) {
+                xs_u[u] = xsc ? xsc[t] : __ldg(a.xscale + tt);
+                sc_u[u][0] = __ldg(a.scale + m0 + row);
+                sc_u[u][1] = __ldg(a.scale + m0 + row + 1);
+            }
+            if constexpr (EPI == kEpiResid)
+                rs_u[u] = *reinterpret_cast<const float2*>(a.resid + (size_t)tt * a.ldy + m0 + row);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -472,9 +485,8 @@ __device__ __forceinline__ void cluster_reduce_items(const TcArgs& a, long long*
             }
             float y[2];
             if constexpr (WK == kWQ8) {
-                const float xs = xsc ? xsc[t] : __ldg(a.xscale + n0 + t);
 #pragma unroll
-                for (int v = 0; v < 2; ++v) y[v] = __fmul_rn(__fmul_rn(__ll2float_rn(vi[v]), xs), __ldg(a.scale + m0 + row + v));
+                for (int v = 0; v < 2; ++v) y[v] = __fmul_rn(__fmul_rn(__ll2float_rn(vi[v]), xs_u[u]), sc_u[u][v]);
             } else {
 #pragma unroll
                 for (int v = 0; v < 2; ++v) y[v] = (float)vd[v];
@@ -483,8 +495,8 @@ __device__ __forceinline__ void cluster_reduce_items(const TcArgs& a, long long*
             if constexpr (EPI == kEpiSwiGLU) {
                 a.y[o + ((m0 + row) >> 1)] = __fmul_rn(silu(y[0]), y[1]);
             } else if constexpr (EPI == kEpiResid) {
-                const float2 rs = *reinterpret_cast<const float2*>(a.resid + o + m0 + row);
-                *reinterpret_cast<float2*>(a.y + o + m0 + row) = make_float2(__fadd_rn(rs.x, y[0]), __fadd_rn(rs.y, y[1]));
+                *reinterpret_cast<float2*>(a.y + o + m0 + row) =
+                    make_float2(__fadd_rn(rs_u[u].x, y[0]), __fadd_rn(rs_u[u].y, y[1]));
             } else {
                 *reinterpret_cast<float2*>(a.y + o + m0 + row) = make_float2(y[0], y[1]);
             }
