@@ -42,7 +42,7 @@ __device__ __forceinline__ int swz(int k) {
 
 
 template <int WK, int NB, int R, int EPI>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
+__global__ void __launch_bounds__(kThreads, NB == 1 ? 4 : 1) gemv_kernel(LinearArgs a) {
     static_assert(EPI != kEpiSwiGLU || R % 2 == 0, "SwiGLU needs (gate, up) row pairs in one unit");
     extern __shared__ float xs[];  // [NB][K] swizzled
     __shared__ float red[kWarps];
@@ -90,43 +90,48 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
     }
     pdl_wait();
 
-    // ---- stage activations (RMSNorm prologue when norm_w is set): every
-    // row at once, kWpr warps per row, so the staging latency does not grow
-    // with the number of rows (NB <= kWarps)
+    // ---- stage activations: every row at once, kWpr warps per row, so the
+    // staging latency does not grow with the number of rows (NB <= kWarps).
+    // RMSNorm (ops.zig:49-67) is a per-row positive scale, so it is factored
+    // out of the dot product: the staged row is w * x, the sum of squares is
+    // reduced in the same pass, and inv multiplies each output at the end
+    // (one barrier instead of two)
+    constexpr int kWpr = kWarps / NB;
     {
-        constexpr int kWpr = kWarps / NB;
         const int b = warp / kWpr, part = warp % kWpr;
         const int t0 = part * kWarp + lane;
         constexpr int nthr = kWpr * kWarp;
         const bool live = b < NB && b < a.N;
         const float* xr = a.x + (size_t)(live ? b : 0) * a.ldx;
-        if (a.norm_w) {
-            float acc = 0.0f;
-            if (live)
-                for (int k = t0; k < K; k += nthr) acc += xr[k] * xr[k];
-            acc = warp_sum(acc);
-            if (lane == 0) red[warp] = acc;
-            __syncthreads();
-        }
+        float ss = 0.0f;
         if (b < NB) {
             if (live) {
-                float inv = 1.0f;
-                if (a.norm_w) {
-                    float tot = 0.0f;
-#pragma unroll
-                    for (int w = 0; w < kWpr; ++w) tot += red[b * kWpr + w];
-                    inv = 1.0f / sqrtf(tot / (float)K + a.eps);
-                }
                 for (int k = t0; k < K; k += nthr) {
                     const float v = xr[k];
-                    xs[b * K + swz<WK>(k)] = a.norm_w ? __fmul_rn(__fmul_rn(a.norm_w[k], v), inv) : v;
+                    ss += v * v;
+                    xs[b * K + swz<WK>(k)] = a.norm_w ? __fmul_rn(a.norm_w[k], v) : v;
                 }
             } else {
                 for (int k = t0; k < K; k += nthr) xs[b * K + k] = 0.0f;
             }
         }
+        if (a.norm_w) {
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+        }
     }
     __syncthreads();
+    float inv_b[NB];  // RMSNorm scale of each row (1 without a norm)
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        inv_b[b] = 1.0f;
+        if (a.norm_w) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWpr; ++w) tot += red[b * kWpr + w];
+            inv_b[b] = 1.0f / sqrtf(tot / (float)K + a.eps);
+        }
+    }
 
     // the next kernel may launch once the activations are staged: its weight
     // loads then do not compete with this kernel's (batch 1: 0.837 -> 0.808 ms/token)
@@ -138,9 +143,13 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
     // acc[r][b] += W[r0 + r][k0 .. k0 + kElems) . x[b][same]: four k at a
     // time, converted once for every row, each activation float4 read once
     // from shared memory for all R weight rows
-    auto dot_chunk = [&](const uint4 (&wr)[R], int k0, float (&acc)[R][NB]) {
+    // One activation row: two accumulators per weight row (even and odd
+    // groups of four k), which halves the dependent FMA chain of a lane.
+    constexpr int kAcc = NB == 1 ? 2 : 1;
+    auto dot_chunk = [&](const uint4 (&wr)[R], int k0, float (&acc2)[kAcc][R][NB]) {
 #pragma unroll
         for (int q = 0; q < kElems / 4; ++q) {
+            float (&acc)[R][NB] = acc2[q % kAcc];
             float w[R][4];
 #pragma unroll
             for (int r = 0; r < R; ++r) {
@@ -169,17 +178,19 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
 
     for (int g = g_first; g < groups; g += gridDim.x * kWarps) {
         const int r0 = g * R;
-        float acc[R][NB];
+        float accs[kAcc][R][NB];
 #pragma unroll
-        for (int r = 0; r < R; ++r)
+        for (int i = 0; i < kAcc; ++i)
 #pragma unroll
-            for (int b = 0; b < NB; ++b) acc[r][b] = 0.0f;
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int b = 0; b < NB; ++b) accs[i][r][b] = 0.0f;
 
         if (held) {
             if (g != g_first) load_group(g);
 #pragma unroll
             for (int it = 0; it < kMaxIt; ++it)
-                if (it < iters) dot_chunk(wv[it], it * kElems * kWarp + lane * kElems, acc);
+                if (it < iters) dot_chunk(wv[it], it * kElems * kWarp + lane * kElems, accs);
         } else {
             // two chunks in flight: the next chunk's loads are issued before
             // this one's products
@@ -195,15 +206,21 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
             load_chunk(0, cur);
             for (int it = 0; it < iters; ++it) {
                 if (it + 1 < iters) load_chunk(it + 1, nxt);
-                dot_chunk(cur, it * kElems * kWarp + lane * kElems, acc);
+                dot_chunk(cur, it * kElems * kWarp + lane * kElems, accs);
 #pragma unroll
                 for (int r = 0; r < R; ++r) cur[r] = nxt[r];
             }
         }
+        float acc[R][NB];
 #pragma unroll
         for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int b = 0; b < NB; ++b) acc[r][b] = warp_sum(acc[r][b]);
+            for (int b = 0; b < NB; ++b) {
+                float v = accs[0][r][b];
+#pragma unroll
+                for (int i = 1; i < kAcc; ++i) v += accs[i][r][b];
+                acc[r][b] = warp_sum(v);
+            }
 
         // every lane holds the sums; lane b (< NB) writes batch row b
 #pragma unroll
@@ -214,10 +231,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(LinearArgs a) {
                 const int row = r0 + r;
                 if (row >= a.M) break;
                 const float s = a.scale ? a.scale[row] : 1.0f;
-                const float val = __fmul_rn(acc[r][b], s);
+                const float val = __fmul_rn(__fmul_rn(acc[r][b], inv_b[b]), s);
                 if constexpr (EPI == kEpiSwiGLU) {
                     if ((r & 1) == 1 && lane == b) {
-                        const float gate = __fmul_rn(acc[r - 1][b], a.scale ? a.scale[row - 1] : 1.0f);
+                        const float gate = __fmul_rn(__fmul_rn(acc[r - 1][b], inv_b[b]), a.scale ? a.scale[row - 1] : 1.0f);
                         a.y[(size_t)b * a.ldy + (row >> 1)] = __fmul_rn(silu(gate), val);
                     }
                 } else if constexpr (EPI == kEpiResid) {
