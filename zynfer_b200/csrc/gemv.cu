@@ -105,14 +105,25 @@ __global__ void __launch_bounds__(kThreads, NB == 1 ? 4 : 1) gemv_kernel(LinearA
         const float* xr = a.x + (size_t)(live ? b : 0) * a.ldx;
         float ss = 0.0f;
         if (b < NB) {
+            // four consecutive k stay together under swz, so whole float4s move
+            // (x rows are 16-byte aligned: ldx and K are multiples of 4)
             if (live) {
-                for (int k = t0; k < K; k += nthr) {
-                    const float v = xr[k];
-                    ss += v * v;
-                    xs[b * K + swz<WK>(k)] = a.norm_w ? __fmul_rn(a.norm_w[k], v) : v;
+                for (int k = 4 * t0; k < K; k += 4 * nthr) {
+                    const float4 v = *reinterpret_cast<const float4*>(xr + k);
+                    ss += v.x * v.x;
+                    ss += v.y * v.y;
+                    ss += v.z * v.z;
+                    ss += v.w * v.w;
+                    float4 o = v;
+                    if (a.norm_w) {
+                        const float4 w = __ldg(reinterpret_cast<const float4*>(a.norm_w + k));
+                        o = make_float4(__fmul_rn(w.x, v.x), __fmul_rn(w.y, v.y), __fmul_rn(w.z, v.z), __fmul_rn(w.w, v.w));
+                    }
+                    *reinterpret_cast<float4*>(xs + b * K + swz<WK>(k)) = o;
                 }
             } else {
-                for (int k = t0; k < K; k += nthr) xs[b * K + k] = 0.0f;
+                for (int k = 4 * t0; k < K; k += 4 * nthr)
+                    *reinterpret_cast<float4*>(xs + b * K + k) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
         if (a.norm_w) {
