@@ -88,7 +88,26 @@ __global__ void __launch_bounds__(kThreads, NB == 1 ? 4 : 1) gemv_kernel(LinearA
         for (int r = 0; r < R && r0 + r < a.M; ++r)
             for (int off = lane * 128; off < row_bytes; off += kWarp * 128) prefetch_l2(wbase + (size_t)(r0 + r) * row_bytes + off);
     }
+    // the first row group's scales (weights: before the wait) and residuals
+    // (after it, issued with the staging loads) are in registers before the
+    // products finish, so the epilogue waits for no load
+    float sc_first[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int row = min(g_first * R + r, a.M - 1);
+        sc_first[r] = (a.scale && g_first < groups) ? __ldg(a.scale + row) : 1.0f;
+    }
     pdl_wait();
+    float rs_first[R][NB];
+    if constexpr (EPI == kEpiResid) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int row = min(g_first * R + r, a.M - 1);
+                rs_first[r][b] = (g_first < groups && b < a.N && lane == b) ? a.resid[(size_t)b * a.ldy + row] : 0.0f;
+            }
+    }
 
     // ---- stage activations: every row at once, kWpr warps per row, so the
     // staging latency does not grow with the number of rows (NB <= kWarps).
@@ -241,15 +260,20 @@ __global__ void __launch_bounds__(kThreads, NB == 1 ? 4 : 1) gemv_kernel(LinearA
             for (int r = 0; r < R; ++r) {
                 const int row = r0 + r;
                 if (row >= a.M) break;
-                const float s = a.scale ? a.scale[row] : 1.0f;
+                const bool first = g == g_first;
+                const float s = first ? sc_first[r] : (a.scale ? a.scale[row] : 1.0f);
                 const float val = __fmul_rn(__fmul_rn(acc[r][b], inv_b[b]), s);
                 if constexpr (EPI == kEpiSwiGLU) {
                     if ((r & 1) == 1 && lane == b) {
-                        const float gate = __fmul_rn(__fmul_rn(acc[r - 1][b], inv_b[b]), a.scale ? a.scale[row - 1] : 1.0f);
+                        const float sg = first ? sc_first[r - 1] : (a.scale ? a.scale[row - 1] : 1.0f);
+                        const float gate = __fmul_rn(__fmul_rn(acc[r - 1][b], inv_b[b]), sg);
                         a.y[(size_t)b * a.ldy + (row >> 1)] = __fmul_rn(silu(gate), val);
                     }
                 } else if constexpr (EPI == kEpiResid) {
-                    if (lane == b) a.y[(size_t)b * a.ldy + row] = __fadd_rn(a.resid[(size_t)b * a.ldy + row], val);
+                    if (lane == b) {
+                        const float rs = first ? rs_first[r][b] : a.resid[(size_t)b * a.ldy + row];
+                        a.y[(size_t)b * a.ldy + row] = __fadd_rn(rs, val);
+                    }
                 } else if constexpr (EPI == kEpiArgmax) {
                     if (lane == b && a.y) a.y[(size_t)b * a.ldy + row] = val;
                     const unsigned long long key = argmax_key(val, (uint32_t)row);
