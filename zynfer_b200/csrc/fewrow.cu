@@ -105,7 +105,24 @@ __global__ void __launch_bounds__(kFrThreads, TN == 2 ? 2 : 1) fewrow_q8_kernel(
         }
     }
     prefetch_l2_ranges(a.pf);
+    // this thread's first epilogue item: its row scales now (weights), its
+    // residual right after the wait, so the epilogue waits for no load
+    constexpr int OUTS = EPI == kEpiSwiGLU ? ROWS / 2 : ROWS;
+    const bool item0 = threadIdx.x < N * OUTS;
+    const int b_0 = threadIdx.x / OUTS, o_0 = threadIdx.x % OUTS;
+    float sc0[2] = {1.0f, 1.0f};
+    if (item0) {
+        if constexpr (EPI == kEpiSwiGLU) {
+            sc0[0] = __ldg(a.scale + row0 + 2 * o_0);
+            sc0[1] = __ldg(a.scale + row0 + 2 * o_0 + 1);
+        } else {
+            sc0[0] = __ldg(a.scale + row0 + o_0);
+        }
+    }
     pdl_wait();
+    float rs0 = 0.0f;
+    if constexpr (EPI == kEpiResid)
+        if (item0) rs0 = a.resid[(size_t)b_0 * a.ldy + row0 + o_0];
 
     // ---- activation rows -> digit planes, with the plane kernel's thread
     // mapping (thread i holds k = 4 (i + 256 j) of every row) and the
@@ -234,23 +251,24 @@ __global__ void __launch_bounds__(kFrThreads, TN == 2 ? 2 : 1) fewrow_q8_kernel(
     __syncthreads();
 
     // ---- epilogue: one thread per (activation row, weight row or SwiGLU pair)
-    constexpr int OUTS = EPI == kEpiSwiGLU ? ROWS / 2 : ROWS;
     for (int idx = threadIdx.x; idx < N * OUTS; idx += kFrThreads) {
         const int b = idx / OUTS, o = idx % OUTS;
-        auto value = [&](int r) -> float {
+        const bool first = idx == threadIdx.x;
+        auto value = [&](int r, float sc) -> float {
             long long v = 0;
 #pragma unroll
             for (int s = 0; s < KS; ++s) v += red[((size_t)s * ROWS + r) * NBP + b];
-            return __fmul_rn(__fmul_rn(__ll2float_rn(v), xscale_s[b]), a.scale[row0 + r]);
+            return __fmul_rn(__fmul_rn(__ll2float_rn(v), xscale_s[b]), sc);
         };
         if constexpr (EPI == kEpiSwiGLU) {
-            const float gate = value(2 * o), up = value(2 * o + 1);
+            const float gate = value(2 * o, first ? sc0[0] : a.scale[row0 + 2 * o]);
+            const float up = value(2 * o + 1, first ? sc0[1] : a.scale[row0 + 2 * o + 1]);
             a.y[(size_t)b * a.ldy + (row0 >> 1) + o] = __fmul_rn(silu(gate), up);
         } else if constexpr (EPI == kEpiResid) {
             const size_t at = (size_t)b * a.ldy + row0 + o;
-            a.y[at] = __fadd_rn(a.resid[at], value(o));
+            a.y[at] = __fadd_rn(first ? rs0 : a.resid[at], value(o, first ? sc0[0] : a.scale[row0 + o]));
         } else {
-            a.y[(size_t)b * a.ldy + row0 + o] = value(o);
+            a.y[(size_t)b * a.ldy + row0 + o] = value(o, first ? sc0[0] : a.scale[row0 + o]);
         }
     }
 }
