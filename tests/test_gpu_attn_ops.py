@@ -60,15 +60,13 @@ def test_kv_fill_matches_oracle_fill(one_layer):
         s.close()
 
 
-@pytest.mark.parametrize("batch", [1, 8, 64])
-def test_attn_decode_matches_attention_into(one_layer, batch):
+def _check_attn_decode(one_layer, lens, qkv_seed):
     m, qn, kn, oracle = one_layer
-    kv_lens = [1, 257, 2304, 4224]
-    lens = [kv_lens[(i + batch) % 4] for i in range(batch)]
+    batch = len(lens)
     seqs = list(range(batch))
     for i, L in enumerate(lens):
         m.kv_fill_synthetic(i, L - 1, 7000 + L + i)
-    qkv = O.synth_normal(batch * 4096, 11, batch, 1.0).reshape(batch, 4096)
+    qkv = O.synth_normal(batch * 4096, 11, qkv_seed, 1.0).reshape(batch, 4096)
     out = torch.empty((batch, 16, 128), dtype=torch.float32, device="cuda")
     m.attn_decode(0, seqs, dev(qkv), out)
     got = out.cpu().numpy()
@@ -88,6 +86,22 @@ def test_attn_decode_matches_attention_into(one_layer, batch):
         assert O.expect_close(ref, got[i], 1e-4, 1e-4), (i, L, d.max_abs, d.failing_index)
         if L == 1:  # one position: the output is the appended V row itself, both heads of each group
             assert np.array_equal(got[i], np.repeat(O.bf16_round(v_new), 2, axis=0)), i
+
+
+@pytest.mark.parametrize("batch", [1, 8, 64])
+def test_attn_decode_matches_attention_into(one_layer, batch):
+    kv_lens = [1, 257, 2304, 4224]
+    _check_attn_decode(one_layer, [kv_lens[(i + batch) % 4] for i in range(batch)], batch)
+
+
+# One sequence runs as one cluster of 8 CTAs (64 warps) per kv head, the CTAs'
+# records merged in the first CTA's shared memory. Lengths: one warp holds the
+# whole row (1, 2, 16 positions), one CTA holds it (17, 128), all 64 warps one
+# block each (1024), shares of 2 and 3 blocks (1025, 2049, 3072) and the
+# cache's last position (4232: shares of 5 blocks, 7 CTAs with records).
+@pytest.mark.parametrize("kv_len", [1, 2, 16, 17, 128, 1024, 1025, 2049, 3072, MAX_SEQ_LEN])
+def test_attn_decode_one_sequence(one_layer, kv_len):
+    _check_attn_decode(one_layer, [kv_len], 100 + kv_len)
 
 
 @pytest.mark.parametrize("pos0", [0, 4219])

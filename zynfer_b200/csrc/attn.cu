@@ -61,6 +61,7 @@ constexpr int kMaxBatch = 1024;
 constexpr int kIdRing = 64;                                 // per-warp ring of block addresses (2 chunks of 32)
 constexpr size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
 constexpr size_t kWarpScratch = kG * kD * 4 + 2 * kD * 2;    // per warp: q (2 x 128 f32), new K/V row
+constexpr int kHeadCtas = 8;                                // CTAs of a kv head's cluster (one-sequence steps)
 // Shared-memory layout for RING slots per warp. Three slots keep a block
 // loading while a warp computes on a pair (the rate at many rows); one row's
 // step gives every warp at most one pair (2 blocks), so two slots hold its
@@ -74,6 +75,10 @@ struct DecLayout {
     static constexpr size_t rec_off = scratch_off + kDecWarps * kWarpScratch;  // [2][kDecWarps] share records
     static constexpr size_t gid_off = rec_off + (size_t)2 * kDecWarps * attn::kPartStride * 4;  // [2][kDecWarps] int
     static constexpr size_t smem = gid_off + 2 * kDecWarps * sizeof(int);
+    // one-sequence head clusters: the first CTA of a cluster receives every
+    // CTA's record here (distributed shared memory)
+    static constexpr size_t cl_off = align16(smem);
+    static constexpr size_t smem_head = cl_off + (size_t)kHeadCtas * attn::kPartStride * 4;
     static_assert(smem <= 232448, "decode attention shared memory");
     static_assert(scratch_off % 16 == 0 && kWarpScratch % 16 == 0 && rec_off % 16 == 0 &&
                       (attn::kPartStride * 4) % 16 == 0,
@@ -84,7 +89,35 @@ struct BlockCursor {
     int b, head, blk, nblk;
 };
 
-template <int kRing>
+// DSMEM address of `p` (this CTA's shared memory) in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_rank(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_f32x4(uint32_t addr, const float4& v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// kHead: a one-sequence step launched as one cluster of kHeadCtas CTAs per
+// kv head. The cluster's 64 warps split that head's blocks into equal
+// contiguous shares, the CTAs' records meet in the first CTA's shared memory
+// and it merges them after one cluster barrier: no global records, no
+// counter, no second pass through L2.
+template <int kRing, bool kHead = false>
 __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
     using Lay = DecLayout<kRing>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -132,17 +165,28 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
     __syncthreads();
 
     const int total = pref[B] * a.n_kv;
-    const int nwarps = gridDim.x * kDecWarps;
-    const int per = max((total + nwarps - 1) / nwarps, kMinBlocksPerWarp);
     // CTA-major shares: the warps of a CTA hold consecutive shares, so the
     // pieces of a (row, kv head) mostly meet in one CTA and merge in shared
-    // memory; only CTA-level records go through global memory.
-    const int w = blockIdx.x * kDecWarps + warp;
-    const int c_lo = blockIdx.x * kDecWarps * per;
-    if (c_lo >= total) return;  // the whole CTA is idle
-    const int c_hi = min(total, c_lo + kDecWarps * per);
-    const int lo = w * per;
-    const int n = max(0, min(total, lo + per) - lo);
+    // memory; only CTA-level records leave the CTA.
+    int per, c_lo, c_hi;
+    if constexpr (kHead) {
+        // every CTA takes part in the cluster barriers, idle or not; the first
+        // arrive tells the others this CTA runs before they write into it
+        cluster_arrive_relaxed();
+        const int head = blockIdx.x / kHeadCtas, rank = blockIdx.x % kHeadCtas;
+        const int nblk = pref[1];
+        per = max((nblk + kHeadCtas * kDecWarps - 1) / (kHeadCtas * kDecWarps), 1);
+        c_lo = head * nblk + min(rank * kDecWarps * per, nblk);
+        c_hi = min(head * nblk + nblk, c_lo + kDecWarps * per);
+    } else {
+        const int nwarps = gridDim.x * kDecWarps;
+        per = max((total + nwarps - 1) / nwarps, kMinBlocksPerWarp);
+        c_lo = blockIdx.x * kDecWarps * per;
+        if (c_lo >= total) return;  // the whole CTA is idle
+        c_hi = min(total, c_lo + kDecWarps * per);
+    }
+    const int lo = c_lo + warp * per;
+    const int n = max(0, min(c_hi, lo + per) - lo);
     if (lane < 2) rec_gid[lane][warp] = -1;
 
     auto locate = [&](int f, BlockCursor& c) {
@@ -402,8 +446,10 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
     // ---- CTA merge: every (row, kv head) that meets this CTA's range in more
     // than one warp, or leaves it, is merged from the warps' records (warp
     // order); a row that ends in this CTA is stored, otherwise the CTA's
-    // record goes to global memory and the last CTA to arrive merges them.
+    // record goes to global memory and the last CTA to arrive merges them
+    // (head clusters: to the cluster's first CTA, which merges them).
     __syncthreads();
+    bool head_wait_done = false;  // this warp already waited on the first cluster barrier
     {
         BlockCursor gc;
         locate(c_lo, gc);
@@ -440,6 +486,20 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
                     }
                     if (g0 >= c_lo && g1 <= c_hi) {
                         attn::merged_store_out(L, A0, A1, a.out, gb, gh, a.n_q);
+                    } else if constexpr (kHead) {
+                        // this CTA's record into slot `rank` of the cluster's first CTA
+                        cluster_wait_acquire();  // (the first barrier: every CTA runs)
+                        const uint32_t rec = map_rank(smem_raw + Lay::cl_off, 0) +
+                                             (uint32_t)((blockIdx.x % kHeadCtas) * attn::kPartStride * 4);
+                        if (lane == 0) {
+                            st_cluster_f32(rec, M[0]);
+                            st_cluster_f32(rec + 4, L[0]);
+                            st_cluster_f32(rec + attn::kPartHead * 4, M[1]);
+                            st_cluster_f32(rec + attn::kPartHead * 4 + 4, L[1]);
+                        }
+                        st_cluster_f32x4(rec + (4 + 4 * lane) * 4, A0);
+                        st_cluster_f32x4(rec + (attn::kPartHead + 4 + 4 * lane) * 4, A1);
+                        head_wait_done = true;
                     } else {
                         const int span = kDecWarps * per;
                         const int fc = g0 / span, nseg = (g1 - 1) / span - fc + 1, seg = (int)blockIdx.x - fc;
@@ -461,6 +521,20 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
             gc.nblk = gc.b < B ? pref[gc.b + 1] - pref[gc.b] : 1;
         }
     }
+    if constexpr (kHead) {
+        if (!head_wait_done) cluster_wait_acquire();
+        cluster_arrive_release();  // this CTA's record is in the first CTA
+        cluster_wait_acquire();
+        const int nblk = pref[1], span = kDecWarps * per;
+        const int nseg = (nblk + span - 1) / span;  // CTAs with blocks; their records, in rank order
+        if (blockIdx.x % kHeadCtas == 0 && nseg > 1 && warp == 0) {
+            float M[kG], L[kG];
+            float4 A0, A1;
+            attn::merge_records<false, kHeadCtas>(reinterpret_cast<const float*>(smem_raw + Lay::cl_off), nseg, M, L,
+                                                  A0, A1);
+            attn::merged_store_out(L, A0, A1, a.out, 0, blockIdx.x / kHeadCtas, a.n_q);
+        }
+    }
 }
 
 // The decode kernels: three ring slots for many rows (the register file is
@@ -469,6 +543,7 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
 // of shared memory) fits on the same SM beside it.
 __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeArgs a) { attn_decode_body<3>(a); }
 __global__ void __maxnreg__(192) attn_decode_row_kernel(AttnDecodeArgs a) { attn_decode_body<2>(a); }
+__global__ void __maxnreg__(192) attn_decode_head_kernel(AttnDecodeArgs a) { attn_decode_body<2, true>(a); }
 
 // ------------------------------------------------------------ prefill
 //
@@ -729,10 +804,29 @@ __global__ void __launch_bounds__(PTHREADS, 1) attn_prefill_kernel(AttnPrefillAr
 void prepare_attn_kernels() {
     configure_kernel((const void*)attn_decode_kernel, DecLayout<3>::smem);
     configure_kernel((const void*)attn_decode_row_kernel, DecLayout<2>::smem);
+    configure_kernel((const void*)attn_decode_head_kernel, DecLayout<2>::smem_head);
     configure_kernel((const void*)attn_prefill_kernel, kPrefillSmem);
 }
 
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st) {
+    if (a.B == 1) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(a.n_kv * kHeadCtas);
+        cfg.blockDim = dim3(kDecThreads);
+        cfg.dynamicSmemBytes = DecLayout<2>::smem_head;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = kHeadCtas;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        cudaLaunchKernelEx(&cfg, attn_decode_head_kernel, a);
+        return;
+    }
     if (a.B == 1) launch_pdl(attn_decode_row_kernel, device_sm_count(), kDecThreads, DecLayout<2>::smem, st, a);
     else launch_pdl(attn_decode_kernel, device_sm_count(), kDecThreads, DecLayout<3>::smem, st, a);
 }

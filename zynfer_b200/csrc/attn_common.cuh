@@ -241,7 +241,9 @@ __device__ __forceinline__ void share_store_record(const float (&acc)[16][4], fl
 // log-sum-exp sense: m = max m_j, l = sum l_j e^(m_j - m), acc = sum acc_j
 // e^(m_j - m). Lane owns dims 4 lane .. 4 lane + 3 of both heads (A0, A1);
 // M and L of both heads are returned in every lane. kGlobal: records written
-// by other CTAs (read through L2), else shared memory.
+// by other CTAs (read through L2), else shared memory. The (m, l) of the
+// first 32 records and the accumulators of the first kBatch are all requested
+// before any of them is used, so up to kBatch records cost one round trip.
 template <bool kGlobal, int kBatch>
 __device__ __forceinline__ void merge_records(const float* base, int count, float (&M)[kG], float (&L)[kG],
                                               float4& A0, float4& A1) {
@@ -251,8 +253,30 @@ __device__ __forceinline__ void merge_records(const float* base, int count, floa
     auto ld4 = [](const float* p) {
         return kGlobal ? __ldcg(reinterpret_cast<const float4*>(p)) : *reinterpret_cast<const float4*>(p);
     };
-    float M0 = -INFINITY, M1 = -INFINITY;
-    for (int s = lane; s < count; s += kWarp) {
+    const float* pa = base + 4 + 4 * lane;
+    float m0 = -INFINITY, l0 = 0.0f, m1 = -INFINITY, l1 = 0.0f;  // record s0 + lane of the current chunk
+    auto load_ml = [&](int s0) {
+        if (s0 + lane < count) {
+            const float* ps = base + (size_t)(s0 + lane) * kPartStride;
+            m0 = ld(ps);
+            l0 = ld(ps + 1);
+            m1 = ld(ps + kPartHead);
+            l1 = ld(ps + kPartHead + 1);
+        }
+    };
+    float4 u0[kBatch], u1[kBatch];
+    auto load_batch = [&](int s0, int j0, int cnt) {
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int jj = s0 + max(0, min(j0 + j, cnt - 1));
+            u0[j] = ld4(pa + (size_t)jj * kPartStride);
+            u1[j] = ld4(pa + (size_t)jj * kPartStride + kPartHead);
+        }
+    };
+    load_ml(0);
+    load_batch(0, 0, min(kWarp, count));
+    float M0 = fmaxf(-INFINITY, m0), M1 = fmaxf(-INFINITY, m1);
+    for (int s = lane + kWarp; s < count; s += kWarp) {
         M0 = fmaxf(M0, ld(base + (size_t)s * kPartStride));
         M1 = fmaxf(M1, ld(base + (size_t)s * kPartStride + kPartHead));
     }
@@ -262,26 +286,17 @@ __device__ __forceinline__ void merge_records(const float* base, int count, floa
     A0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     A1 = A0;
     for (int s0 = 0; s0 < count; s0 += kWarp) {
+        if (s0 > 0) load_ml(s0);
         float c0 = 0.0f, c1 = 0.0f;
         if (s0 + lane < count) {
-            const float* ps = base + (size_t)(s0 + lane) * kPartStride;
-            const float m0 = ld(ps), l0 = ld(ps + 1);
-            const float m1 = ld(ps + kPartHead), l1 = ld(ps + kPartHead + 1);
             c0 = m0 == -INFINITY ? 0.0f : expf(m0 - M0);
             c1 = m1 == -INFINITY ? 0.0f : expf(m1 - M1);
             L0 += l0 * c0;
             L1 += l1 * c1;
         }
         const int cnt = min(kWarp, count - s0);
-        const float* pa = base + (size_t)s0 * kPartStride + 4 + 4 * lane;
         for (int j0 = 0; j0 < cnt; j0 += kBatch) {
-            float4 u0[kBatch], u1[kBatch];  // kBatch records in flight before any is used
-#pragma unroll
-            for (int j = 0; j < kBatch; ++j) {
-                const int jj = min(j0 + j, cnt - 1);
-                u0[j] = ld4(pa + (size_t)jj * kPartStride);
-                u1[j] = ld4(pa + (size_t)jj * kPartStride + kPartHead);
-            }
+            if (s0 > 0 || j0 > 0) load_batch(s0, j0, cnt);  // kBatch records in flight before any is used
 #pragma unroll
             for (int j = 0; j < kBatch; ++j) {
                 const bool live = j0 + j < cnt;
