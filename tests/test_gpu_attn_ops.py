@@ -27,6 +27,7 @@ torch = pytest.importorskip("torch")
 
 ARCH1 = zc.Arch(layers=1)
 MAX_SEQ_LEN = 4232
+LONG_SEQ_LEN = 11008
 THETA = 1_000_000.0
 
 
@@ -34,18 +35,31 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.fixture(scope="module")
-def one_layer():
+def _one_layer(max_batch, max_seq_len):
     gpu = zc.Gpu(0)
-    m = zc.Model(gpu, ARCH1, zc.W_Q8, max_batch=64, max_seqs=64, max_seq_len=MAX_SEQ_LEN)
+    m = zc.Model(gpu, ARCH1, zc.W_Q8, max_batch=max_batch, max_seqs=max_batch, max_seq_len=max_seq_len)
     m.fill_synthetic(3, 0.02, 0.0)
     qn = (1.0 + O.synth_normal(128, 5, 1, 0.1)).astype(np.float32)
     kn = (1.0 + O.synth_normal(128, 5, 2, 0.1)).astype(np.float32)
     m.upload_f32("model.layers.0.self_attn.q_norm.weight", qn)
     m.upload_f32("model.layers.0.self_attn.k_norm.weight", kn)
     oracle = O.Model(O.Arch(layers=1), O.W_Q8, kv_bf16=True, seed=3, w_std=0.02, norm_std=0.0, threads=4)
-    yield m, qn, kn, oracle
-    oracle.close()
+    return gpu, (m, qn, kn, oracle)
+
+
+@pytest.fixture(scope="module")
+def one_layer():
+    gpu, t = _one_layer(64, MAX_SEQ_LEN)
+    yield t
+    t[3].close()
+    gpu.close()
+
+
+@pytest.fixture(scope="module")
+def one_layer_long():
+    gpu, t = _one_layer(1, LONG_SEQ_LEN)
+    yield t
+    t[3].close()
     gpu.close()
 
 
@@ -102,6 +116,14 @@ def test_attn_decode_matches_attention_into(one_layer, batch):
 @pytest.mark.parametrize("kv_len", [1, 2, 16, 17, 128, 1024, 1025, 2049, 3072, MAX_SEQ_LEN])
 def test_attn_decode_one_sequence(one_layer, kv_len):
     _check_attn_decode(one_layer, [kv_len], 100 + kv_len)
+
+
+# Past 640 blocks (10240 positions) one sequence is spread over every SM
+# instead (the batched kernel's split with one-row settings); both sides of
+# the switch and a longer context.
+@pytest.mark.parametrize("kv_len", [10240, 10241, LONG_SEQ_LEN])
+def test_attn_decode_one_long_sequence(one_layer_long, kv_len):
+    _check_attn_decode(one_layer_long, [kv_len], 200 + kv_len)
 
 
 @pytest.mark.parametrize("pos0", [0, 4219])

@@ -809,7 +809,7 @@ void prepare_attn_kernels() {
 }
 
 void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st) {
-    if (a.B == 1) {
+    if (a.B == 1 && a.head_clusters) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(a.n_kv * kHeadCtas);
         cfg.blockDim = dim3(kDecThreads);

@@ -174,7 +174,8 @@ struct ZynferCuCtx {
     uint64_t* ptrace = nullptr;          // its phase timestamps when timing is on
     std::vector<uint64_t> ptrace_host;
 
-    std::map<int, GraphEntry> graphs;
+    std::map<int, GraphEntry> graphs;  // by 2 B + head_clusters
+    bool head_clusters = false;        // the next decode steps' one-sequence attention choice
     int step_launches = 0;  // kernels enqueued by the last decode step
     uint64_t h2d_bytes = 0, d2h_bytes = 0;  // host<->device bytes of decode/generate calls
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -579,7 +580,7 @@ void enqueue_decode(ZynferCuCtx* c, int B, bool want_logits) {
         aa.max_blocks = c->max_blocks; aa.n_pool_blocks = c->n_blocks;
         aa.seq_of = c->dseq; aa.positions = c->dpos; aa.B = B; aa.n_q = m.n_q; aa.n_kv = m.n_kv;
         aa.d = m.head_dim; aa.max_segs = decode_max_segs(c->max_blocks); aa.partial = c->dpart;
-        aa.counters = c->dcnt; aa.out = c->dattn; aa.err = c->derr;
+        aa.counters = c->dcnt; aa.out = c->dattn; aa.err = c->derr; aa.head_clusters = c->head_clusters;
         tbegin(c, ZYNFER_CU_K_ATTN, &te);
         launch_attn_decode(aa, c->stream);
         tend(c, te);
@@ -679,7 +680,8 @@ void set_io_views(ZynferCuCtx* c, int B) {
 }
 
 int get_graph(ZynferCuCtx* c, int B, GraphEntry* out) {
-    auto it = c->graphs.find(B);
+    const int key = 2 * B + (c->head_clusters ? 1 : 0);
+    auto it = c->graphs.find(key);
     if (it != c->graphs.end()) {
         *out = it->second;
         return ZYNFER_CU_OK;
@@ -699,7 +701,7 @@ int get_graph(ZynferCuCtx* c, int B, GraphEntry* out) {
     GraphEntry ent;
     ent.exec = ge;
     ent.paths = c->step_paths;
-    c->graphs[B] = ent;
+    c->graphs[key] = ent;
     *out = ent;
     return ZYNFER_CU_OK;
 }
@@ -1340,6 +1342,7 @@ int zynfer_cu_attn_decode(ZynferCuCtx* c, uint32_t layer, const uint32_t* seqs, 
     aa.seq_of = c->dseq; aa.positions = c->dpos; aa.B = (int)batch; aa.n_q = m.n_q; aa.n_kv = m.n_kv;
     aa.d = m.head_dim; aa.max_segs = decode_max_segs(c->max_blocks); aa.partial = c->dpart;
     aa.counters = c->dcnt; aa.out = out; aa.err = c->derr;
+    aa.head_clusters = attn_head_clusters((int)batch, (long long)c->seq_len[seqs[0]] + 1);
     launch_attn_decode(aa, c->stream);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "attention launch");
@@ -1448,6 +1451,7 @@ int zynfer_cu_decode_step(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* 
     set_io_views(c, (int)batch);
     if ((rc = stage_batch(c, seqs, tokens, batch))) return rc;
     ZC_CHECK(c, cudaMemsetAsync(c->dstep, 0, 4, c->stream), "step counter");
+    c->head_clusters = attn_head_clusters((int)batch, (long long)c->seq_len[seqs[0]] + 1);
     const bool persistent = use_persistent(c, (int)batch);
     const bool eager = logits != nullptr || c->timing || persistent;
     unsigned paths = 0;
@@ -1501,6 +1505,8 @@ int zynfer_cu_generate(ZynferCuCtx* c, const uint32_t* seqs, const uint32_t* fir
     set_io_views(c, (int)batch);
     if ((rc = stage_batch(c, seqs, first, batch))) return rc;
     ZC_CHECK(c, cudaMemsetAsync(c->dstep, 0, 4, c->stream), "step counter");
+    // one sequence: the whole call keeps the choice of its longest step
+    c->head_clusters = attn_head_clusters((int)batch, (long long)c->seq_len[seqs[0]] + steps);
     const bool persistent = use_persistent(c, (int)batch);
     GraphEntry g;
     if (!c->timing && !persistent && (rc = get_graph(c, (int)batch, &g))) return rc;
@@ -1565,6 +1571,7 @@ int zynfer_cu_block_forward(ZynferCuCtx* c, uint32_t layer, uint32_t seq, const 
             aa.B = 1; aa.n_q = m.n_q; aa.n_kv = m.n_kv; aa.d = m.head_dim;
             aa.max_segs = decode_max_segs(c->max_blocks); aa.partial = c->dpart;
             aa.counters = c->dcnt; aa.out = c->dattn; aa.err = c->derr;
+            aa.head_clusters = attn_head_clusters(1, (long long)pos0 + i + 1);
             launch_attn_decode(aa, c->stream);
             linear(c, ZYNFER_CU_K_LINEAR, Ld.wo, Ld.so, &Ld.tm_o, H, c->qd, c->dattn, 1, c->dx1, kEpiResid, c->dx, nullptr, nullptr);
             linear(c, ZYNFER_CU_K_LINEAR, Ld.wgu, Ld.sgu, &Ld.tm_gu, 2 * m.inter, H, c->dx1, 1, c->dh, kEpiSwiGLU, nullptr, Ld.post_ln, nullptr);
