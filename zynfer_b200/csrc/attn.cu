@@ -63,22 +63,24 @@ constexpr size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
 constexpr size_t kWarpScratch = kG * kD * 4 + 2 * kD * 2;    // per warp: q (2 x 128 f32), new K/V row
 constexpr int kHeadCtas = 8;                                // CTAs of a kv head's cluster (one-sequence steps)
 // Shared-memory layout for RING slots per warp. Three slots keep a block
-// loading while a warp computes on a pair (the rate at many rows); one row's
-// step gives every warp at most one pair (2 blocks), so two slots hold its
-// whole share, and the smaller footprint (~163 KB instead of ~227 KB) lets the
-// neighbouring one-row GEMV kernels' CTAs be resident on the same SM.
-template <int RING>
+// loading while a warp computes on a pair (the rate at many rows); a one-row
+// step over the whole GPU gives every warp at most one pair (2 blocks), so
+// two slots hold its whole share, and the smaller footprint (~163 KB instead
+// of ~227 KB) lets the neighbouring one-row GEMV kernels' CTAs be resident on
+// the same SM. HEAD (one sequence, one cluster per kv head): the block-count
+// prefix has one row, a warp holds one piece of one (row, kv head) and so one
+// record, and the first CTA of a cluster receives every CTA's record in cl.
+template <int RING, bool HEAD = false>
 struct DecLayout {
+    static constexpr int kPref = HEAD ? 2 : kMaxBatch + 1;  // block-count prefix entries
+    static constexpr int kRecK = HEAD ? 1 : 2;              // records per warp
     static constexpr size_t ring_bytes = (size_t)kDecWarps * RING * kSlotBytes;
     static constexpr size_t scratch_off = align16(ring_bytes + kDecWarps * RING * sizeof(uint64_t) +
-                                                  (kMaxBatch + 1) * sizeof(int) + kDecWarps * kIdRing * sizeof(uint32_t));
-    static constexpr size_t rec_off = scratch_off + kDecWarps * kWarpScratch;  // [2][kDecWarps] share records
-    static constexpr size_t gid_off = rec_off + (size_t)2 * kDecWarps * attn::kPartStride * 4;  // [2][kDecWarps] int
-    static constexpr size_t smem = gid_off + 2 * kDecWarps * sizeof(int);
-    // one-sequence head clusters: the first CTA of a cluster receives every
-    // CTA's record here (distributed shared memory)
-    static constexpr size_t cl_off = align16(smem);
-    static constexpr size_t smem_head = cl_off + (size_t)kHeadCtas * attn::kPartStride * 4;
+                                                  kPref * sizeof(int) + kDecWarps * kIdRing * sizeof(uint32_t));
+    static constexpr size_t rec_off = scratch_off + kDecWarps * kWarpScratch;  // [kRecK][kDecWarps] share records
+    static constexpr size_t gid_off = rec_off + (size_t)kRecK * kDecWarps * attn::kPartStride * 4;  // [kRecK][kDecWarps]
+    static constexpr size_t cl_off = align16(gid_off + kRecK * kDecWarps * sizeof(int));
+    static constexpr size_t smem = cl_off + (HEAD ? (size_t)kHeadCtas * attn::kPartStride * 4 : 0);
     static_assert(smem <= 232448, "decode attention shared memory");
     static_assert(scratch_off % 16 == 0 && kWarpScratch % 16 == 0 && rec_off % 16 == 0 &&
                       (attn::kPartStride * 4) % 16 == 0,
@@ -119,20 +121,21 @@ __device__ __forceinline__ void cluster_wait_acquire() {
 // counter, no second pass through L2.
 template <int kRing, bool kHead = false>
 __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
-    using Lay = DecLayout<kRing>;
+    using Lay = DecLayout<kRing, kHead>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     unsigned char* ring = smem_raw + (size_t)warp * kRing * kSlotBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + Lay::ring_bytes) + warp * kRing;
     int* pref = reinterpret_cast<int*>(smem_raw + Lay::ring_bytes + kDecWarps * kRing * sizeof(uint64_t));
-    uint32_t* kidx = reinterpret_cast<uint32_t*>(pref + kMaxBatch + 1) + warp * kIdRing;
+    uint32_t* kidx = reinterpret_cast<uint32_t*>(pref + Lay::kPref) + warp * kIdRing;
     float* qb = reinterpret_cast<float*>(smem_raw + Lay::scratch_off + warp * kWarpScratch);
     float* recs = reinterpret_cast<float*>(smem_raw + Lay::rec_off);  // record (warp, k) at (k * kDecWarps + warp)
+    auto rec_k = [](int k) { return Lay::kRecK == 1 ? 0 : k; };        // one record per warp in a head cluster
     int (*rec_gid)[kDecWarps] = reinterpret_cast<int (*)[kDecWarps]>(smem_raw + Lay::gid_off);  // (row, kv head) of each record
     uint16_t* kvnew = reinterpret_cast<uint16_t*>(qb + kG * kD);
     constexpr unsigned kAll = 0xFFFFFFFFu;
 
-    const int B = a.B;
+    const int B = kHead ? 1 : a.B;
     const int max_len = a.max_blocks * kKvBlock;
     // Row-major prefix of KV block counts. Positions and block tables are
     // written before the step starts, never by the kernels this launch may
@@ -187,7 +190,7 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
     }
     const int lo = c_lo + warp * per;
     const int n = max(0, min(c_hi, lo + per) - lo);
-    if (lane < 2) rec_gid[lane][warp] = -1;
+    if (lane < Lay::kRecK) rec_gid[lane][warp] = -1;
 
     auto locate = [&](int f, BlockCursor& c) {
         int l = 0, h = B - 1;
@@ -434,7 +437,7 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
             if (f0 >= lo && f0 + cc.nblk <= lo + n) {
                 attn::share_store_out(acc, Lh, a.out, cc.b, cc.head, a.n_q);
             } else {
-                const int k = f0 < lo ? 0 : 1;
+                const int k = rec_k(f0 < lo ? 0 : 1);
                 attn::share_store_record(acc, Lh, Mh, recs + (size_t)(k * kDecWarps + warp) * attn::kPartStride);
                 if (lane == 0) rec_gid[k][warp] = cc.b * a.n_kv + cc.head;
             }
@@ -464,7 +467,7 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
                     // records of warps wa..wb, in order; shared memory, so read them directly
                     float M[attn::kG] = {-INFINITY, -INFINITY};
                     for (int wi = wa; wi <= wb; ++wi) {
-                        const int k = (wi == wa && g0 >= c_lo + wi * per) ? 1 : 0;
+                        const int k = rec_k((wi == wa && g0 >= c_lo + wi * per) ? 1 : 0);
                         const float* r = recs + (size_t)(k * kDecWarps + wi) * attn::kPartStride;
                         M[0] = fmaxf(M[0], r[0]);
                         M[1] = fmaxf(M[1], r[attn::kPartHead]);
@@ -472,7 +475,7 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
                     float L[attn::kG] = {0.0f, 0.0f};
                     float4 A0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), A1 = A0;
                     for (int wi = wa; wi <= wb; ++wi) {
-                        const int k = (wi == wa && g0 >= c_lo + wi * per) ? 1 : 0;
+                        const int k = rec_k((wi == wa && g0 >= c_lo + wi * per) ? 1 : 0);
                         const float* r = recs + (size_t)(k * kDecWarps + wi) * attn::kPartStride;
                         if (rec_gid[k][wi] != gb * a.n_kv + gh) continue;  // a warp that stopped early
                         const float c0 = r[0] == -INFINITY ? 0.0f : expf(r[0] - M[0]);
@@ -538,12 +541,15 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
 }
 
 // The decode kernels: three ring slots for many rows (the register file is
-// the kernel's own); two slots and at most 192 registers per thread for a
-// one-row step, so a one-row GEMV CTA (256 threads, <= 64 registers, <= 48 KB
-// of shared memory) fits on the same SM beside it.
+// the kernel's own); for a one-row step over the whole GPU two slots and at
+// most 192 registers per thread, so a one-row GEMV CTA (256 threads, <= 64
+// registers, <= 48 KB of shared memory) fits on the same SM beside it; a
+// one-row step in head clusters (64 SMs, the rest left to the next GEMV) has
+// three slots, so a warp's blocks are all requested before the wait while
+// shares are at most 3 blocks (contexts up to 3072).
 __global__ void __launch_bounds__(kDecThreads, 1) attn_decode_kernel(AttnDecodeArgs a) { attn_decode_body<3>(a); }
 __global__ void __maxnreg__(192) attn_decode_row_kernel(AttnDecodeArgs a) { attn_decode_body<2>(a); }
-__global__ void __maxnreg__(192) attn_decode_head_kernel(AttnDecodeArgs a) { attn_decode_body<2, true>(a); }
+__global__ void __launch_bounds__(kDecThreads, 1) attn_decode_head_kernel(AttnDecodeArgs a) { attn_decode_body<3, true>(a); }
 
 // ------------------------------------------------------------ prefill
 //
@@ -804,7 +810,7 @@ __global__ void __launch_bounds__(PTHREADS, 1) attn_prefill_kernel(AttnPrefillAr
 void prepare_attn_kernels() {
     configure_kernel((const void*)attn_decode_kernel, DecLayout<3>::smem);
     configure_kernel((const void*)attn_decode_row_kernel, DecLayout<2>::smem);
-    configure_kernel((const void*)attn_decode_head_kernel, DecLayout<2>::smem_head);
+    configure_kernel((const void*)attn_decode_head_kernel, DecLayout<3, true>::smem);
     configure_kernel((const void*)attn_prefill_kernel, kPrefillSmem);
 }
 
@@ -813,7 +819,7 @@ void launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(a.n_kv * kHeadCtas);
         cfg.blockDim = dim3(kDecThreads);
-        cfg.dynamicSmemBytes = DecLayout<2>::smem_head;
+        cfg.dynamicSmemBytes = DecLayout<3, true>::smem;
         cfg.stream = st;
         cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
