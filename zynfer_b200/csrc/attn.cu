@@ -466,26 +466,63 @@ __device__ __forceinline__ void attn_decode_body(const AttnDecodeArgs& a) {
                 if (!whole) {
                     // records of warps wa..wb, in order; shared memory, so read them directly
                     float M[attn::kG] = {-INFINITY, -INFINITY};
-                    for (int wi = wa; wi <= wb; ++wi) {
-                        const int k = rec_k((wi == wa && g0 >= c_lo + wi * per) ? 1 : 0);
-                        const float* r = recs + (size_t)(k * kDecWarps + wi) * attn::kPartStride;
-                        M[0] = fmaxf(M[0], r[0]);
-                        M[1] = fmaxf(M[1], r[attn::kPartHead]);
-                    }
                     float L[attn::kG] = {0.0f, 0.0f};
                     float4 A0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), A1 = A0;
-                    for (int wi = wa; wi <= wb; ++wi) {
-                        const int k = rec_k((wi == wa && g0 >= c_lo + wi * per) ? 1 : 0);
-                        const float* r = recs + (size_t)(k * kDecWarps + wi) * attn::kPartStride;
-                        if (rec_gid[k][wi] != gb * a.n_kv + gh) continue;  // a warp that stopped early
-                        const float c0 = r[0] == -INFINITY ? 0.0f : expf(r[0] - M[0]);
-                        const float c1 = r[attn::kPartHead] == -INFINITY ? 0.0f : expf(r[attn::kPartHead] - M[1]);
-                        L[0] += r[1] * c0;
-                        L[1] += r[attn::kPartHead + 1] * c1;
-                        const float4 u0 = *reinterpret_cast<const float4*>(r + 4 + 4 * lane);
-                        const float4 u1 = *reinterpret_cast<const float4*>(r + attn::kPartHead + 4 + 4 * lane);
-                        A0.x += u0.x * c0; A0.y += u0.y * c0; A0.z += u0.z * c0; A0.w += u0.w * c0;
-                        A1.x += u1.x * c1; A1.y += u1.y * c1; A1.z += u1.z * c1; A1.w += u1.w * c1;
+                    if constexpr (kHead) {
+                        // one record per warp, in slots wa..wb: every shared-memory
+                        // load is issued before any is used (same sums, same order)
+                        float rm0[kDecWarps], rm1[kDecWarps], rl0[kDecWarps], rl1[kDecWarps];
+                        float4 ru0[kDecWarps], ru1[kDecWarps];
+                        bool live[kDecWarps];
+#pragma unroll
+                        for (int i = 0; i < kDecWarps; ++i) {
+                            const int wi = min(wa + i, wb);
+                            const float* r = recs + (size_t)wi * attn::kPartStride;
+                            live[i] = wa + i <= wb;
+                            rm0[i] = live[i] ? r[0] : -INFINITY;
+                            rm1[i] = live[i] ? r[attn::kPartHead] : -INFINITY;
+                            rl0[i] = r[1];
+                            rl1[i] = r[attn::kPartHead + 1];
+                            ru0[i] = *reinterpret_cast<const float4*>(r + 4 + 4 * lane);
+                            ru1[i] = *reinterpret_cast<const float4*>(r + attn::kPartHead + 4 + 4 * lane);
+                            live[i] = live[i] && rec_gid[0][wi] == gb * a.n_kv + gh;  // a warp that stopped early
+                        }
+#pragma unroll
+                        for (int i = 0; i < kDecWarps; ++i) {
+                            M[0] = fmaxf(M[0], rm0[i]);
+                            M[1] = fmaxf(M[1], rm1[i]);
+                        }
+#pragma unroll
+                        for (int i = 0; i < kDecWarps; ++i) {
+                            if (!live[i]) continue;
+                            const float c0 = rm0[i] == -INFINITY ? 0.0f : expf(rm0[i] - M[0]);
+                            const float c1 = rm1[i] == -INFINITY ? 0.0f : expf(rm1[i] - M[1]);
+                            L[0] += rl0[i] * c0;
+                            L[1] += rl1[i] * c1;
+                            const float4 u0 = ru0[i], u1 = ru1[i];
+                            A0.x += u0.x * c0; A0.y += u0.y * c0; A0.z += u0.z * c0; A0.w += u0.w * c0;
+                            A1.x += u1.x * c1; A1.y += u1.y * c1; A1.z += u1.z * c1; A1.w += u1.w * c1;
+                        }
+                    } else {
+                        for (int wi = wa; wi <= wb; ++wi) {
+                            const int k = (wi == wa && g0 >= c_lo + wi * per) ? 1 : 0;
+                            const float* r = recs + (size_t)(k * kDecWarps + wi) * attn::kPartStride;
+                            M[0] = fmaxf(M[0], r[0]);
+                            M[1] = fmaxf(M[1], r[attn::kPartHead]);
+                        }
+                        for (int wi = wa; wi <= wb; ++wi) {
+                            const int k = (wi == wa && g0 >= c_lo + wi * per) ? 1 : 0;
+                            const float* r = recs + (size_t)(k * kDecWarps + wi) * attn::kPartStride;
+                            if (rec_gid[k][wi] != gb * a.n_kv + gh) continue;  // a warp that stopped early
+                            const float c0 = r[0] == -INFINITY ? 0.0f : expf(r[0] - M[0]);
+                            const float c1 = r[attn::kPartHead] == -INFINITY ? 0.0f : expf(r[attn::kPartHead] - M[1]);
+                            L[0] += r[1] * c0;
+                            L[1] += r[attn::kPartHead + 1] * c1;
+                            const float4 u0 = *reinterpret_cast<const float4*>(r + 4 + 4 * lane);
+                            const float4 u1 = *reinterpret_cast<const float4*>(r + attn::kPartHead + 4 + 4 * lane);
+                            A0.x += u0.x * c0; A0.y += u0.y * c0; A0.z += u0.z * c0; A0.w += u0.w * c0;
+                            A1.x += u1.x * c1; A1.y += u1.y * c1; A1.z += u1.z * c1; A1.w += u1.w * c1;
+                        }
                     }
                     if (g0 >= c_lo && g1 <= c_hi) {
                         attn::merged_store_out(L, A0, A1, a.out, gb, gh, a.n_q);
