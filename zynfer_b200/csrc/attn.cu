@@ -41,6 +41,10 @@ namespace {
 // (max, sum, acc[d]) per query head; the last warp to finish one (atomic
 // counter) merges them in segment order:
 //   m = max m_s,  l = sum l_s e^(m_s - m),  o = sum acc_s e^(m_s - m) / l.
+// A one-sequence step of up to kHeadClusterMaxBlocks blocks runs instead as
+// one 8-CTA cluster per kv head: the same per-warp loop over that head's
+// blocks, the CTAs' partials merged in the cluster's first CTA after one
+// cluster barrier (distributed shared memory, no counter).
 //
 // KV blocks are stored with their 16-byte chunks XOR-swizzled by token
 // (kv_swizzle), so the ldmatrix reads of K rows and the transposing reads of
